@@ -1,0 +1,202 @@
+// Device-side helpers shared by the sm_100a kernels: 16-bit element types,
+// mbarriers, TMA bulk-tensor loads, programmatic dependent launch, cluster
+// distributed shared memory and the bounded waits every kernel uses.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cq {
+
+// Element type codes shared with the C ABI (cq_dtype).
+enum DType : int { kF16 = 0, kBF16 = 1, kF32 = 2 };
+
+// Fused epilogue activations (applied to the widened T result, re-rounded to T).
+enum Act : int { kActNone = 0, kActSilu = 1, kActRelu = 2 };
+
+constexpr int kStatusWaitTimeout = 1;
+
+// Upper bound for any device-side wait (nanoseconds of %globaltimer).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+template <int DT>
+__device__ __forceinline__ float ld_t(const void* p, size_t i) {
+  if constexpr (DT == kF32) {
+    return reinterpret_cast<const float*>(p)[i];
+  } else {
+    const uint16_t v = __ldg(reinterpret_cast<const unsigned short*>(p) + i);
+    if constexpr (DT == kBF16) return __uint_as_float(static_cast<uint32_t>(v) << 16);
+    else return __half2float(__ushort_as_half(v));
+  }
+}
+
+// Round an fp32 value to T (round to nearest even) and widen it back.
+template <int DT>
+__device__ __forceinline__ float round_t(float v) {
+  if constexpr (DT == kF32) return v;
+  else if constexpr (DT == kBF16) return __bfloat162float(__float2bfloat16_rn(v));
+  else return __half2float(__float2half_rn(v));
+}
+
+template <int DT>
+__device__ __forceinline__ void st_t(void* p, size_t i, float v) {
+  if constexpr (DT == kF32) {
+    reinterpret_cast<float*>(p)[i] = v;
+  } else if constexpr (DT == kBF16) {
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  }
+}
+
+// Epilogue shared by every linear kernel: the quantized_matmul result is
+// rounded to T, the output bias is added in T, the activation is applied to
+// the widened value and rounded to T again.
+template <int DT>
+__device__ __forceinline__ float linear_epilogue(float acc, const void* bias, int n, int act) {
+  float o = round_t<DT>(acc);
+  if (bias != nullptr) o = round_t<DT>(o + ld_t<DT>(bias, n));
+  if (act == kActSilu) {
+    o = round_t<DT>(o / (1.0f + expf(-o)));
+  } else if (act == kActRelu) {
+    o = o > 0.0f ? o : 0.0f;
+  }
+  return o;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ------------------------------------------------------------------ mbarrier
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the given phase parity; gives up after kWaitLimitNs, records the
+// timeout in the per-device status word (read and cleared by the host through
+// cq_device_status) and returns false.
+static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (status != nullptr) atomicOr(status, kStatusWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ TMA
+
+// 2-D tiled bulk-tensor load global -> shared, completion on an mbarrier.
+// No multicast: the destination is this CTA's own shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y,
+                                            uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::"
+      "cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// L2 policy for data read exactly once (the packed weights).
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ------------------------------------------------------------------ PDL
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------------------------ clusters
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// ------------------------------------------------------------------ loads
+
+__device__ __forceinline__ uint4 ld_global_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// ------------------------------------------------------------------ MMA
+
+// D = A(16x16, row) * B(16x8, col) + C, f16 inputs, f32 accumulation.
+__device__ __forceinline__ void mma_16816_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                              uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+}  // namespace cq

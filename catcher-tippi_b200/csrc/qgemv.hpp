@@ -1,0 +1,35 @@
+// Host-side interface of the K1 dequant-GEMV (qgemv.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace cq {
+
+struct GemvArgs {
+  const void* x;       // T [M, ldx], 16-byte aligned rows
+  const void* scales;  // T [N, K/g]
+  const void* biases;  // T [N, K/g]
+  const void* bias;    // T [N] or nullptr
+  void* y;             // T [M, ldy]
+  int* status;         // device status word (watchdog)
+  int M, N, K, ldx, ldy;
+  int sb_per_cta;      // 64-wide K sub-blocks per CTA
+  int act;             // cq::Act
+};
+
+// Work decomposition: RB = 16*rt weight rows per CTA, K split across a
+// cluster of `ksplit` CTAs, each owning `sb_per_cta` sub-blocks of 64.
+struct GemvPlan {
+  int rt;
+  int ksplit;
+  int sb_per_cta;
+};
+
+GemvPlan plan_gemv(int N, int K, int num_sms);
+size_t gemv_smem_bytes(const GemvPlan& plan, int group);
+cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
+                        const GemvArgs& args, cudaStream_t stream, bool pdl);
+
+}  // namespace cq

@@ -1,0 +1,435 @@
+// C++ host layer: device contexts, weight binding, shape validation and
+// kernel dispatch for the quantized linear.  See qlinear.hpp.
+#include "qlinear.hpp"
+
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <sstream>
+
+#include "common.cuh"
+#include "qops.hpp"
+
+namespace nemotron_cuda {
+
+namespace {
+
+std::string fmt_shape_error(const char* prefix, const std::string& msg) {
+  return std::string(prefix) + msg;
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("CQ_PDL");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return on;
+}
+
+void validate_group(int group) {
+  if (group != 32 && group != 64 && group != 128) {
+    std::ostringstream os;
+    os << "group size " << group << " is not supported; supported group sizes are 32, 64 and 128";
+    throw_invalid(os.str());
+  }
+}
+
+void validate_dtype(cq_dtype dtype) {
+  if (dtype != CQ_F16 && dtype != CQ_BF16 && dtype != CQ_F32)
+    throw_invalid("unknown dtype " + std::to_string(dtype));
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+[[noreturn]] void throw_invalid(const std::string& msg) { throw Error(CQ_INVALID_ARGUMENT, msg); }
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // clear a sticky launch error so later calls report their own
+    throw Error(CQ_RUNTIME_ERROR, std::string(what) + ": " + cudaGetErrorString(e));
+  }
+}
+
+size_t dtype_size(cq_dtype dtype) { return dtype == CQ_F32 ? 4 : 2; }
+
+DeviceGuard::DeviceGuard(int device) {
+  check_cuda(cudaGetDevice(&prev_), "cudaGetDevice");
+  if (prev_ != device) check_cuda(cudaSetDevice(device), "cudaSetDevice");
+}
+
+DeviceGuard::~DeviceGuard() {
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_ && prev_ >= 0) cudaSetDevice(prev_);
+}
+
+DeviceContext& device_context(int device) {
+  static std::mutex mu;
+  static std::vector<std::unique_ptr<DeviceContext>> contexts;
+  std::lock_guard<std::mutex> lock(mu);
+  int count = 0;
+  check_cuda(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+  if (device < 0 || device >= count)
+    throw_invalid("device " + std::to_string(device) + " does not exist (" +
+                  std::to_string(count) + " visible)");
+  if (contexts.size() < static_cast<size_t>(count)) contexts.resize(count);
+  if (!contexts[device]) {
+    DeviceGuard guard(device);
+    auto ctx = std::make_unique<DeviceContext>();
+    ctx->device = device;
+    int major = 0, minor = 0;
+    check_cuda(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device), "attr");
+    check_cuda(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device), "attr");
+    if (major != 10)
+      throw Error(CQ_RUNTIME_ERROR, "device " + std::to_string(device) + " is sm_" +
+                                        std::to_string(major) + std::to_string(minor) +
+                                        "; this library is built for sm_100a only");
+    check_cuda(cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, device),
+               "attr");
+    check_cuda(cudaMalloc(&ctx->status, sizeof(int)), "cudaMalloc(status)");
+    check_cuda(cudaMemset(ctx->status, 0, sizeof(int)), "cudaMemset(status)");
+    contexts[device] = std::move(ctx);
+  }
+  return *contexts[device];
+}
+
+CUtensorMap make_weight_map(const void* q, int N, int K, int box_rows) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult qres{};
+    check_cuda(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &qres),
+               "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+    if (fn == nullptr || qres != cudaDriverEntryPointSuccess)
+      throw Error(CQ_RUNTIME_ERROR, "cuTensorMapEncodeTiled is unavailable");
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  CUtensorMap map{};
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};  // bytes between rows
+  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides,
+                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    throw Error(CQ_RUNTIME_ERROR, "cuTensorMapEncodeTiled failed with " + std::to_string(r));
+  return map;
+}
+
+// ------------------------------------------------------------------ layer
+
+QuantizedLinear::QuantizedLinear(int N, int K, int group, cq_dtype dtype, int device)
+    : N_(N), K_(K), group_(group), dtype_(dtype), device_(device) {}
+
+QuantizedLinear::~QuantizedLinear() {
+  int prev = -1;
+  cudaGetDevice(&prev);
+  cudaSetDevice(device_);
+  cudaFree(q_);
+  cudaFree(scales_);
+  cudaFree(biases_);
+  cudaFree(bias_);
+  cudaFree(host_scratch_);
+  if (prev >= 0) cudaSetDevice(prev);
+}
+
+void QuantizedLinear::allocate(bool with_bias) {
+  const size_t groups = static_cast<size_t>(N_) * (K_ / group_);
+  check_cuda(cudaMalloc(&q_, static_cast<size_t>(N_) * K_), "cudaMalloc(qweight)");
+  check_cuda(cudaMalloc(&scales_, groups * dtype_size(dtype_)), "cudaMalloc(scales)");
+  check_cuda(cudaMalloc(&biases_, groups * dtype_size(dtype_)), "cudaMalloc(biases)");
+  if (with_bias) check_cuda(cudaMalloc(&bias_, N_ * dtype_size(dtype_)), "cudaMalloc(bias)");
+}
+
+void QuantizedLinear::finalize() {
+  if (dtype_ == CQ_F32) return;  // the f32 path uses the CUDA-core kernel
+  DeviceContext& ctx = device_context(device_);
+  plan_ = cq::plan_gemv(N_, K_, ctx.num_sms);
+  wmap_ = make_weight_map(q_, N_, K_, 16 * plan_.rt);
+}
+
+std::unique_ptr<QuantizedLinear> QuantizedLinear::from_packed(const uint32_t* qweight,
+                                                              const void* scales,
+                                                              const void* biases, const void* bias,
+                                                              int output_dims, int input_dims,
+                                                              int group, cq_dtype dtype,
+                                                              int device) {
+  if (qweight == nullptr || scales == nullptr || biases == nullptr)
+    throw_invalid("qweight, scales and biases must not be null");
+  validate_dtype(dtype);
+  if (output_dims <= 0 || input_dims <= 0)
+    throw_invalid("invalid model shape: linear dimensions must be positive, got " +
+                  std::to_string(output_dims) + "x" + std::to_string(input_dims));
+  validate_group(group);
+  if (input_dims % group != 0)
+    throw_invalid("invalid model shape: linear input dimension " + std::to_string(input_dims) +
+                  " is incompatible with group size " + std::to_string(group));
+  device_context(device);
+  DeviceGuard guard(device);
+  std::unique_ptr<QuantizedLinear> L(
+      new QuantizedLinear(output_dims, input_dims, group, dtype, device));
+  L->allocate(bias != nullptr);
+  const size_t groups = static_cast<size_t>(output_dims) * (input_dims / group);
+  // cudaMemcpyDefault: the source arrays may live in host or device memory.
+  check_cuda(cudaMemcpy(L->q_, qweight, static_cast<size_t>(output_dims) * input_dims,
+                        cudaMemcpyDefault),
+             "copy qweight");
+  check_cuda(cudaMemcpy(L->scales_, scales, groups * dtype_size(dtype), cudaMemcpyDefault),
+             "copy scales");
+  check_cuda(cudaMemcpy(L->biases_, biases, groups * dtype_size(dtype), cudaMemcpyDefault),
+             "copy biases");
+  if (bias != nullptr)
+    check_cuda(cudaMemcpy(L->bias_, bias, output_dims * dtype_size(dtype), cudaMemcpyDefault),
+               "copy bias");
+  check_cuda(cudaDeviceSynchronize(), "copy weights");
+  L->finalize();
+  return L;
+}
+
+std::unique_ptr<QuantizedLinear> QuantizedLinear::from_f32(const float* weight, size_t weight_len,
+                                                           int output_dims, int input_dims,
+                                                           const float* bias, size_t bias_len,
+                                                           int group, cq_dtype dtype, int device) {
+  // validate_linear_shapes (crates/nemotron-mlx/src/model/layers.rs:510-530)
+  const std::string dims = std::to_string(output_dims) + "x" + std::to_string(input_dims);
+  if (output_dims < 0 || input_dims < 0 ||
+      static_cast<size_t>(output_dims) * static_cast<size_t>(input_dims) != weight_len ||
+      bias_len != static_cast<size_t>(output_dims))
+    throw_invalid("invalid model shape: linear weight/bias mismatch for " + dims);
+  if (group <= 0 || input_dims % group != 0)
+    throw_invalid("invalid model shape: linear input dimension " + std::to_string(input_dims) +
+                  " is incompatible with group size " + std::to_string(group));
+  if ((weight == nullptr && weight_len > 0) || (bias == nullptr && bias_len > 0))
+    throw_invalid("weight and bias must not be null");
+  validate_dtype(dtype);
+  validate_group(group);
+  if (output_dims == 0 || input_dims == 0)
+    throw_invalid("invalid model shape: linear dimensions must be positive, got " + dims);
+  device_context(device);
+  DeviceGuard guard(device);
+  std::unique_ptr<QuantizedLinear> L(
+      new QuantizedLinear(output_dims, input_dims, group, dtype, device));
+  L->allocate(true);
+  float* dw = nullptr;
+  float* db = nullptr;
+  check_cuda(cudaMalloc(&dw, weight_len * sizeof(float)), "cudaMalloc(weight)");
+  check_cuda(cudaMalloc(&db, bias_len * sizeof(float)), "cudaMalloc(bias f32)");
+  cudaError_t e = cudaMemcpy(dw, weight, weight_len * sizeof(float), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(db, bias, bias_len * sizeof(float), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess)
+    e = cq::launch_quantize(dtype, dw, output_dims, input_dims, group, dtype != CQ_F32, L->q_,
+                            L->scales_, L->biases_, nullptr);
+  if (e == cudaSuccess) e = cq::launch_f32_to_t(dtype, db, bias_len, L->bias_, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(dw);
+  cudaFree(db);
+  check_cuda(e, "quantize weight");
+  L->finalize();
+  return L;
+}
+
+std::unique_ptr<QuantizedLinear> QuantizedLinear::concat(
+    const std::vector<const QuantizedLinear*>& parts) {
+  if (parts.empty()) throw_invalid("concat needs at least one layer");
+  for (const auto* p : parts)
+    if (p == nullptr) throw_invalid("concat: null layer");
+  const QuantizedLinear& f = *parts[0];
+  int total_n = 0;
+  bool any_bias = false;
+  for (const auto* p : parts) {
+    if (p->K_ != f.K_ || p->group_ != f.group_ || p->dtype_ != f.dtype_ || p->device_ != f.device_)
+      throw_invalid("concat: layers differ in input_dims, group size, dtype or device");
+    total_n += p->N_;
+    any_bias = any_bias || p->bias_ != nullptr;
+  }
+  DeviceGuard guard(f.device_);
+  std::unique_ptr<QuantizedLinear> L(
+      new QuantizedLinear(total_n, f.K_, f.group_, f.dtype_, f.device_));
+  L->allocate(any_bias);
+  const size_t es = dtype_size(f.dtype_);
+  const size_t gpr = f.K_ / f.group_;
+  size_t row = 0;
+  for (const auto* p : parts) {
+    check_cuda(cudaMemcpy(L->q_ + row * f.K_, p->q_, static_cast<size_t>(p->N_) * f.K_,
+                          cudaMemcpyDeviceToDevice),
+               "concat qweight");
+    check_cuda(cudaMemcpy(static_cast<char*>(L->scales_) + row * gpr * es, p->scales_,
+                          p->N_ * gpr * es, cudaMemcpyDeviceToDevice),
+               "concat scales");
+    check_cuda(cudaMemcpy(static_cast<char*>(L->biases_) + row * gpr * es, p->biases_,
+                          p->N_ * gpr * es, cudaMemcpyDeviceToDevice),
+               "concat biases");
+    if (any_bias) {
+      char* dst = static_cast<char*>(L->bias_) + row * es;
+      if (p->bias_ != nullptr)
+        check_cuda(cudaMemcpy(dst, p->bias_, p->N_ * es, cudaMemcpyDeviceToDevice), "concat bias");
+      else
+        check_cuda(cudaMemset(dst, 0, p->N_ * es), "concat zero bias");
+    }
+    row += p->N_;
+  }
+  L->finalize();
+  return L;
+}
+
+void QuantizedLinear::forward_array(const void* x, int ldx, int rows, void* y, int ldy, int act,
+                                    cudaStream_t stream) const {
+  if (rows < 0) throw_invalid("invalid model shape: negative row count");
+  if (rows == 0) return;
+  if (x == nullptr || y == nullptr) throw_invalid("input and output must not be null");
+  if (ldx < K_ || ldy < N_)
+    throw_invalid("leading dimensions (" + std::to_string(ldx) + ", " + std::to_string(ldy) +
+                  ") are smaller than the layer (" + std::to_string(K_) + ", " +
+                  std::to_string(N_) + ")");
+  if (act != CQ_ACT_NONE && act != CQ_ACT_SILU && act != CQ_ACT_RELU)
+    throw_invalid("unknown activation " + std::to_string(act));
+  DeviceContext& ctx = device_context(device_);
+  DeviceGuard guard(device_);
+  if (dtype_ == CQ_F32) {
+    if (ldx != K_ || ldy != N_ || act != CQ_ACT_NONE)
+      throw_invalid("the f32 path takes contiguous rows and no fused activation");
+    check_cuda(cq::launch_qmatmul_f32(static_cast<const float*>(x), rows, K_, q_,
+                                      static_cast<const float*>(scales_),
+                                      static_cast<const float*>(biases_), N_, group_,
+                                      static_cast<float*>(y), stream),
+               "qmatmul_f32");
+    return;
+  }
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0)
+    throw_invalid("input rows must be 16-byte aligned (x % 16 == 0 and ldx % 8 == 0)");
+  cq::GemvArgs a{};
+  a.x = x;
+  a.scales = scales_;
+  a.biases = biases_;
+  a.bias = bias_;
+  a.y = y;
+  a.status = ctx.status;
+  a.M = rows;
+  a.N = N_;
+  a.K = K_;
+  a.ldx = ldx;
+  a.ldy = ldy;
+  a.sb_per_cta = plan_.sb_per_cta;
+  a.act = act;
+  check_cuda(cq::launch_gemv(dtype_, group_, plan_, wmap_, a, stream, pdl_enabled()), "qgemv");
+}
+
+void QuantizedLinear::forward_f32(const float* input, size_t input_len, int rows, float* output,
+                                  size_t output_len) {
+  if (rows < 0 || static_cast<size_t>(rows) * static_cast<size_t>(K_) != input_len)
+    throw_invalid("invalid model shape: linear input has " + std::to_string(input_len) +
+                  " values, expected " + std::to_string(rows) + "x" + std::to_string(K_));
+  if (static_cast<size_t>(rows) * static_cast<size_t>(N_) != output_len)
+    throw_invalid("invalid model shape: linear output has " + std::to_string(output_len) +
+                  " values, expected " + std::to_string(rows) + "x" + std::to_string(N_));
+  if (rows == 0) return;
+  if (input == nullptr || output == nullptr) throw_invalid("input and output must not be null");
+  std::lock_guard<std::mutex> lock(host_mu_);
+  DeviceContext& ctx = device_context(device_);
+  DeviceGuard guard(device_);
+  const size_t es = dtype_size(dtype_);
+  const size_t xin = align_up(input_len * sizeof(float), 256);
+  const size_t xt = align_up(input_len * es, 256);
+  const size_t yt = align_up(output_len * es, 256);
+  const size_t yout = align_up(output_len * sizeof(float), 256);
+  const size_t need = xin + xt + yt + yout;
+  if (need > host_scratch_bytes_) {
+    cudaFree(host_scratch_);
+    host_scratch_ = nullptr;
+    host_scratch_bytes_ = 0;
+    check_cuda(cudaMalloc(&host_scratch_, need), "cudaMalloc(host scratch)");
+    host_scratch_bytes_ = need;
+  }
+  char* base = static_cast<char*>(host_scratch_);
+  float* d_xin = reinterpret_cast<float*>(base);
+  void* d_xt = base + xin;
+  void* d_yt = base + xin + xt;
+  float* d_yout = reinterpret_cast<float*>(base + xin + xt + yt);
+  cudaStream_t s = cudaStreamPerThread;
+  check_cuda(cudaMemcpyAsync(d_xin, input, input_len * sizeof(float), cudaMemcpyHostToDevice, s),
+             "upload input");
+  if (dtype_ == CQ_F32) {
+    forward_array(d_xin, K_, rows, d_yout, N_, CQ_ACT_NONE, s);
+  } else {
+    check_cuda(cq::launch_f32_to_t(dtype_, d_xin, input_len, d_xt, s), "cast input");
+    forward_array(d_xt, K_, rows, d_yt, N_, CQ_ACT_NONE, s);
+    check_cuda(cq::launch_t_to_f32(dtype_, d_yt, output_len, d_yout, s), "widen output");
+  }
+  check_cuda(cudaMemcpyAsync(output, d_yout, output_len * sizeof(float), cudaMemcpyDeviceToHost, s),
+             "download output");
+  int status = 0;
+  check_cuda(cudaMemcpyAsync(&status, ctx.status, sizeof(int), cudaMemcpyDeviceToHost, s),
+             "read device status");
+  check_cuda(cudaStreamSynchronize(s), "forward_f32");
+  if (status != 0)
+    throw Error(CQ_RUNTIME_ERROR, "device watchdog: a kernel gave up waiting (status " +
+                                      std::to_string(status) + ")");
+}
+
+// ------------------------------------------------------------------ backend
+
+void quantized_matmul(const float* input, size_t input_len, size_t rows, size_t input_dims,
+                      const float* weight, size_t weight_len, size_t output_dims,
+                      size_t group_size, float* output, size_t output_len) {
+  // Validation order and texts of backend::quantized_matmul
+  // (crates/nemotron-mlx/src/backend/mod.rs:49-75).
+  const char* P = "invalid matrix shape: ";
+  if (rows * input_dims != input_len || (input_dims != 0 && (rows * input_dims) / input_dims != rows))
+    throw_invalid(fmt_shape_error(P, "input has " + std::to_string(input_len) +
+                                         " values, expected " + std::to_string(rows) + "x" +
+                                         std::to_string(input_dims)));
+  if (output_dims * input_dims != weight_len)
+    throw_invalid(fmt_shape_error(P, "weight has " + std::to_string(weight_len) +
+                                         " values, expected " + std::to_string(output_dims) +
+                                         "x" + std::to_string(input_dims)));
+  if (group_size == 0) throw_invalid(fmt_shape_error(P, "group size must be positive"));
+  if (input_dims % group_size != 0)
+    throw_invalid(fmt_shape_error(P, "input dimension " + std::to_string(input_dims) +
+                                         " is not divisible by group size " +
+                                         std::to_string(group_size)));
+  validate_group(static_cast<int>(group_size));
+  if (output_len != rows * output_dims)
+    throw_invalid(fmt_shape_error(P, "output has " + std::to_string(output_len) +
+                                         " values, expected " + std::to_string(rows) + "x" +
+                                         std::to_string(output_dims)));
+  if (rows == 0 || output_dims == 0) return;
+  if (input == nullptr || weight == nullptr || output == nullptr)
+    throw_invalid("input, weight and output must not be null");
+  int device = 0;
+  check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+  device_context(device);
+  const size_t groups = output_dims * (input_dims / group_size);
+  char* buf = nullptr;
+  const size_t o_w = 0;
+  const size_t o_x = align_up(o_w + weight_len * 4, 256);
+  const size_t o_q = align_up(o_x + input_len * 4, 256);
+  const size_t o_s = align_up(o_q + weight_len, 256);
+  const size_t o_b = align_up(o_s + groups * 4, 256);
+  const size_t o_y = align_up(o_b + groups * 4, 256);
+  const size_t total = o_y + output_len * 4;
+  check_cuda(cudaMalloc(&buf, total), "cudaMalloc(quantized_matmul)");
+  float* dw = reinterpret_cast<float*>(buf + o_w);
+  float* dx = reinterpret_cast<float*>(buf + o_x);
+  uint8_t* dq = reinterpret_cast<uint8_t*>(buf + o_q);
+  float* ds = reinterpret_cast<float*>(buf + o_s);
+  float* db = reinterpret_cast<float*>(buf + o_b);
+  float* dy = reinterpret_cast<float*>(buf + o_y);
+  cudaStream_t s = cudaStreamPerThread;
+  cudaError_t e = cudaMemcpyAsync(dw, weight, weight_len * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dx, input, input_len * 4, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess)
+    e = cq::launch_quantize(CQ_F32, dw, static_cast<int>(output_dims), static_cast<int>(input_dims),
+                            static_cast<int>(group_size), false, dq, ds, db, s);
+  if (e == cudaSuccess)
+    e = cq::launch_qmatmul_f32(dx, static_cast<int>(rows), static_cast<int>(input_dims), dq, ds, db,
+                               static_cast<int>(output_dims), static_cast<int>(group_size), dy, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(output, dy, output_len * 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  cudaFree(buf);
+  check_cuda(e, "quantized_matmul");
+}
+
+}  // namespace nemotron_cuda

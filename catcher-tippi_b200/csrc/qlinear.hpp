@@ -1,0 +1,123 @@
+// C++ host layer of the B200 quantized linear: the counterpart of the
+// reference's Rust `QuantizedLinear` (crates/nemotron-mlx/src/model/layers.rs:208-319),
+// `PointwiseConv1d` (layers.rs:321-352) and `backend::quantized_matmul`
+// (crates/nemotron-mlx/src/backend/mod.rs:41-94).  The C ABI in
+// include/cqlinear.h wraps these classes; errors are C++ exceptions inside the
+// library and status codes at the ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "cqlinear.h"
+#include "qgemv.hpp"
+
+namespace nemotron_cuda {
+
+// Error carrying the ABI status.  Shape errors use the reference's texts
+// (ModelError::InvalidShape prints "invalid model shape: ...",
+// BackendError::InvalidShape prints "invalid matrix shape: ...").
+class Error : public std::runtime_error {
+ public:
+  Error(cq_status status, const std::string& msg) : std::runtime_error(msg), status_(status) {}
+  cq_status status() const { return status_; }
+
+ private:
+  cq_status status_;
+};
+
+[[noreturn]] void throw_invalid(const std::string& msg);
+void check_cuda(cudaError_t e, const char* what);
+
+// Per-device state: SM count and the device watchdog word.
+struct DeviceContext {
+  int device = 0;
+  int num_sms = 0;
+  int* status = nullptr;  // device int, see cq_device_status
+};
+DeviceContext& device_context(int device);
+
+// Restores the caller's current device on scope exit.
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int device);
+  ~DeviceGuard();
+
+ private:
+  int prev_ = -1;
+};
+
+// Builds the 2-D u8 tensor map the K1 kernel streams weights through.
+CUtensorMap make_weight_map(const void* q, int N, int K, int box_rows);
+
+class QuantizedLinear {
+ public:
+  // Packed arrays in host memory -> owned device copy (from_artifact).
+  static std::unique_ptr<QuantizedLinear> from_packed(const uint32_t* qweight, const void* scales,
+                                                      const void* biases, const void* bias,
+                                                      int output_dims, int input_dims, int group,
+                                                      cq_dtype dtype, int device);
+  // f32 weight in host memory, quantised on the device (from_f32).
+  static std::unique_ptr<QuantizedLinear> from_f32(const float* weight, size_t weight_len,
+                                                   int output_dims, int input_dims,
+                                                   const float* bias, size_t bias_len, int group,
+                                                   cq_dtype dtype, int device);
+  static std::unique_ptr<QuantizedLinear> concat(const std::vector<const QuantizedLinear*>& parts);
+
+  ~QuantizedLinear();
+  QuantizedLinear(const QuantizedLinear&) = delete;
+  QuantizedLinear& operator=(const QuantizedLinear&) = delete;
+
+  // Device pointers in T, asynchronous (forward_array).
+  void forward_array(const void* x, int ldx, int rows, void* y, int ldy, int act,
+                     cudaStream_t stream) const;
+  // Host f32 in / out, synchronous (forward_f32).
+  void forward_f32(const float* input, size_t input_len, int rows, float* output,
+                   size_t output_len);
+
+  int input_dims() const { return K_; }
+  int output_dims() const { return N_; }
+  int group_size() const { return group_; }
+  cq_dtype dtype() const { return dtype_; }
+  int device() const { return device_; }
+  const void* qweight() const { return q_; }
+  const void* scales() const { return scales_; }
+  const void* biases() const { return biases_; }
+  const void* bias() const { return bias_; }
+
+ private:
+  QuantizedLinear(int N, int K, int group, cq_dtype dtype, int device);
+  void allocate(bool with_bias);
+  void finalize();  // plan + tensor map once the arrays are in place
+
+  int N_, K_, group_;
+  cq_dtype dtype_;
+  int device_;
+  uint8_t* q_ = nullptr;
+  void* scales_ = nullptr;
+  void* biases_ = nullptr;
+  void* bias_ = nullptr;
+  cq::GemvPlan plan_{};
+  CUtensorMap wmap_{};
+
+  // Scratch of the synchronous host-f32 path, grown on demand.
+  std::mutex host_mu_;
+  void* host_scratch_ = nullptr;
+  size_t host_scratch_bytes_ = 0;
+};
+
+size_t dtype_size(cq_dtype dtype);
+
+// backend::quantized_matmul: quantise the f32 weight (f32 scales) on the
+// device and return input . dequant(weight)^T as f32.
+void quantized_matmul(const float* input, size_t input_len, size_t rows, size_t input_dims,
+                      const float* weight, size_t weight_len, size_t output_dims,
+                      size_t group_size, float* output, size_t output_len);
+
+}  // namespace nemotron_cuda
