@@ -11,12 +11,16 @@
 //  * Each CTA owns a band of RB = 16*RT weight rows and a K-range of
 //    `sb_per_cta` 64-wide sub-blocks.  Its whole weight tile is requested up
 //    front with 2-D TMA bulk-tensor loads (one mbarrier per sub-block, L2
-//    evict-first), together with the group scales/biases, BEFORE
+//    evict-first), and the group scales/biases are loaded, BEFORE
 //    griddepcontrol.wait: under programmatic dependent launch the weight
-//    stream of this linear overlaps the tail of the previous kernel.
-//  * The K-split CTAs of one band form a thread-block cluster and reduce their
-//    fp32 partials through distributed shared memory: no global scratch, no
-//    atomics, deterministic order.
+//    stream of this linear overlaps the previous kernel.
+//  * After the wait the critical path is short: every warp owns at most two
+//    sub-blocks and issues all of its activation loads at once (one L2 round
+//    trip), converts, runs the MMAs, and the K-split partials are reduced.
+//  * The K-split CTAs of one band form a thread-block cluster: each pushes its
+//    fp32 partial into the leader CTA's shared memory (distributed shared
+//    memory stores), one cluster barrier, and the leader finishes the
+//    epilogue.  No global scratch, no atomics, deterministic order.
 //  * Tensor cores via mma.m16n8k16 (f16 x f16 -> f32): weight rows are the MMA
 //    M dimension, tokens the N dimension.  A weight byte q becomes the f16
 //    value 1024 + q with one PRMT (bits 0x64qq), exact; the 1024 offset is
@@ -26,7 +30,7 @@
 //    to f16 with a per-(token, 64-wide sub-block) power-of-two scale that is
 //    undone in fp32, which is exact for every element within 2^-28 of the
 //    block's largest magnitude.
-//  * Each lane loads 16 contiguous weight bytes per row; the k-slot order of
+//  * Each lane reads 16 contiguous weight bytes per row; the k-slot order of
 //    the MMA fragments is permuted identically for A and B, so the MLX layout
 //    is consumed as is (no repacking) and shared-memory reads are
 //    conflict-free.
@@ -42,58 +46,64 @@ namespace cq {
 
 namespace {
 
-constexpr int kNW = 4;            // warps per CTA
+constexpr int kNW = 8;  // warps per CTA
 constexpr int kThreads = kNW * 32;
-constexpr int kMaxSubBlocks = 16;  // sub-blocks (of 64 k) per CTA
+constexpr int kMaxSubBlocks = 16;               // sub-blocks (of 64 k) per CTA
+constexpr int kSbPerWarp = kMaxSubBlocks / kNW;  // at most two per warp
+constexpr int kMaxSbPerThread = (kMaxSubBlocks * 2 * 64 + kThreads - 1) / kThreads;
+constexpr int kMaxCluster = 8;
 
 struct GemvSmem {
-  size_t wt, bars, sbsm, red, fin, total;
+  size_t wt, bars, sbsm, biasm, red, fin, total;
 };
 
-__host__ __device__ inline GemvSmem gemv_smem_layout(int rt, int sb_per_cta, int subg) {
+__host__ __device__ inline GemvSmem gemv_smem_layout(int rt, int sb_per_cta, int subg,
+                                                     int ksplit) {
   const int rb = 16 * rt;
   GemvSmem L{};
   size_t off = 0;
-  L.wt = off;
+  L.wt = off;  // [sb_per_cta][rb][64] u8, TMA destination
   off += static_cast<size_t>(sb_per_cta) * rb * 64;
-  off = (off + 127) & ~static_cast<size_t>(127);
-  L.bars = off;
+  L.bars = off;  // one weight barrier per sub-block
   off += kMaxSubBlocks * 8;
-  L.sbsm = off;
+  L.sbsm = off;  // [sb_per_cta * subg][rb] (s, b - 1024 s)
   off += static_cast<size_t>(sb_per_cta) * subg * rb * sizeof(float2);
-  L.red = off;
+  L.biasm = off;  // [rb] output bias
+  off += static_cast<size_t>(rb) * sizeof(float);
+  L.red = off;  // [kNW][rb][16] per-warp partials
   off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
-  L.fin = off;
-  off += static_cast<size_t>(rb) * 16 * sizeof(float);
+  L.fin = off;  // [ksplit][rb][16]: CTA partials pushed into the cluster leader
+  off += static_cast<size_t>(ksplit > 1 ? ksplit : 0) * rb * 16 * sizeof(float);
   L.total = off;
   return L;
 }
 
-// Loads this lane's 16 activation values of one token for one 64-wide
-// sub-block, converts them to f16 MMA B-fragments and returns the per-half
-// sums of the converted values (reduced over the 4 lanes of the quad) and the
-// inverse of the power-of-two scale that was applied.
-//   G >= 64: values k = kb + 16c + [0, 16)
-//   G == 32: values k = kb + 8c + [0, 8) and kb + 32 + 8c + [0, 8)
-template <int DT, int G>
-__device__ __forceinline__ void load_x_frag(const void* __restrict__ x, int ldx, int M, int K,
-                                            int m, int kb, int c, uint32_t (&xb)[8],
-                                            float (&xs)[2], float& inv) {
-  uint4 r0 = make_uint4(0, 0, 0, 0), r1 = make_uint4(0, 0, 0, 0);
-  if (m < M) {
-    const uint16_t* xr = reinterpret_cast<const uint16_t*>(x) + static_cast<size_t>(m) * ldx;
-    if constexpr (G >= 64) {
-      const int k = kb + 16 * c;
-      if (k < K) {
-        r0 = ld_global_cg_v4(xr + k);
-        r1 = ld_global_cg_v4(xr + k + 8);
-      }
-    } else {
-      const int k0 = kb + 8 * c, k1 = kb + 32 + 8 * c;
-      if (k0 < K) r0 = ld_global_cg_v4(xr + k0);
-      if (k1 < K) r1 = ld_global_cg_v4(xr + k1);
-    }
+// Raw activation loads of one token for one 64-wide sub-block (this lane's 16
+// values; zeros past M and past K):
+//   G >= 64: k = kb + 16c + [0, 16)
+//   G == 32: k = kb + 8c + [0, 8) and kb + 32 + 8c + [0, 8)
+template <int G>
+__device__ __forceinline__ void load_x_raw(const void* __restrict__ x, int ldx, int M, int K, int m,
+                                           int kb, int c, uint4& r0, uint4& r1) {
+  r0 = make_uint4(0, 0, 0, 0);
+  r1 = make_uint4(0, 0, 0, 0);
+  if (m >= M) return;
+  const uint16_t* xr = reinterpret_cast<const uint16_t*>(x) + static_cast<size_t>(m) * ldx;
+  if constexpr (G >= 64) {
+    r0 = ld_global_cg_v4(xr + kb + 16 * c);
+    r1 = ld_global_cg_v4(xr + kb + 16 * c + 8);
+  } else {
+    r0 = ld_global_cg_v4(xr + kb + 8 * c);
+    if (kb + 32 < K) r1 = ld_global_cg_v4(xr + kb + 32 + 8 * c);
   }
+}
+
+// Converts this lane's 16 raw activation values into f16 MMA B-fragments and
+// returns the per-half sums of the converted values (reduced over the 4 lanes
+// of the quad) and the inverse of the power-of-two scale that was applied.
+template <int DT, int G>
+__device__ __forceinline__ void x_frag(const uint4& r0, const uint4& r1, uint32_t (&xb)[8],
+                                       float (&xs)[2], float& inv) {
   const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
   float s0 = 0.f, s1 = 0.f;
   if constexpr (DT == kF16) {
@@ -145,8 +155,24 @@ __device__ __forceinline__ void load_x_frag(const void* __restrict__ x, int ldx,
   }
 }
 
+template <int DT>
+__device__ __forceinline__ float epilogue_value(float acc, bool has_bias, float bias, int act) {
+  float o = round_t<DT>(acc);
+  if (has_bias) o = round_t<DT>(o + bias);
+  if (act == kActSilu) {
+    o = round_t<DT>(o / (1.0f + expf(-o)));
+  } else if (act == kActRelu) {
+    o = o > 0.0f ? o : 0.0f;
+  }
+  return o;
+}
+
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
 template <int DT, int G, int RT>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 2)
     qgemv_kernel(const __grid_constant__ CUtensorMap wmap, const GemvArgs a) {
   constexpr int RB = 16 * RT;
   constexpr int SUBG = (G == 32) ? 2 : 1;  // groups per 64-wide sub-block
@@ -160,56 +186,91 @@ __global__ void __launch_bounds__(kThreads)
   const int sbn = max(0, min(a.sb_per_cta, nsb - sb0));
   const int groups_per_row = a.K / G;
 
-  const GemvSmem L = gemv_smem_layout(RT, a.sb_per_cta, SUBG);
+  const GemvSmem L = gemv_smem_layout(RT, a.sb_per_cta, SUBG, S);
   uint8_t* wt = smem + L.wt;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   float2* sbsm = reinterpret_cast<float2*>(smem + L.sbsm);
+  float* biasm = reinterpret_cast<float*>(smem + L.biasm);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* fin = reinterpret_cast<float*>(smem + L.fin);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = lane & 3, r4 = lane >> 2;
 
-  // Let the next kernel in the stream start its own weight prefetch now.
-  pdl_launch_dependents();
-
   // ---- weight tile: independent of the previous kernel, issued first.
   if (tid == 0) {
     prefetch_tensormap(&wmap);
     for (int j = 0; j < sbn; ++j) mbar_init(&bars[j], 1);
     fence_mbar_init();
-    const uint64_t pol = l2_policy_evict_first();
+    // weights are read once, unless token tiles are spread over grid.z
+    const uint64_t pol = gridDim.z == 1 ? l2_policy_evict_first() : l2_policy_evict_normal();
     for (int j = 0; j < sbn; ++j) {
       mbar_arrive_expect_tx(&bars[j], RB * 64);
       tma_load_2d(wt + static_cast<size_t>(j) * RB * 64, &wmap, (sb0 + j) * 64, n0, &bars[j], pol);
     }
   }
 
-  // ---- group scales/biases as fp32 (s, b - 1024 s), groups fastest.
+  // ---- group scales/biases (fp32 (s, b - 1024 s)) and the output bias: all
+  // loads issued back to back, then stored, so the CTA pays one latency.
   {
     const int per_row = sbn * SUBG;
     const int total = per_row * RB;
-    for (int e = tid; e < total; e += kThreads) {
-      const int row = e / per_row, jh = e - row * per_row;
-      const int n = n0 + row;
-      const int kfirst = (sb0 + jh / SUBG) * 64 + (jh % SUBG) * 32;
-      float s = 0.f, b = 0.f;
-      if (n < a.N && kfirst < a.K) {
-        const size_t gi = static_cast<size_t>(n) * groups_per_row + kfirst / G;
-        s = ld_t<DT>(a.scales, gi);
-        b = ld_t<DT>(a.biases, gi);
+    float sv[kMaxSbPerThread], bv[kMaxSbPerThread];
+#pragma unroll
+    for (int i = 0; i < kMaxSbPerThread; ++i) {
+      const int e = tid + i * kThreads;
+      sv[i] = 0.f;
+      bv[i] = 0.f;
+      if (e < total) {
+        const int row = e / per_row, jh = e - row * per_row;
+        const int n = n0 + row;
+        const int kfirst = (sb0 + jh / SUBG) * 64 + (jh % SUBG) * 32;
+        if (n < a.N && kfirst < a.K) {
+          const size_t gi = static_cast<size_t>(n) * groups_per_row + kfirst / G;
+          sv[i] = ld_t<DT>(a.scales, gi);
+          bv[i] = ld_t<DT>(a.biases, gi);
+        }
       }
-      sbsm[jh * RB + row] = make_float2(s, fmaf(-1024.0f, s, b));
     }
+    float bias_v = 0.f;
+    if (a.bias != nullptr && tid < RB && n0 + tid < a.N) bias_v = ld_t<DT>(a.bias, n0 + tid);
+#pragma unroll
+    for (int i = 0; i < kMaxSbPerThread; ++i) {
+      const int e = tid + i * kThreads;
+      if (e < total) {
+        const int row = e / per_row, jh = e - row * per_row;
+        sbsm[jh * RB + row] = make_float2(sv[i], fmaf(-1024.0f, sv[i], bv[i]));
+      }
+    }
+    if (tid < RB) biasm[tid] = bias_v;
   }
+
+  // Let the next kernel in the stream start its own weight prefetch.
+  pdl_launch_dependents();
   __syncthreads();
 
   // ---- from here on the activations of the previous kernel are needed.
   pdl_wait();
 
   bool ok = true;
+  const bool has_bias = a.bias != nullptr;
   const int mtiles = (a.M + 15) >> 4;
-  for (int mt = 0; mt < mtiles; ++mt) {
+  // Token tiles blockIdx.z, blockIdx.z + gridDim.z, ... belong to this CTA.
+  const int mt0 = blockIdx.z, mstep = gridDim.z;
+  // All activation loads of this warp's sub-blocks in flight at once.
+  uint4 xr[kSbPerWarp][2][2];
+#pragma unroll
+  for (int u = 0; u < kSbPerWarp; ++u) {
+    const int j = warp + u * kNW;
+    if (j < sbn) {
+      const int kb = (sb0 + j) * 64;
+      load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt0 * 16 + r4, kb, c, xr[u][0][0], xr[u][0][1]);
+      load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt0 * 16 + 8 + r4, kb, c, xr[u][1][0], xr[u][1][1]);
+    }
+  }
+  bool first_tile = true;
+  for (int mt = mt0; mt < mtiles; mt += mstep) {
+
     float acc[RT][2][4];
 #pragma unroll
     for (int i = 0; i < RT; ++i)
@@ -218,12 +279,14 @@ __global__ void __launch_bounds__(kThreads)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
 
-    for (int j = warp; j < sbn; j += kNW) {
-      const int kb = (sb0 + j) * 64;
+#pragma unroll
+    for (int u = 0; u < kSbPerWarp; ++u) {
+      const int j = warp + u * kNW;
+      if (j >= sbn) break;
       uint32_t xb[2][8];
       float xs[2][2], inv[2];
-      load_x_frag<DT, G>(a.x, a.ldx, a.M, a.K, mt * 16 + r4, kb, c, xb[0], xs[0], inv[0]);
-      load_x_frag<DT, G>(a.x, a.ldx, a.M, a.K, mt * 16 + 8 + r4, kb, c, xb[1], xs[1], inv[1]);
+      x_frag<DT, G>(xr[u][0][0], xr[u][0][1], xb[0], xs[0], inv[0]);
+      x_frag<DT, G>(xr[u][1][0], xr[u][1][1], xb[1], xs[1], inv[1]);
       // Token-side epilogue operands for the accumulator columns 2c, 2c+1.
       float xsA[2][SUBG], xsB[2][SUBG], ivA[2], ivB[2];
 #pragma unroll
@@ -237,7 +300,7 @@ __global__ void __launch_bounds__(kThreads)
         ivB[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c + 4);
       }
 
-      if (mt == 0) ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
+      if (first_tile) ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
 
       const uint8_t* wj = wt + static_cast<size_t>(j) * RB * 64;
       const float2* sbj = sbsm + static_cast<size_t>(j) * SUBG * RB;
@@ -304,7 +367,23 @@ __global__ void __launch_bounds__(kThreads)
       }
     }
 
-    // ---- reduce the K-split partials: warps of this CTA, then the cluster.
+    first_tile = false;
+    // Next token tile's activations: the loads overlap this tile's reduction.
+    const int mt_next = mt + mstep;
+    if (mt_next < mtiles) {
+#pragma unroll
+      for (int u = 0; u < kSbPerWarp; ++u) {
+        const int j = warp + u * kNW;
+        if (j < sbn) {
+          const int kb = (sb0 + j) * 64;
+          load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt_next * 16 + r4, kb, c, xr[u][0][0], xr[u][0][1]);
+          load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt_next * 16 + 8 + r4, kb, c, xr[u][1][0],
+                        xr[u][1][1]);
+        }
+      }
+    }
+
+    // ---- reduce: warps of this CTA through shared memory ...
 #pragma unroll
     for (int i = 0; i < RT; ++i) {
       const int ra = 16 * i + r4, rb = ra + 8;
@@ -318,6 +397,7 @@ __global__ void __launch_bounds__(kThreads)
     }
     __syncthreads();
 
+    // element e = tok * RB + row: consecutive threads write consecutive n
     if (S == 1) {
       for (int e = tid; e < RB * 16; e += kThreads) {
         const int row = e % RB, tok = e / RB;
@@ -326,35 +406,41 @@ __global__ void __launch_bounds__(kThreads)
         for (int w = 0; w < kNW; ++w) v += red[(w * RB + row) * 16 + tok];
         const int n = n0 + row, m = mt * 16 + tok;
         if (n < a.N && m < a.M)
-          st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n, linear_epilogue<DT>(v, a.bias, n, a.act));
+          st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n,
+                   epilogue_value<DT>(v, has_bias, biasm[row], a.act));
       }
       __syncthreads();
     } else {
+      // ... then every CTA of the cluster pushes its partial into the
+      // leader's slot `rank`; one cluster barrier; the leader finishes.
+      const uint32_t slot = mapa_shared(smem_u32(fin), 0) +
+                            static_cast<uint32_t>(rank * RB * 16 * sizeof(float));
       for (int e = tid; e < RB * 16; e += kThreads) {
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < kNW; ++w) v += red[w * RB * 16 + e];
-        fin[e] = v;
+        st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
       }
       cluster_sync_all();
-      const int r_lo = rank * RB / S, r_hi = (rank + 1) * RB / S, nr = r_hi - r_lo;
-      const uint32_t fin_addr = smem_u32(fin);
-      for (int e = tid; e < nr * 16; e += kThreads) {
-        const int row = r_lo + e % nr, tok = e / nr;
-        const uint32_t off = static_cast<uint32_t>((row * 16 + tok) * sizeof(float));
-        float v = 0.f;
-        for (int q = 0; q < S; ++q) v += ld_dsmem_f32(mapa_shared(fin_addr + off, q));
-        const int n = n0 + row, m = mt * 16 + tok;
-        if (n < a.N && m < a.M)
-          st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n, linear_epilogue<DT>(v, a.bias, n, a.act));
+      if (rank == 0) {
+        for (int e = tid; e < RB * 16; e += kThreads) {
+          const int row = e % RB, tok = e / RB;
+          float v = 0.f;
+          for (int q = 0; q < S; ++q) v += fin[(q * RB + row) * 16 + tok];
+          const int n = n0 + row, m = mt * 16 + tok;
+          if (n < a.N && m < a.M)
+            st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n,
+                     epilogue_value<DT>(v, has_bias, biasm[row], a.act));
+        }
       }
-      cluster_sync_all();
+      // the leader's slots are rewritten by the next token tile
+      if (mt_next < mtiles) cluster_sync_all();
     }
   }
 
   if (!ok && tid == 0) {
-    // A weight copy never completed: wait (bounded) once more for the copies
-    // in flight before the shared memory is released.
+    // A copy never completed: wait (bounded) once more for the copies in
+    // flight before the shared memory is released.
     for (int j = 0; j < sbn; ++j) mbar_wait_bounded(&bars[j], 0, a.status);
   }
 }
@@ -363,7 +449,7 @@ template <int DT, int G, int RT>
 cudaError_t launch_typed(const GemvPlan& plan, const CUtensorMap& wmap, const GemvArgs& args,
                          cudaStream_t stream, bool pdl) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
-  const GemvSmem L = gemv_smem_layout(RT, plan.sb_per_cta, SUBG);
+  const GemvSmem L = gemv_smem_layout(RT, plan.sb_per_cta, SUBG, plan.ksplit);
   auto kern = qgemv_kernel<DT, G, RT>;
   static int configured_smem = 0;
   if (static_cast<int>(L.total) > configured_smem) {
@@ -373,7 +459,11 @@ cudaError_t launch_typed(const GemvPlan& plan, const CUtensorMap& wmap, const Ge
     configured_smem = static_cast<int>(L.total);
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(plan.ksplit, (args.N + 16 * RT - 1) / (16 * RT), 1);
+  // token tiles beyond the first spread over grid.z, within one wave
+  const int bands = (args.N + 16 * RT - 1) / (16 * RT);
+  const int mtiles = (args.M + 15) / 16;
+  const int zmax = std::max(1, (2 * plan.num_sms) / std::max(1, bands * plan.ksplit));
+  cfg.gridDim = dim3(plan.ksplit, bands, std::min(mtiles, zmax));
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
@@ -418,45 +508,40 @@ cudaError_t launch_g(int group, const GemvPlan& plan, const CUtensorMap& wmap,
   }
 }
 
+bool plan_ok(int nsb, int s, int spc) {
+  return s >= 1 && s <= kMaxCluster && spc >= 1 && spc <= kMaxSubBlocks && (s - 1) * spc < nsb;
+}
+
 }  // namespace
 
 GemvPlan plan_gemv(int N, int K, int num_sms) {
   const int nsb = (K + 63) / 64;
   if (const char* env = std::getenv("CQ_GEMV_PLAN")) {
     int rt = 0, s = 0;
-    if (std::sscanf(env, "%d,%d", &rt, &s) == 2 && (rt == 1 || rt == 2 || rt == 4) && s >= 1 &&
-        s <= 8) {
-      const int spc = (nsb + s - 1) / s;
-      if (spc <= kMaxSubBlocks) return GemvPlan{rt, s, spc};
+    if (std::sscanf(env, "%d,%d", &rt, &s) == 2 && (rt == 1 || rt == 2 || rt == 4)) {
+      const int spc = (nsb + s - 1) / std::max(s, 1);
+      if (plan_ok(nsb, s, spc)) return GemvPlan{rt, s, spc, num_sms};
     }
   }
-  GemvPlan best{4, 1, std::min(nsb, kMaxSubBlocks)};
-  double best_score = -1e300;
-  for (int rt : {4, 2, 1}) {
-    const int rb = 16 * rt;
-    const int bands = (N + rb - 1) / rb;
-    for (int s = 1; s <= 8; ++s) {
-      const int spc = (nsb + s - 1) / s;
-      if (spc > kMaxSubBlocks) continue;
-      if ((s - 1) * spc >= nsb) continue;  // every rank must own work
-      const int ctas = bands * s;
-      // SMs that receive work, discounted for warps left idle inside a CTA,
-      // for cluster-reduction overhead and for very small tiles.
-      const double busy = std::min(ctas, num_sms);
-      const double warp_eff = std::min(spc, kNW) / static_cast<double>(kNW);
-      const double waves = std::ceil(ctas / (2.0 * num_sms));
-      const double score = busy * warp_eff / waves - 2.0 * (s - 1) + 0.5 * rt;
-      if (score > best_score) {
-        best_score = score;
-        best = GemvPlan{rt, s, spc};
-      }
+  // Measured on B200 (back-to-back launches, M = 14): the cluster reduction
+  // costs more than it saves, so K is split only as far as the 16 sub-blocks
+  // a CTA can hold require; rows per CTA grow only to stay within one wave of
+  // two CTAs per SM.
+  const int s = std::max(1, (nsb + kMaxSubBlocks - 1) / kMaxSubBlocks);
+  const int spc = (nsb + s - 1) / s;
+  GemvPlan best{4, s, spc, num_sms};
+  for (int rt : {1, 2, 4}) {
+    const int bands = (N + 16 * rt - 1) / (16 * rt);
+    if (bands * s <= 2 * num_sms) {
+      best = GemvPlan{rt, s, spc, num_sms};
+      break;
     }
   }
   return best;
 }
 
 size_t gemv_smem_bytes(const GemvPlan& plan, int group) {
-  return gemv_smem_layout(plan.rt, plan.sb_per_cta, group == 32 ? 2 : 1).total;
+  return gemv_smem_layout(plan.rt, plan.sb_per_cta, group == 32 ? 2 : 1, plan.ksplit).total;
 }
 
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,

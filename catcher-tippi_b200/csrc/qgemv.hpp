@@ -25,6 +25,7 @@ struct GemvPlan {
   int rt;
   int ksplit;
   int sb_per_cta;
+  int num_sms;  // of the device the plan is for (bounds grid.z to one wave)
 };
 
 GemvPlan plan_gemv(int N, int K, int num_sms);

@@ -42,6 +42,8 @@ void validate_dtype(cq_dtype dtype) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+constexpr int kMaxInputDims = 8192;
+
 }  // namespace
 
 [[noreturn]] void throw_invalid(const std::string& msg) { throw Error(CQ_INVALID_ARGUMENT, msg); }
@@ -146,6 +148,11 @@ void QuantizedLinear::allocate(bool with_bias) {
 
 void QuantizedLinear::finalize() {
   if (dtype_ == CQ_F32) return;  // the f32 path uses the CUDA-core kernel
+  // K1 holds at most 16 sub-blocks of 64 per CTA and splits K over a
+  // portable cluster of at most 8 CTAs.
+  if (K_ > kMaxInputDims)
+    throw_invalid("input_dims " + std::to_string(K_) + " exceeds the supported maximum " +
+                  std::to_string(kMaxInputDims));
   DeviceContext& ctx = device_context(device_);
   plan_ = cq::plan_gemv(N_, K_, ctx.num_sms);
   wmap_ = make_weight_map(q_, N_, K_, 16 * plan_.rt);

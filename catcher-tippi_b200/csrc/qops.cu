@@ -64,7 +64,8 @@ __global__ void dequantize_kernel(const uint8_t* __restrict__ q, const void* __r
        i += static_cast<size_t>(gridDim.x) * blockDim.x) {
     const size_t n = i / K, k = i % K;
     const size_t gi = n * groups + k / g;
-    w[i] = ld_t<DT>(scales, gi) * static_cast<float>(q[i]) + ld_t<DT>(biases, gi);
+    // scale * q + bias with two roundings (no contraction), as the formula reads
+    w[i] = __fadd_rn(__fmul_rn(ld_t<DT>(scales, gi), static_cast<float>(q[i])), ld_t<DT>(biases, gi));
   }
 }
 
