@@ -180,6 +180,41 @@ class EncoderLinears:
                                   stream_ptr)
 
 
+class SingleLinear:
+    """Back-to-back independent launches of the single-linear workload:
+    x bf16 [14, 1024] . W[4096, 1024]^T, group 64, over 40 distinct weight
+    copies (~184 MB, larger than L2); every launch reads the same x."""
+
+    COPIES = 40
+    N, K = 4096, 1024
+
+    def __init__(self, torch, cq, device: int, seed: int = 0):
+        dev = torch.device("cuda", device)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        self.layers = []
+        for _ in range(self.COPIES):
+            w = torch.randn((self.N, self.K), generator=gen, device=dev) * 0.02
+            q, s, b = cq.quantize(w, GROUP, "bf16")
+            self.layers.append(cq.QuantizedLinear.from_device(q, s, b, None, GROUP, "bf16", device))
+            del w, q, s, b
+        self.x0 = torch.randn((M_FRAMES, self.K), generator=gen, device=dev).to(torch.bfloat16)
+        self.ys = [torch.empty((M_FRAMES, self.N), dtype=torch.bfloat16, device=dev)
+                   for _ in range(2)]
+        self.final = self.ys[(self.COPIES - 1) % 2]
+
+    def launch_step(self, stream_ptr: int) -> None:
+        for i, layer in enumerate(self.layers):
+            y = self.ys[i % 2]
+            layer.forward_raw(self.x0.data_ptr(), self.K, M_FRAMES, y.data_ptr(), self.N, "none",
+                              stream_ptr)
+
+
+LINEAR_BYTES = linear_bytes(SingleLinear.N, SingleLinear.K, M_FRAMES)
+LINEAR_WORKLOAD = ("single INT8 affine quantized linear x bf16 [14,1024] . W[4096,1024]^T, "
+                   "group 64, 40 independent back-to-back launches over distinct weight copies")
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import nemotron_cuda as cq
@@ -190,7 +225,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    enc = EncoderLinears(torch, cq, local_rank)
+    if args.workload == "linear":
+        enc = SingleLinear(torch, cq, local_rank)
+        step_bytes, launches, workload = LINEAR_BYTES * SingleLinear.COPIES, SingleLinear.COPIES, LINEAR_WORKLOAD
+        in_shape, out_t = (M_FRAMES, SingleLinear.K), None
+    else:
+        enc = EncoderLinears(torch, cq, local_rank)
+        step_bytes, launches, workload = STEP_BYTES, LAUNCHES_PER_STEP, WORKLOAD
+        in_shape, out_t = (M_FRAMES, 1024), None
 
     # eager warm-up (sets kernel attributes before capture), then capture.
     stream = torch.cuda.Stream()
@@ -201,14 +243,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     with torch.cuda.graph(graph, stream=stream):
         enc.launch_step(stream.cuda_stream)
     # end-to-end graph: pinned host input -> device, chain, device -> pinned host
-    host_in = torch.empty((M_FRAMES, 1024), dtype=torch.bfloat16).pin_memory()
+    final = enc.final if args.workload == "linear" else enc.out["ffn2_down"]
+    host_in = torch.empty(in_shape, dtype=torch.bfloat16).pin_memory()
     host_in.copy_(enc.x0.cpu())
-    host_out = torch.empty((M_FRAMES, 1024), dtype=torch.bfloat16).pin_memory()
+    host_out = torch.empty(tuple(final.shape), dtype=torch.bfloat16).pin_memory()
     graph_e2e = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph_e2e, stream=stream):
         enc.x0.copy_(host_in, non_blocking=True)
         enc.launch_step(stream.cuda_stream)
-        host_out.copy_(enc.out["ffn2_down"], non_blocking=True)
+        host_out.copy_(final, non_blocking=True)
     torch.cuda.synchronize()
 
     def timed(g) -> float:
@@ -248,27 +291,27 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if status != 0:
         raise RuntimeError(f"device watchdog reported status {status}")
     ms_step = ms / args.steps
-    value = world * STEP_BYTES / (ms_step * 1e-3) / 1e9
-    value_e2e = world * STEP_BYTES / (ms_e2e / args.steps * 1e-3) / 1e9
+    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+    value_e2e = world * step_bytes / (ms_e2e / args.steps * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
-    per_launch_us = ms_step * 1e3 / LAUNCHES_PER_STEP
-    achieved = (STEP_BYTES / LAUNCHES_PER_STEP) / (per_launch_us * 1e-6) / 1e9
+    per_launch_us = ms_step * 1e3 / launches
+    achieved = (step_bytes / launches) / (per_launch_us * 1e-6) / 1e9
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init INT8 weights N(0,0.02) quantised on device; bf16 x ~ N(0,1))",
-        "config": {"workload": WORKLOAD, "group_size": GROUP, "rows": M_FRAMES,
-                   "bytes_per_step_per_gpu": STEP_BYTES, "launches_per_step": LAUNCHES_PER_STEP,
-                   "l2": "inputs larger than L2 (640 MB of distinct weights per step)",
+        "config": {"workload": workload, "group_size": GROUP, "rows": M_FRAMES,
+                   "bytes_per_step_per_gpu": step_bytes, "launches_per_step": launches,
+                   "l2": "inputs larger than L2 (distinct weights per step exceed 126 MB)",
                    "parallelism": f"dp{world} (replicated weights, independent streams)",
                    "graph": "one CUDA graph per step, programmatic dependent launch edges"},
         "e2e": {"value": round(value_e2e, 2), "unit": UNIT,
-                "h2d_bytes_per_step": M_FRAMES * 1024 * 2,
-                "d2h_bytes_per_step": M_FRAMES * 1024 * 2,
+                "h2d_bytes_per_step": host_in.numel() * 2,
+                "d2h_bytes_per_step": host_out.numel() * 2,
                 "path": "C-ABI cq_linear_forward_ex calls captured in a CUDA graph with the "
                         "pinned-host input copy and output read inside the timed region"},
-        "gpu_launches": LAUNCHES_PER_STEP * args.steps,
+        "gpu_launches": launches * args.steps,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
                      "traffic": None, "kernel": "qgemv_kernel (K1)",
@@ -276,7 +319,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         "clocks": clock_info,
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(target_s=args.cpu_seconds)
+        line["cpu_baseline"] = cpu_baseline(target_s=args.cpu_seconds, workload=args.workload)
     return line
 
 
@@ -284,33 +327,37 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 
 
 class OracleBlocks:
-    """Host copies of a few blocks' packed weights for the CPU restatement."""
+    """Host copies of a few blocks' packed weights for the CPU restatement
+    (workload "linear": each block is the single 4096x1024 linear)."""
 
-    def __init__(self, n_blocks: int, seed: int = 1):
+    def __init__(self, n_blocks: int, seed: int = 1, workload: str = "block"):
         import numpy as np
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle
         self.oracle = oracle
         rng = np.random.default_rng(seed)
+        self.spec = BLOCK if workload == "block" else [
+            ("linear", SingleLinear.N, SingleLinear.K, M_FRAMES, "none", "x0")]
+        self.bytes = sum(linear_bytes(n, k, m) for _, n, k, m, _, _ in self.spec)
         self.blocks = []
         for _ in range(n_blocks):
             blk = []
-            for _, n, k, m, act, _ in BLOCK:
+            for _, n, k, m, act, _ in self.spec:
                 q = rng.integers(0, 256, size=(n, k), dtype=np.uint8).view(np.uint32)
                 s = oracle.to_t((rng.random((n, k // GROUP)) * 1e-3).astype(np.float32), "bf16")
                 b = oracle.to_t((rng.random((n, k // GROUP)) * -0.1).astype(np.float32), "bf16")
                 blk.append((q, s, b))
             self.blocks.append(blk)
         self.x = {name: oracle.to_t(rng.standard_normal((m, k)).astype(np.float32), "bf16")
-                  for name, n, k, m, _, _ in BLOCK}
+                  for name, n, k, m, _, _ in self.spec}
 
     def run_block(self, i: int) -> None:
-        for (q, s, b), (name, n, k, m, act, _) in zip(self.blocks[i % len(self.blocks)], BLOCK):
+        for (q, s, b), (name, n, k, m, act, _) in zip(self.blocks[i % len(self.blocks)], self.spec):
             self.oracle.qmatmul(self.x[name], q, s, b, GROUP, "bf16", None, act)
 
 
-def cpu_baseline(target_s: float = 12.0) -> dict:
-    ob = OracleBlocks(4)
+def cpu_baseline(target_s: float = 12.0, workload: str = "block") -> dict:
+    ob = OracleBlocks(4 if workload == "block" else 40, workload=workload)
     ob.run_block(0)  # warm
     t0 = time.perf_counter()
     n = 0
@@ -320,30 +367,35 @@ def cpu_baseline(target_s: float = 12.0) -> dict:
         if time.perf_counter() - t0 >= target_s and n >= 2:
             break
     dt = time.perf_counter() - t0
-    return {"value": round(n * BLOCK_BYTES / dt / 1e9, 3), "unit": UNIT,
+    what = ("blocks x 9 linears (M=14, pos M=139) rotating over 4 weight sets"
+            if workload == "block" else "4096x1024 linears (M=14) rotating over 40 weight sets")
+    return {"value": round(n * ob.bytes / dt / 1e9, 3), "unit": UNIT,
             "cores": ob.oracle.max_threads(), "kind": "port",
-            "sample": f"{n} blocks x 9 linears (M=14, pos M=139) rotating over 4 weight sets, "
-                      f"{dt:.1f} s, OpenMP C restatement of quantized_matmul (oracle/)"}
+            "sample": f"{n} {what}, {dt:.1f} s, OpenMP C restatement of quantized_matmul "
+                      f"(oracle/)"}
 
 
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
-    ob = OracleBlocks(4)
+    ob = OracleBlocks(4 if args.workload == "block" else 40, workload=args.workload)
+    reps = 1 if args.workload == "block" else SingleLinear.COPIES
     for i in range(args.warmup):
         ob.run_block(i)
     t0 = time.perf_counter()
-    for i in range(args.steps):
+    for i in range(args.steps * reps):
         ob.run_block(i)
     dt = time.perf_counter() - t0
-    value = args.steps * BLOCK_BYTES / dt / 1e9
+    value = args.steps * reps * ob.bytes / dt / 1e9
     return {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD, "group_size": GROUP, "rows": M_FRAMES,
-                   "step": "one block's 9 linears (1/24 of the GPU arm's step; same metric)"},
+        "config": {"workload": WORKLOAD if args.workload == "block" else LINEAR_WORKLOAD,
+                   "group_size": GROUP, "rows": M_FRAMES,
+                   "step": ("one block's 9 linears (1/24 of the GPU arm's step; same metric)"
+                            if args.workload == "block" else "40 linears, as the GPU arm")},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": ob.oracle.max_threads(),
                          "kind": "port",
                          "sample": "OpenMP C restatement of MLX quantized_matmul (oracle/); "
@@ -359,6 +411,9 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["block", "linear"], default="block",
+                    help="block: the 24-block M=14 linear chain (default); linear: one "
+                         "4096x1024 linear, independent back-to-back launches")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()

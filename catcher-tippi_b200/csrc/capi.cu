@@ -137,6 +137,13 @@ cq_status cq_linear_forward_f32(cq_linear* layer, const float* input, size_t inp
   });
 }
 
+cq_status cq_linear_reserve(cq_linear* layer, int32_t max_rows) {
+  return guarded([&] {
+    need_handle(layer, "layer");
+    layer->impl->reserve(max_rows);
+  });
+}
+
 int32_t cq_linear_input_dims(const cq_linear* layer) {
   return layer ? layer->impl->input_dims() : -1;
 }

@@ -1,0 +1,392 @@
+// K2: affine INT8 dequant-GEMM for many rows (concurrent streams stacked to
+// M >= 128), on the 5th-generation tensor cores.
+//
+//   y[m, n] = sum_k x[m, k] * (s[n, k/g] * q[n, k] + b[n, k/g])      (T out)
+//
+// the operation behind QuantizedLinear::forward_array
+// (crates/nemotron-mlx/src/model/layers.rs:298-310) at batched row counts.
+//
+// Per CTA: one 128 x BN output tile over the full K, 6 warps:
+//   warp 0   TMA producer: x tile [128 x 64] f16 (128B swizzle) and the packed
+//            weight tile [BN x 64] u8 (64B swizzle) into a 4-stage ring
+//   warp 1   tcgen05.mma issuer (one elected lane), kind::f16, M=128, N=BN,
+//            K=16 per instruction, fp32 accumulator in tensor memory; owns the
+//            tensor-memory allocation
+//   warps 2-5 dequantisers: one weight row per thread, w = s * q + b in f16
+//            (the byte becomes the exact f16 1024 + q by one PRMT, 1024 is
+//            subtracted exactly, then one fused multiply-add), written into
+//            the 128B-swizzled K-major layout the MMA reads; after the last
+//            k-tile the same warps run the epilogue (tcgen05.ld, row scale,
+//            rounding to T, output bias, activation, stores).
+// Both MMA operands are f16 (A and B of one MMA share the type): bf16
+// activations are converted beforehand by qgemm_prepass (per-row power-of-two
+// scale, undone in the epilogue), and the weights are dequantised to f16, whose
+// 11-bit significand holds s*q + b more precisely than bf16 would.  Layers
+// whose scales/biases leave the f16 normal range never reach this kernel.
+// No multicast: every TMA load targets this CTA's own shared memory.
+#include "common.cuh"
+#include "qgemm.hpp"
+
+#include <algorithm>
+
+namespace cq {
+
+namespace {
+
+constexpr int kBM = 128;  // MMA M (tokens)
+constexpr int kBK = 64;   // k per stage: one 128-byte swizzle atom of f16
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kDequantWarp0 = 2;
+
+template <int BN>
+struct GemmSmem {
+  static constexpr int kA = kBM * kBK * 2;  // 16 KB
+  static constexpr int kB = BN * kBK * 2;   // dequantised f16 weights
+  static constexpr int kQ = BN * kBK;       // packed u8 weights
+  static constexpr int kStage = kA + kB + kQ;
+  static constexpr int kBarOff = kStages * kStage;
+  // full[S], bready[S], empty[S], accum; tmem address word
+  static constexpr int kBytes = kBarOff + (3 * kStages + 1) * 8 + 16;
+};
+
+// --------------------------------------------------------------- tcgen05
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          smem_u32(bar))
+      : "memory");
+}
+// 32 lanes x 32 columns of 32-bit: thread i of the warp gets lane (quarter*32+i)
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: 8-row atoms of
+// 128-byte rows, atoms 1024 bytes apart (SBO), LBO unused (1), version 1.
+__device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+         (static_cast<uint64_t>(1024 >> 4) << 32) | (static_cast<uint64_t>(1) << 46) |
+         (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor: f32 accumulate, f16 A and B, both K-major, M=128, N=BN.
+template <int BN>
+__host__ __device__ constexpr uint32_t idesc_f16_f32() {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+         (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+template <int DT, int G, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    qgemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap qmap,
+                 const GemmArgs a) {
+  using L = GemmSmem<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzled tiles
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* bready = full + kStages;
+  uint64_t* empty = bready + kStages;
+  uint64_t* accum = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+  const int KT = (a.K + kBK - 1) / kBK;
+  const int groups_per_row = a.K / G;
+
+  if (threadIdx.x == 0) {
+    prefetch_tensormap(&amap);
+    prefetch_tensormap(&qmap);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&bready[s], 4);  // one arrival per dequant warp
+      mbar_init(&empty[s], 1);   // tcgen05.commit
+    }
+    mbar_init(accum, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_d = *tmem_slot;
+
+  pdl_launch_dependents();
+  pdl_wait();
+
+  bool ok = true;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t wpol = l2_policy_evict_normal();
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % kStages;
+        const uint32_t ph = (kt / kStages) & 1;
+        ok = mbar_wait_bounded(&empty[s], ph ^ 1, a.status) && ok;
+        uint8_t* st = smem + s * L::kStage;
+        mbar_arrive_expect_tx(&full[s], L::kA + L::kQ);
+        tma_load_2d(st, &amap, kt * kBK, m0, &full[s], wpol);
+        tma_load_2d(st + L::kA + L::kB, &qmap, kt * kBK, n0, &full[s], wpol);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32<BN>();
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % kStages;
+        const uint32_t ph = (kt / kStages) & 1;
+        ok = mbar_wait_bounded(&full[s], ph, a.status) && ok;
+        ok = mbar_wait_bounded(&bready[s], ph, a.status) && ok;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
+        const uint32_t b_addr = a_addr + L::kA;
+#pragma unroll
+        for (int ks = 0; ks < kBK / 16; ++ks) {
+          // advancing K by 16 f16 = 32 bytes inside the swizzle atom
+          tc_mma_f16(tmem_d, sw128_kmajor_desc(a_addr + 32 * ks), sw128_kmajor_desc(b_addr + 32 * ks),
+                     idesc, (kt | ks) != 0);
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(accum);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant
+    static_assert(BN == 128, "one weight row per dequant thread");
+    const int row = threadIdx.x - kDequantWarp0 * 32;  // 0..127
+    const int n = n0 + row;
+    const bool row_ok = n < a.N;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % kStages;
+      const uint32_t ph = (kt / kStages) & 1;
+      // group scale/bias of this row for the k-tile (read before the wait)
+      const int k0 = kt * kBK;
+      __half2 s2[2], b2[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int kk = k0 + h * 32;
+        float sv = 0.f, bv = 0.f;
+        if (row_ok && kk < a.K) {
+          const size_t gi = static_cast<size_t>(n) * groups_per_row + kk / G;
+          sv = ld_t<DT>(a.scales, gi);
+          bv = ld_t<DT>(a.biases, gi);
+        }
+        s2[h] = __float2half2_rn(sv);
+        b2[h] = __float2half2_rn(bv);
+      }
+      ok = mbar_wait_bounded(&full[s], ph, a.status) && ok;
+      uint8_t* st = smem + s * L::kStage;
+      const uint8_t* qrow = st + L::kA + L::kB + row * 64;  // 64B-swizzled u8 row
+      uint8_t* brow = st + L::kA + row * 128;               // 128B-swizzled f16 row
+      const int sw64 = (row >> 1) & 3, sw128 = row & 7;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        // logical 16-byte chunk c of the packed row = k0 + 16c .. k0 + 16c + 15
+        const uint4 qv = *reinterpret_cast<const uint4*>(qrow + ((c ^ sw64) << 4));
+        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+        const int h = (G == 32) ? (c >> 1) : 0;
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t lo = __byte_perm(qw[i], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
+          uint32_t hi = __byte_perm(qw[i], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
+          const __half2 k1024 = __float2half2_rn(1024.0f);
+          __half2 ql = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
+          __half2 qh = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
+          __half2 wl = __hfma2(s2[h], ql, b2[h]);
+          __half2 wh = __hfma2(s2[h], qh, b2[h]);
+          out[2 * i] = *reinterpret_cast<uint32_t*>(&wl);
+          out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&wh);
+        }
+        // 16 f16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row
+        *reinterpret_cast<uint4*>(brow + (((2 * c) ^ sw128) << 4)) =
+            make_uint4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ sw128) << 4)) =
+            make_uint4(out[4], out[5], out[6], out[7]);
+      }
+      fence_proxy_async_shared();  // generic-proxy writes -> tensor-core reads
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bready[s]);
+    }
+
+    // ------------------------------------------------------------ epilogue
+    ok = mbar_wait_bounded(accum, 0, a.status) && ok;
+    tc_fence_after();
+    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    const int m = m0 + quarter * 32 + lane;
+    const float rs = (a.row_scale != nullptr && m < a.M) ? a.row_scale[m] : 1.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
+      tmem_wait_ld();
+      if (m < a.M) {
+        for (int j = 0; j < 32; ++j) {
+          const int nn = n0 + c0 + j;
+          if (nn < a.N) {
+            const float v = __uint_as_float(r[j]) * rs;
+            float o = round_t<DT>(v);
+            if (a.bias != nullptr) o = round_t<DT>(o + ld_t<DT>(a.bias, nn));
+            if (a.act == kActSilu) o = round_t<DT>(o / (1.0f + expf(-o)));
+            else if (a.act == kActRelu) o = o > 0.f ? o : 0.f;
+            st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + nn, o);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_d, BN);
+  }
+  (void)ok;
+}
+
+// bf16 -> f16 activations with a per-row power-of-two scale: the row maximum
+// lands in [2^14, 2^15); row_scale[m] = 2^e undoes it in the epilogue.
+__global__ void __launch_bounds__(256)
+    qgemm_prepass_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int K,
+                         __half* __restrict__ xo, int ldo, float* __restrict__ row_scale) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.x;
+  if (m >= M) return;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(m) * ldx;
+  float amax = 0.f;
+  for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(__bfloat162float(xr[k])));
+  __shared__ float red[8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = 0.f;
+  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
+  const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
+  int sh = e == 0 ? 0 : 141 - e;
+  sh = max(-126, min(126, sh));
+  const float scale = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
+  if (threadIdx.x == 0) row_scale[m] = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+  __half* orow = xo + static_cast<size_t>(m) * ldo;
+  for (int k = threadIdx.x; k < K; k += blockDim.x)
+    orow[k] = __float2half_rn(__bfloat162float(xr[k]) * scale);
+}
+
+template <int DT, int G, int BN>
+cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, const GemmArgs& a,
+                              cudaStream_t stream, bool pdl) {
+  using L = GemmSmem<BN>;
+  auto kern = qgemm_kernel<DT, G, BN>;
+  static bool configured = false;
+  const int smem = L::kBytes + 1024;  // + alignment slack
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.N + BN - 1) / BN, (a.M + kBM - 1) / kBM, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  int na = 0;
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    na = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, amap, qmap, a);
+}
+
+template <int DT>
+cudaError_t launch_gemm_g(int group, const CUtensorMap& amap, const CUtensorMap& qmap,
+                          const GemmArgs& a, cudaStream_t stream, bool pdl) {
+  switch (group) {
+    case 32: return launch_gemm_typed<DT, 32, kGemmBN>(amap, qmap, a, stream, pdl);
+    case 64: return launch_gemm_typed<DT, 64, kGemmBN>(amap, qmap, a, stream, pdl);
+    case 128: return launch_gemm_typed<DT, 128, kGemmBN>(amap, qmap, a, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_gemm(int dtype, int group, const CUtensorMap& amap, const CUtensorMap& qmap,
+                        const GemmArgs& a, cudaStream_t stream, bool pdl) {
+  if (dtype == kF16) return launch_gemm_g<kF16>(group, amap, qmap, a, stream, pdl);
+  if (dtype == kBF16) return launch_gemm_g<kBF16>(group, amap, qmap, a, stream, pdl);
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, int ldo,
+                                float* row_scale, cudaStream_t stream, bool pdl) {
+  if (M == 0) return cudaSuccess;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, qgemm_prepass_kernel, reinterpret_cast<const __nv_bfloat16*>(x),
+                            ldx, M, K, reinterpret_cast<__half*>(xo), ldo, row_scale);
+}
+
+size_t gemm_smem_bytes() { return GemmSmem<kGemmBN>::kBytes + 1024; }
+
+}  // namespace cq

@@ -4,6 +4,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <sstream>
@@ -17,6 +18,14 @@ namespace {
 
 std::string fmt_shape_error(const char* prefix, const std::string& msg) {
   return std::string(prefix) + msg;
+}
+
+bool gemm_allowed() {
+  static const bool on = [] {
+    const char* e = std::getenv("CQ_GEMM");
+    return e == nullptr || std::strcmp(e, "0") != 0;
+  }();
+  return on;
 }
 
 bool pdl_enabled() {
@@ -97,7 +106,8 @@ DeviceContext& device_context(int device) {
   return *contexts[device];
 }
 
-CUtensorMap make_weight_map(const void* q, int N, int K, int box_rows) {
+CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
+                        int box_rows, int box_cols, CUtensorMapSwizzle swizzle) {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -109,13 +119,15 @@ CUtensorMap make_weight_map(const void* q, int N, int K, int box_rows) {
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
   CUtensorMap map{};
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(N)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};  // bytes between rows
-  const cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};  // bytes per row
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(q), dims, strides,
-                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUtensorMapDataType dt =
+      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = encode(&map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw Error(CQ_RUNTIME_ERROR, "cuTensorMapEncodeTiled failed with " + std::to_string(r));
   return map;
@@ -155,7 +167,87 @@ void QuantizedLinear::finalize() {
                   std::to_string(kMaxInputDims));
   DeviceContext& ctx = device_context(device_);
   plan_ = cq::plan_gemv(N_, K_, ctx.num_sms);
-  wmap_ = make_weight_map(q_, N_, K_, 16 * plan_.rt);
+  wmap_ = make_map_2d(q_, 1, N_, K_, K_, 16 * plan_.rt, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
+  qmap_gemm_ = make_map_2d(q_, 1, N_, K_, K_, cq::kGemmBN, 64, CU_TENSOR_MAP_SWIZZLE_64B);
+  gemm_ok_ = check_f16_range();
+}
+
+// K2 dequantises to f16.  f16 layers are exact by construction; a bf16 layer
+// qualifies when every nonzero scale is an f16 normal number and every
+// dequantised weight (|s| * 255 + |b|) stays below the f16 maximum.
+bool QuantizedLinear::check_f16_range() const {
+  if (dtype_ == CQ_F16) return true;
+  if (dtype_ != CQ_BF16) return false;
+  const size_t groups = static_cast<size_t>(N_) * (K_ / group_);
+  std::vector<uint16_t> s(groups), b(groups);
+  check_cuda(cudaMemcpy(s.data(), scales_, groups * 2, cudaMemcpyDeviceToHost), "read scales");
+  check_cuda(cudaMemcpy(b.data(), biases_, groups * 2, cudaMemcpyDeviceToHost), "read biases");
+  auto widen = [](uint16_t v) {
+    uint32_t u = static_cast<uint32_t>(v) << 16;
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+  };
+  for (size_t i = 0; i < groups; ++i) {
+    const float sv = std::fabs(widen(s[i])), bv = std::fabs(widen(b[i]));
+    if (!(sv == 0.0f || (sv >= 6.103515625e-05f && sv <= 65504.0f))) return false;
+    if (!(sv * 255.0f + bv <= 65504.0f)) return false;  // also rejects NaN/inf
+  }
+  return true;
+}
+
+void QuantizedLinear::reserve(int max_rows) {
+  if (max_rows < 0) throw_invalid("reserve: negative row count");
+  if (dtype_ != CQ_BF16 || !gemm_ok_ || max_rows < cq::kGemmMinRows) return;
+  std::lock_guard<std::mutex> lock(ws_mu_);
+  if (max_rows <= ws_rows_) return;
+  DeviceGuard guard(device_);
+  const size_t xbytes = align_up(static_cast<size_t>(max_rows) * K_ * 2, 256);
+  const size_t need = xbytes + static_cast<size_t>(max_rows) * sizeof(float);
+  void* p = nullptr;
+  check_cuda(cudaMalloc(&p, need), "cudaMalloc(gemm workspace)");
+  cudaFree(ws_);
+  ws_ = p;
+  ws_bytes_ = need;
+  ws_rows_ = max_rows;
+  amap_ptr_ = nullptr;  // the cached map may point into the old workspace
+}
+
+void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, int ldy, int act,
+                                   cudaStream_t stream) {
+  DeviceContext& ctx = device_context(device_);
+  const void* a_ptr = x;
+  int a_ld = ldx;
+  const float* row_scale = nullptr;
+  if (dtype_ == CQ_BF16) {
+    reserve(rows);
+    const size_t xbytes = align_up(static_cast<size_t>(ws_rows_) * K_ * 2, 256);
+    float* rs = reinterpret_cast<float*>(static_cast<char*>(ws_) + xbytes);
+    check_cuda(cq::launch_gemm_prepass(x, ldx, rows, K_, ws_, K_, rs, stream, pdl_enabled()),
+               "qgemm prepass");
+    a_ptr = ws_;
+    a_ld = K_;
+    row_scale = rs;
+  }
+  if (a_ptr != amap_ptr_ || a_ld != amap_ld_ || rows != amap_rows_) {
+    amap_ = make_map_2d(a_ptr, 2, rows, K_, a_ld, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_ptr_ = a_ptr;
+    amap_ld_ = a_ld;
+    amap_rows_ = rows;
+  }
+  cq::GemmArgs g{};
+  g.row_scale = row_scale;
+  g.scales = scales_;
+  g.biases = biases_;
+  g.bias = bias_;
+  g.y = y;
+  g.status = ctx.status;
+  g.M = rows;
+  g.N = N_;
+  g.K = K_;
+  g.ldy = ldy;
+  g.act = act;
+  check_cuda(cq::launch_gemm(dtype_, group_, amap_, qmap_gemm_, g, stream, pdl_enabled()), "qgemm");
 }
 
 std::unique_ptr<QuantizedLinear> QuantizedLinear::from_packed(const uint32_t* qweight,
@@ -307,6 +399,10 @@ void QuantizedLinear::forward_array(const void* x, int ldx, int rows, void* y, i
   }
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0)
     throw_invalid("input rows must be 16-byte aligned (x % 16 == 0 and ldx % 8 == 0)");
+  if (rows >= cq::kGemmMinRows && gemm_ok_ && gemm_allowed()) {
+    const_cast<QuantizedLinear*>(this)->forward_gemm(x, ldx, rows, y, ldy, act, stream);
+    return;
+  }
   cq::GemvArgs a{};
   a.x = x;
   a.scales = scales_;

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "cqlinear.h"
+#include "qgemm.hpp"
 #include "qgemv.hpp"
 
 namespace nemotron_cuda {
@@ -53,8 +54,10 @@ class DeviceGuard {
   int prev_ = -1;
 };
 
-// Builds the 2-D u8 tensor map the K1 kernel streams weights through.
-CUtensorMap make_weight_map(const void* q, int N, int K, int box_rows);
+// 2-D tiled tensor map over a row-major [rows, cols] matrix of 1- or 2-byte
+// elements (row stride in elements), box [box_rows, box_cols].
+CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
+                        int box_rows, int box_cols, CUtensorMapSwizzle swizzle);
 
 class QuantizedLinear {
  public:
@@ -80,6 +83,11 @@ class QuantizedLinear {
   // Host f32 in / out, synchronous (forward_f32).
   void forward_f32(const float* input, size_t input_len, int rows, float* output,
                    size_t output_len);
+  // Allocates the batched-path workspace for up to `max_rows` rows now, so
+  // later calls of that size allocate nothing (e.g. before graph capture).
+  void reserve(int max_rows);
+  // True when batched calls run on the tensor-core GEMM (K2).
+  bool gemm_enabled() const { return gemm_ok_; }
 
   int input_dims() const { return K_; }
   int output_dims() const { return N_; }
@@ -105,6 +113,21 @@ class QuantizedLinear {
   void* bias_ = nullptr;
   cq::GemvPlan plan_{};
   CUtensorMap wmap_{};
+  // K2: packed weights with a 64-byte swizzle; scales/biases fit f16
+  CUtensorMap qmap_gemm_{};
+  bool gemm_ok_ = false;
+  // K2 workspace (bf16 layers): f16 activations [rows, K] + row scales [rows]
+  std::mutex ws_mu_;
+  void* ws_ = nullptr;
+  size_t ws_bytes_ = 0;
+  int ws_rows_ = 0;
+  // cached activation tensor map
+  CUtensorMap amap_{};
+  const void* amap_ptr_ = nullptr;
+  int amap_ld_ = 0, amap_rows_ = 0;
+  void forward_gemm(const void* x, int ldx, int rows, void* y, int ldy, int act,
+                    cudaStream_t stream);
+  bool check_f16_range() const;
 
   // Scratch of the synchronous host-f32 path, grown on demand.
   std::mutex host_mu_;

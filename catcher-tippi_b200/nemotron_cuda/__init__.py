@@ -51,6 +51,7 @@ def lib() -> ctypes.CDLL:
         "cq_linear_forward": ([vp, vp, i32, vp, vp], i32),
         "cq_linear_forward_ex": ([vp, vp, i32, i32, vp, i32, i32, vp], i32),
         "cq_linear_forward_f32": ([vp, vp, sz, i32, vp, sz], i32),
+        "cq_linear_reserve": ([vp, i32], i32),
         "cq_linear_input_dims": ([vp], i32),
         "cq_linear_output_dims": ([vp], i32),
         "cq_linear_group_size": ([vp], i32),
@@ -196,6 +197,10 @@ class QuantizedLinear:
         _check(lib().cq_linear_forward_ex(self._h, _ptr(x), x.stride(0), m, _ptr(y), y.stride(0),
                                           ACTS[act], _stream_ptr(stream)))
         return y
+
+    def reserve(self, max_rows: int) -> None:
+        """Allocate the batched-path workspace now (before graph capture)."""
+        _check(lib().cq_linear_reserve(self._h, max_rows))
 
     def forward_raw(self, x_ptr: int, ldx: int, rows: int, y_ptr: int, ldy: int,
                     act: str = "none", stream: int = 0) -> None:

@@ -121,6 +121,15 @@ cq_status cq_linear_forward_ex(cq_linear *layer, const void *x, int32_t ldx, int
 cq_status cq_linear_forward_f32(cq_linear *layer, const float *input, size_t input_len,
                                 int32_t rows, float *output, size_t output_len);
 
+/*
+ * Sizes the layer's workspace for calls of up to max_rows rows.  Calls with
+ * rows >= 128 run on the tensor-core GEMM; for bf16 layers that path stages
+ * the activations as f16 in a per-layer workspace that is otherwise
+ * allocated on the first such call.  Reserve before capturing calls into a
+ * CUDA graph.  No reference counterpart (MLX allocates inside its graph).
+ */
+cq_status cq_linear_reserve(cq_linear *layer, int32_t max_rows);
+
 /* Dimensions and type of a layer (layers.rs:312-318). */
 int32_t cq_linear_input_dims(const cq_linear *layer);
 int32_t cq_linear_output_dims(const cq_linear *layer);
