@@ -35,19 +35,26 @@ namespace {
 
 constexpr int kBM = 128;  // MMA M (tokens)
 constexpr int kBK = 64;   // k per stage: one 128-byte swizzle atom of f16
-constexpr int kStages = 4;
-constexpr int kThreads = 192;
+constexpr int kStages = 4;  // TMA ring depth
+constexpr int kBBufs = 2;   // dequantised weight tiles (double buffer)
+constexpr int kDequantWarps = 8;
+constexpr int kThreads = (2 + kDequantWarps) * 32;
 constexpr int kDequantWarp0 = 2;
 
-template <int BN>
+template <int BN, int SUBG>
 struct GemmSmem {
-  static constexpr int kA = kBM * kBK * 2;  // 16 KB
-  static constexpr int kB = BN * kBK * 2;   // dequantised f16 weights
-  static constexpr int kQ = BN * kBK;       // packed u8 weights
-  static constexpr int kStage = kA + kB + kQ;
-  static constexpr int kBarOff = kStages * kStage;
-  // full[S], bready[S], empty[S], accum; tmem address word
-  static constexpr int kBytes = kBarOff + (3 * kStages + 1) * 8 + 16;
+  static constexpr int kA = kBM * kBK * 2;   // x tile, f16, 128B swizzle (16 KB)
+  static constexpr int kQ = BN * kBK;        // packed u8 weights, 64B swizzle
+  static constexpr int kSB = BN * SUBG * 4;  // f16 (scale, bias) per row and group
+  static constexpr int kStage = kA + kQ + 2048;  // TMA stage, 1024-aligned
+  static constexpr int kB = BN * kBK * 2;    // dequantised f16 weights, 128B swizzle
+  static constexpr int kBOff = kStages * kStage;
+  static constexpr int kBiasOff = kBOff + kBBufs * kB;  // [BN] output bias (fp32)
+  static constexpr int kBarOff = kBiasOff + BN * 4;
+  // full[S], empty[S], bfull[2], bempty[2], accum; tmem address word
+  static constexpr int kBytes = kBarOff + (2 * kStages + 2 * kBBufs + 1) * 8 + 16;
+  static_assert(kSB <= 2048, "scale/bias slot");
+  static_assert(kStage % 1024 == 0 && kB % 1024 == 0, "swizzled tiles stay 1024-aligned");
 };
 
 // --------------------------------------------------------------- tcgen05
@@ -122,29 +129,36 @@ template <int DT, int G, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap qmap,
                  const GemmArgs a) {
-  using L = GemmSmem<BN>;
+  constexpr int SUBG = (G == 32) ? 2 : 1;
+  constexpr int kRowsPerThread = BN / (kDequantWarps * 32);
+  static_assert(BN % (kDequantWarps * 32) == 0, "rows per dequant thread");
+  using L = GemmSmem<BN, SUBG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* bready = full + kStages;
-  uint64_t* empty = bready + kStages;
-  uint64_t* accum = empty + kStages;
+  uint64_t* empty = full + kStages;
+  uint64_t* bfull = empty + kStages;
+  uint64_t* bempty = bfull + kBBufs;
+  uint64_t* accum = bempty + kBBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  float* bias_s = reinterpret_cast<float*>(smem + L::kBiasOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
   const int KT = (a.K + kBK - 1) / kBK;
-  const int groups_per_row = a.K / G;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&amap);
     prefetch_tensormap(&qmap);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bready[s], 4);  // one arrival per dequant warp
-      mbar_init(&empty[s], 1);   // tcgen05.commit
+      mbar_init(&empty[s], kDequantWarps + 1);  // dequant warps (q, scales) + MMA commit (x)
+    }
+    for (int b = 0; b < kBBufs; ++b) {
+      mbar_init(&bfull[b], kDequantWarps);  // one arrival per dequant warp
+      mbar_init(&bempty[b], 1);  // tcgen05.commit
     }
     mbar_init(accum, 1);
     fence_mbar_init();
@@ -165,15 +179,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t wpol = l2_policy_evict_normal();
+      const uint64_t pol = l2_policy_evict_normal();
       for (int kt = 0; kt < KT; ++kt) {
         const int s = kt % kStages;
         const uint32_t ph = (kt / kStages) & 1;
         ok = mbar_wait_bounded(&empty[s], ph ^ 1, a.status) && ok;
         uint8_t* st = smem + s * L::kStage;
-        mbar_arrive_expect_tx(&full[s], L::kA + L::kQ);
-        tma_load_2d(st, &amap, kt * kBK, m0, &full[s], wpol);
-        tma_load_2d(st + L::kA + L::kB, &qmap, kt * kBK, n0, &full[s], wpol);
+        mbar_arrive_expect_tx(&full[s], L::kA + L::kQ + L::kSB);
+        tma_load_2d(st, &amap, kt * kBK, m0, &full[s], pol);
+        tma_load_2d(st + L::kA, &qmap, kt * kBK, n0, &full[s], pol);
+        // the k-tile's (scale, bias) pairs of the BN rows: one contiguous block
+        bulk_copy_g2s(st + L::kA + L::kQ,
+                      reinterpret_cast<const uint8_t*>(a.sb_tiles) +
+                          (static_cast<size_t>(blockIdx.x) * KT + kt) * L::kSB,
+                      L::kSB, &full[s]);
       }
     }
   } else if (warp == 1) {
@@ -181,104 +200,140 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32<BN>();
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % kStages;
-        const uint32_t ph = (kt / kStages) & 1;
-        ok = mbar_wait_bounded(&full[s], ph, a.status) && ok;
-        ok = mbar_wait_bounded(&bready[s], ph, a.status) && ok;
+        const int s = kt % kStages, b = kt % kBBufs;
+        ok = mbar_wait_bounded(&full[s], (kt / kStages) & 1, a.status) && ok;
+        ok = mbar_wait_bounded(&bfull[b], (kt / kBBufs) & 1, a.status) && ok;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * L::kStage);
-        const uint32_t b_addr = a_addr + L::kA;
+        const uint32_t b_addr = smem_u32(smem + L::kBOff + b * L::kB);
 #pragma unroll
         for (int ks = 0; ks < kBK / 16; ++ks) {
           // advancing K by 16 f16 = 32 bytes inside the swizzle atom
           tc_mma_f16(tmem_d, sw128_kmajor_desc(a_addr + 32 * ks), sw128_kmajor_desc(b_addr + 32 * ks),
                      idesc, (kt | ks) != 0);
         }
-        tc_commit(&empty[s]);
+        tc_commit(&empty[s]);   // x tile consumed
+        tc_commit(&bempty[b]);  // dequantised tile consumed
       }
       tc_commit(accum);
     }
   } else {
     // ------------------------------------------------------------ dequant
-    static_assert(BN == 128, "one weight row per dequant thread");
-    const int row = threadIdx.x - kDequantWarp0 * 32;  // 0..127
-    const int n = n0 + row;
-    const bool row_ok = n < a.N;
+    constexpr int kDT = kDequantWarps * 32;
+    const int t = threadIdx.x - kDequantWarp0 * 32;  // rows t, t + kDT, ...
+#pragma unroll
+    for (int rr = 0; rr < kRowsPerThread; ++rr) {
+      const int n = n0 + t + kDT * rr;
+      bias_s[t + kDT * rr] = (a.bias != nullptr && n < a.N) ? ld_t<DT>(a.bias, n) : 0.0f;
+    }
+    const __half2 k1024 = __float2half2_rn(1024.0f);
     for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % kStages;
-      const uint32_t ph = (kt / kStages) & 1;
-      // group scale/bias of this row for the k-tile (read before the wait)
-      const int k0 = kt * kBK;
-      __half2 s2[2], b2[2];
+      const int s = kt % kStages, b = kt % kBBufs;
+      ok = mbar_wait_bounded(&full[s], (kt / kStages) & 1, a.status) && ok;
+      ok = mbar_wait_bounded(&bempty[b], ((kt / kBBufs) & 1) ^ 1, a.status) && ok;
+      const uint8_t* st = smem + s * L::kStage;
+      const __half2* sbp = reinterpret_cast<const __half2*>(st + L::kA + L::kQ);
+      uint8_t* bt = smem + L::kBOff + b * L::kB;
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int kk = k0 + h * 32;
-        float sv = 0.f, bv = 0.f;
-        if (row_ok && kk < a.K) {
-          const size_t gi = static_cast<size_t>(n) * groups_per_row + kk / G;
-          sv = ld_t<DT>(a.scales, gi);
-          bv = ld_t<DT>(a.biases, gi);
+      for (int rr = 0; rr < kRowsPerThread; ++rr) {
+        const int row = t + kDT * rr;
+        // this row's (scale, bias) for the k-tile's group(s), f16
+        __half2 s2[2], b2[2];
+#pragma unroll
+        for (int h = 0; h < SUBG; ++h) {
+          const __half2 p = sbp[row * SUBG + h];
+          s2[h] = __low2half2(p);
+          b2[h] = __high2half2(p);
         }
-        s2[h] = __float2half2_rn(sv);
-        b2[h] = __float2half2_rn(bv);
-      }
-      ok = mbar_wait_bounded(&full[s], ph, a.status) && ok;
-      uint8_t* st = smem + s * L::kStage;
-      const uint8_t* qrow = st + L::kA + L::kB + row * 64;  // 64B-swizzled u8 row
-      uint8_t* brow = st + L::kA + row * 128;               // 128B-swizzled f16 row
-      const int sw64 = (row >> 1) & 3, sw128 = row & 7;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        // logical 16-byte chunk c of the packed row = k0 + 16c .. k0 + 16c + 15
-        const uint4 qv = *reinterpret_cast<const uint4*>(qrow + ((c ^ sw64) << 4));
-        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-        const int h = (G == 32) ? (c >> 1) : 0;
-        uint32_t out[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t lo = __byte_perm(qw[i], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
-          uint32_t hi = __byte_perm(qw[i], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
-          const __half2 k1024 = __float2half2_rn(1024.0f);
-          __half2 ql = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
-          __half2 qh = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
-          __half2 wl = __hfma2(s2[h], ql, b2[h]);
-          __half2 wh = __hfma2(s2[h], qh, b2[h]);
-          out[2 * i] = *reinterpret_cast<uint32_t*>(&wl);
-          out[2 * i + 1] = *reinterpret_cast<uint32_t*>(&wh);
+        if constexpr (SUBG == 1) {
+          s2[1] = s2[0];
+          b2[1] = b2[0];
         }
-        // 16 f16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row
-        *reinterpret_cast<uint4*>(brow + (((2 * c) ^ sw128) << 4)) =
-            make_uint4(out[0], out[1], out[2], out[3]);
-        *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ sw128) << 4)) =
-            make_uint4(out[4], out[5], out[6], out[7]);
+        const uint8_t* qrow = st + L::kA + row * 64;  // 64B-swizzled u8 row
+        uint8_t* brow = bt + row * 128;               // 128B-swizzled f16 row
+        const int sw64 = (row >> 1) & 3, sw128 = row & 7;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          // logical 16-byte chunk c of the packed row = k0 + 16c .. k0 + 16c + 15
+          const uint4 qv = *reinterpret_cast<const uint4*>(qrow + ((c ^ sw64) << 4));
+          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+          const int h = (G == 32) ? (c >> 1) : 0;
+          uint32_t out[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint32_t lo = __byte_perm(qw[i], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
+            uint32_t hi = __byte_perm(qw[i], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
+            const __half2 ql = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
+            const __half2 qh = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
+            const __half2 wl = __hfma2(s2[h], ql, b2[h]);
+            const __half2 wh = __hfma2(s2[h], qh, b2[h]);
+            out[2 * i] = *reinterpret_cast<const uint32_t*>(&wl);
+            out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&wh);
+          }
+          // 16 f16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row
+          *reinterpret_cast<uint4*>(brow + (((2 * c) ^ sw128) << 4)) =
+              make_uint4(out[0], out[1], out[2], out[3]);
+          *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ sw128) << 4)) =
+              make_uint4(out[4], out[5], out[6], out[7]);
+        }
       }
       fence_proxy_async_shared();  // generic-proxy writes -> tensor-core reads
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bready[s]);
+      if (lane == 0) {
+        mbar_arrive(&bfull[b]);
+        mbar_arrive(&empty[s]);  // packed weights and scales of stage s consumed
+      }
     }
 
     // ------------------------------------------------------------ epilogue
+    // the dequant warps wrote bias_s; make it visible to each other
+    asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
     ok = mbar_wait_bounded(accum, 0, a.status) && ok;
     tc_fence_after();
     const int quarter = warp & 3;  // TMEM lanes this warp may read
+    // warps sharing a lane quarter split the columns
+    constexpr int kColSplit = kDequantWarps / 4;
+    const int csub = (warp - kDequantWarp0) / 4;
     const int m = m0 + quarter * 32 + lane;
     const float rs = (a.row_scale != nullptr && m < a.M) ? a.row_scale[m] : 1.0f;
+    const bool has_bias = a.bias != nullptr;
+    const bool vec_ok = (a.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
       uint32_t r[32];
       tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
       tmem_wait_ld();
       if (m < a.M) {
+        float o[32];
+#pragma unroll
         for (int j = 0; j < 32; ++j) {
-          const int nn = n0 + c0 + j;
-          if (nn < a.N) {
-            const float v = __uint_as_float(r[j]) * rs;
-            float o = round_t<DT>(v);
-            if (a.bias != nullptr) o = round_t<DT>(o + ld_t<DT>(a.bias, nn));
-            if (a.act == kActSilu) o = round_t<DT>(o / (1.0f + expf(-o)));
-            else if (a.act == kActRelu) o = o > 0.f ? o : 0.f;
-            st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + nn, o);
+          float v = round_t<DT>(__uint_as_float(r[j]) * rs);
+          if (has_bias) v = round_t<DT>(v + bias_s[c0 + j]);
+          if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
+          else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
+          o[j] = v;
+        }
+        const int nb = n0 + c0;
+        if (vec_ok && nb + 32 <= a.N) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            if constexpr (DT == kBF16) {
+              const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
+              pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+            } else {
+              const __half2 h = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+              pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+            }
           }
+          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.y) +
+                                                static_cast<size_t>(m) * a.ldy + nb);
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (nb + j < a.N) st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + nb + j, o[j]);
         }
       }
     }
@@ -325,10 +380,11 @@ __global__ void __launch_bounds__(256)
 template <int DT, int G, int BN>
 cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, const GemmArgs& a,
                               cudaStream_t stream, bool pdl) {
-  using L = GemmSmem<BN>;
+  using L = GemmSmem<BN, (G == 32) ? 2 : 1>;
   auto kern = qgemm_kernel<DT, G, BN>;
   static bool configured = false;
   const int smem = L::kBytes + 1024;  // + alignment slack
+  static_assert(GemmSmem<BN, (G == 32) ? 2 : 1>::kBytes + 1024 <= 227 * 1024, "smem budget");
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -387,6 +443,56 @@ cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, 
                             ldx, M, K, reinterpret_cast<__half*>(xo), ldo, row_scale);
 }
 
-size_t gemm_smem_bytes() { return GemmSmem<kGemmBN>::kBytes + 1024; }
+size_t gemm_smem_bytes() { return GemmSmem<kGemmBN, 2>::kBytes + 1024; }
+
+// (scale, bias) pairs as f16 in the GEMM's k-tile order:
+// out[ntile][ktile][row][h], h over the 32-wide halves of a 64-wide k-tile
+// when g = 32 (otherwise one pair per row and k-tile); zero past N and K.
+template <int DT>
+__global__ void build_sb_tiles_kernel(const void* __restrict__ scales,
+                                      const void* __restrict__ biases, int N, int K, int G,
+                                      int subg, __half2* __restrict__ out) {
+  const int KT = (K + kBK - 1) / kBK;
+  const int NT = (N + kGemmBN - 1) / kGemmBN;
+  const size_t total = static_cast<size_t>(NT) * KT * kGemmBN * subg;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int h = static_cast<int>(i % subg);
+    const int r = static_cast<int>((i / subg) % kGemmBN);
+    const int kt = static_cast<int>((i / subg / kGemmBN) % KT);
+    const int nt = static_cast<int>(i / subg / kGemmBN / KT);
+    const int n = nt * kGemmBN + r, k = kt * kBK + h * 32;
+    float sv = 0.f, bv = 0.f;
+    if (n < N && k < K) {
+      const size_t gi = static_cast<size_t>(n) * (K / G) + k / G;
+      sv = ld_t<DT>(scales, gi);
+      bv = ld_t<DT>(biases, gi);
+    }
+    out[i] = __halves2half2(__float2half_rn(sv), __float2half_rn(bv));
+  }
+}
+
+size_t sb_tiles_bytes(int N, int K, int group) {
+  const int KT = (K + kBK - 1) / kBK;
+  const int NT = (N + kGemmBN - 1) / kGemmBN;
+  return static_cast<size_t>(NT) * KT * kGemmBN * (group == 32 ? 2 : 1) * sizeof(__half2);
+}
+
+cudaError_t build_sb_tiles(int dtype, const void* scales, const void* biases, int N, int K,
+                           int group, void* out, cudaStream_t stream) {
+  const int subg = group == 32 ? 2 : 1;
+  const size_t total = sb_tiles_bytes(N, K, group) / sizeof(__half2);
+  const int block = 256;
+  const int grid = static_cast<int>(std::min<size_t>((total + block - 1) / block, 65535));
+  if (dtype == kF16)
+    build_sb_tiles_kernel<kF16><<<grid, block, 0, stream>>>(scales, biases, N, K, group, subg,
+                                                           reinterpret_cast<__half2*>(out));
+  else if (dtype == kBF16)
+    build_sb_tiles_kernel<kBF16><<<grid, block, 0, stream>>>(scales, biases, N, K, group, subg,
+                                                            reinterpret_cast<__half2*>(out));
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
 
 }  // namespace cq

@@ -7,13 +7,12 @@
 
 namespace cq {
 
-constexpr int kGemmBN = 128;       // output columns per CTA
+constexpr int kGemmBN = 256;       // output columns per CTA
 constexpr int kGemmMinRows = 128;  // below this the GEMV (K1) is used
 
 struct GemmArgs {
   const float* row_scale;  // [M] per-row scale of the f16 activations, or nullptr
-  const void* scales;      // T [N, K/g]
-  const void* biases;      // T [N, K/g]
+  const void* sb_tiles;    // f16 (scale, bias) pairs in k-tile order (build_sb_tiles)
   const void* bias;        // T [N] or nullptr
   void* y;                 // T [M, ldy]
   int* status;             // device status word (watchdog)
@@ -22,12 +21,17 @@ struct GemmArgs {
 };
 
 // amap: f16 activations [M, K] (box 64 x 128, 128B swizzle);
-// qmap: packed weights u8 [N, K] (box 64 x 128, 64B swizzle).
+// qmap: packed weights u8 [N, K] (box 64 x kGemmBN, 64B swizzle).
 cudaError_t launch_gemm(int dtype, int group, const CUtensorMap& amap, const CUtensorMap& qmap,
                         const GemmArgs& args, cudaStream_t stream, bool pdl);
 // bf16 [M, ldx] -> f16 [M, ldo] with row_scale[m] = 2^e (power-of-two per row).
 cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, int ldo,
                                 float* row_scale, cudaStream_t stream, bool pdl);
 size_t gemm_smem_bytes();
+// Repacks T scales/biases [N, K/g] into the f16 (scale, bias) pair order the
+// GEMM streams per k-tile: [ceil(N/kGemmBN)][ceil(K/64)][kGemmBN][g == 32 ? 2 : 1].
+size_t sb_tiles_bytes(int N, int K, int group);
+cudaError_t build_sb_tiles(int dtype, const void* scales, const void* biases, int N, int K,
+                           int group, void* out, cudaStream_t stream);
 
 }  // namespace cq

@@ -147,6 +147,8 @@ QuantizedLinear::~QuantizedLinear() {
   cudaFree(biases_);
   cudaFree(bias_);
   cudaFree(host_scratch_);
+  cudaFree(ws_);
+  cudaFree(sb_tiles_);
   if (prev >= 0) cudaSetDevice(prev);
 }
 
@@ -170,6 +172,12 @@ void QuantizedLinear::finalize() {
   wmap_ = make_map_2d(q_, 1, N_, K_, K_, 16 * plan_.rt, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
   qmap_gemm_ = make_map_2d(q_, 1, N_, K_, K_, cq::kGemmBN, 64, CU_TENSOR_MAP_SWIZZLE_64B);
   gemm_ok_ = check_f16_range();
+  if (gemm_ok_) {
+    check_cuda(cudaMalloc(&sb_tiles_, cq::sb_tiles_bytes(N_, K_, group_)), "cudaMalloc(sb tiles)");
+    check_cuda(cq::build_sb_tiles(dtype_, scales_, biases_, N_, K_, group_, sb_tiles_, nullptr),
+               "build sb tiles");
+    check_cuda(cudaDeviceSynchronize(), "build sb tiles");
+  }
 }
 
 // K2 dequantises to f16.  f16 layers are exact by construction; a bf16 layer
@@ -237,8 +245,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
   }
   cq::GemmArgs g{};
   g.row_scale = row_scale;
-  g.scales = scales_;
-  g.biases = biases_;
+  g.sb_tiles = sb_tiles_;
   g.bias = bias_;
   g.y = y;
   g.status = ctx.status;

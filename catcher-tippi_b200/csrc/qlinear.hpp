@@ -116,6 +116,7 @@ class QuantizedLinear {
   // K2: packed weights with a 64-byte swizzle; scales/biases fit f16
   CUtensorMap qmap_gemm_{};
   bool gemm_ok_ = false;
+  void* sb_tiles_ = nullptr;  // (scale, bias) pairs in the GEMM's k-tile order
   // K2 workspace (bf16 layers): f16 activations [rows, K] + row scales [rows]
   std::mutex ws_mu_;
   void* ws_ = nullptr;
