@@ -71,6 +71,21 @@ WORKLOAD = ("quantized linears of the 24-block FastConformer encoder for one 112
             "at batch 1 (M=14; pos-proj M=139), bf16, INT8 group 64, 24 distinct weight sets")
 
 
+# DRAM bytes (read + write) per algorithmic byte of K1, from one ncu capture of
+# the 4096x1024 linear at M = 14 (4.531 MB for 4.600 MB algorithmic); traffic
+# grows with the bytes a launch streams, so it is scaled to the average launch.
+K1_TRAFFIC_PER_ALGO_BYTE = 4.5312e6 / 4599808
+
+
+def measured_tensor_peak() -> tuple[float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops_sustained"]), "measured"
+    except Exception:
+        return 1400.0, "fallback"
+
+
 def measured_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -141,9 +156,11 @@ class ClockSampler:
 
 
 class EncoderLinears:
-    """Weights and activation buffers of the 24-block linear chain on one GPU."""
+    """Weights and activation buffers of the 24-block linear chain on one GPU.
+    rows = 14 is one stream's chunk; rows = 896 stacks 64 streams' chunks (the
+    pos-proj input is shared by all streams and keeps its 139 rows)."""
 
-    def __init__(self, torch, cq, device: int, seed: int = 0):
+    def __init__(self, torch, cq, device: int, seed: int = 0, rows: int = M_FRAMES):
         self.torch, self.cq = torch, cq
         dev = torch.device("cuda", device)
         gen = torch.Generator(device=dev)
@@ -154,20 +171,25 @@ class EncoderLinears:
             for _, n, k, _, _, _ in BLOCK:
                 w = torch.randn((n, k), generator=gen, device=dev, dtype=torch.float32) * 0.02
                 q, s, b = cq.quantize(w, GROUP, "bf16")
-                blk.append(cq.QuantizedLinear.from_device(q, s, b, None, GROUP, "bf16", device))
+                layer = cq.QuantizedLinear.from_device(q, s, b, None, GROUP, "bf16", device)
+                layer.reserve(rows)  # batched-path workspace, before graph capture
+                blk.append(layer)
                 del w, q, s, b
             self.layers.append(blk)
         torch.cuda.synchronize()
         bf = torch.bfloat16
-        self.x0 = torch.randn((M_FRAMES, 1024), generator=gen, device=dev).to(bf)
+        self.rows = rows
+        self.spec = [(nm, n, k, rows if m == M_FRAMES else m, act, src)
+                     for nm, n, k, m, act, src in BLOCK]
+        self.x0 = torch.randn((rows, 1024), generator=gen, device=dev).to(bf)
         self.pe = torch.randn((POS_ROWS, 1024), generator=gen, device=dev).to(bf)
         self.out = {name: torch.empty((m, n), dtype=bf, device=dev)
-                    for name, n, _, m, _, _ in BLOCK}
+                    for name, n, _, m, _, _ in self.spec}
 
     def launch_step(self, stream_ptr: int) -> None:
         """All 24 blocks' linears, each consuming its producer's output."""
         for blk in self.layers:
-            for layer, (name, n, k, m, act, src) in zip(blk, BLOCK):
+            for layer, (name, n, k, m, act, src) in zip(blk, self.spec):
                 if src == "x0":
                     # block input: the previous block's output (or the chunk input)
                     x = self.x0 if blk is self.layers[0] else self.out["ffn2_down"]
@@ -210,6 +232,10 @@ class SingleLinear:
                               stream_ptr)
 
 
+BATCH_ROWS = 64 * M_FRAMES  # 64 concurrent streams' chunks stacked per linear
+BATCHED_WORKLOAD = ("quantized linears of the 24-block FastConformer encoder for one 1120 ms chunk "
+                    "of 64 concurrent streams (M=896 rows per linear; pos-proj M=139), bf16, INT8 "
+                    "group 64, 24 distinct weight sets")
 LINEAR_BYTES = linear_bytes(SingleLinear.N, SingleLinear.K, M_FRAMES)
 LINEAR_WORKLOAD = ("single INT8 affine quantized linear x bf16 [14,1024] . W[4096,1024]^T, "
                    "group 64, 40 independent back-to-back launches over distinct weight copies")
@@ -225,14 +251,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    step_flops = None
     if args.workload == "linear":
         enc = SingleLinear(torch, cq, local_rank)
         step_bytes, launches, workload = LINEAR_BYTES * SingleLinear.COPIES, SingleLinear.COPIES, LINEAR_WORKLOAD
-        in_shape, out_t = (M_FRAMES, SingleLinear.K), None
+        in_shape = (M_FRAMES, SingleLinear.K)
+    elif args.workload == "batched":
+        enc = EncoderLinears(torch, cq, local_rank, rows=BATCH_ROWS)
+        step_bytes = N_BLOCKS * sum(linear_bytes(n, k, m) for _, n, k, m, _, _ in enc.spec)
+        step_flops = N_BLOCKS * sum(2 * m * n * k for _, n, k, m, _, _ in enc.spec)
+        launches, workload = LAUNCHES_PER_STEP, BATCHED_WORKLOAD
+        in_shape = (BATCH_ROWS, 1024)
     else:
         enc = EncoderLinears(torch, cq, local_rank)
         step_bytes, launches, workload = STEP_BYTES, LAUNCHES_PER_STEP, WORKLOAD
-        in_shape, out_t = (M_FRAMES, 1024), None
+        in_shape = (M_FRAMES, 1024)
 
     # eager warm-up (sets kernel attributes before capture), then capture.
     stream = torch.cuda.Stream()
@@ -296,6 +329,20 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     peak, peak_kind = measured_peak()
     per_launch_us = ms_step * 1e3 / launches
     achieved = (step_bytes / launches) / (per_launch_us * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
+                "traffic": round(K1_TRAFFIC_PER_ALGO_BYTE * step_bytes / launches),
+                "traffic_note": "bytes per launch, scaled from the ncu capture of the 4096x1024 "
+                                "linear (dram read+write / algorithmic = 0.985)",
+                "kernel": "qgemv_kernel (K1)", "avg_launch_us": round(per_launch_us, 3)}
+    if step_flops is not None:
+        tpeak, tkind = measured_tensor_peak()
+        tflops = step_flops / (ms_step * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "achieved": round(tflops, 2), "peak": tpeak,
+                    "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4),
+                    "peak_kind": f"{tkind} dense bf16 (sustained: a step is a long run)",
+                    "traffic": None, "kernel": "qgemm_kernel (K2)",
+                    "avg_launch_us": round(per_launch_us, 3)}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -312,13 +359,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 "path": "C-ABI cq_linear_forward_ex calls captured in a CUDA graph with the "
                         "pinned-host input copy and output read inside the timed region"},
         "gpu_launches": launches * args.steps,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
-                     "traffic": None, "kernel": "qgemv_kernel (K1)",
-                     "avg_launch_us": round(per_launch_us, 3)},
+        "roofline": roofline,
         "clocks": clock_info,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if step_flops is not None:
+        line["tflops"] = round(step_flops / (ms_step * 1e-3) / 1e12 * world, 2)
+    if world == 1 and not args.no_cpu_baseline and args.workload != "batched":
         line["cpu_baseline"] = cpu_baseline(target_s=args.cpu_seconds, workload=args.workload)
     return line
 
@@ -411,9 +457,10 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "linear"], default="block",
+    ap.add_argument("--workload", choices=["block", "linear", "batched"], default="block",
                     help="block: the 24-block M=14 linear chain (default); linear: one "
-                         "4096x1024 linear, independent back-to-back launches")
+                         "4096x1024 linear, independent back-to-back launches; batched: the "
+                         "24-block chain at M=896 (64 streams), tensor-core path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()

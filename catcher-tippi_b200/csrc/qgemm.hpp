@@ -8,7 +8,7 @@
 namespace cq {
 
 constexpr int kGemmBN = 256;       // output columns per CTA
-constexpr int kGemmMinRows = 128;  // below this the GEMV (K1) is used
+constexpr int kGemmMinRows = 256;  // below this the GEMV (K1) is used
 
 struct GemmArgs {
   const float* row_scale;  // [M] per-row scale of the f16 activations, or nullptr

@@ -123,7 +123,7 @@ cq_status cq_linear_forward_f32(cq_linear *layer, const float *input, size_t inp
 
 /*
  * Sizes the layer's workspace for calls of up to max_rows rows.  Calls with
- * rows >= 128 run on the tensor-core GEMM; for bf16 layers that path stages
+ * rows >= 256 run on the tensor-core GEMM; for bf16 layers that path stages
  * the activations as f16 in a per-layer workspace that is otherwise
  * allocated on the first such call.  Reserve before capturing calls into a
  * CUDA graph.  No reference counterpart (MLX allocates inside its graph).

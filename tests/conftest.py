@@ -49,31 +49,48 @@ def widen(bits: np.ndarray, dtype: str) -> np.ndarray:
     return oracle.np_from_t(bits, dtype).astype(np.float64)
 
 
+MANT_BITS = {"bf16": 8, "f16": 11}
+MIN_ULP = {"bf16": 2.0 ** -133, "f16": 2.0 ** -24}
+
+
+def ulp(v: np.ndarray, dtype: str) -> np.ndarray:
+    """Spacing of T around |v| (T = bf16 or f16)."""
+    _, e = np.frexp(np.abs(v))
+    return np.maximum(np.ldexp(1.0, e - MANT_BITS[dtype]), MIN_ULP[dtype])
+
+
 def parity_stats(got_bits: np.ndarray, want_bits: np.ndarray, dtype: str) -> dict[str, float]:
-    """max-abs, relative L2 and exact-match fraction of two T bit-pattern arrays."""
+    """max-abs, max distance in T ulps, relative L2 and exact-match fraction."""
     g, w = widen(got_bits, dtype), widen(want_bits, dtype)
     diff = np.abs(g - w)
     scale = max(float(np.abs(w).max()), 1e-30)
+    if not diff.size:
+        return {"max_abs": 0.0, "max_rel_to_max": 0.0, "max_ulp": 0.0, "rel_l2": 0.0, "exact": 1.0}
     return {
-        "max_abs": float(diff.max()) if diff.size else 0.0,
-        "max_rel_to_max": float(diff.max() / scale) if diff.size else 0.0,
+        "max_abs": float(diff.max()),
+        "max_rel_to_max": float(diff.max() / scale),
+        "max_ulp": float((diff / ulp(np.maximum(np.abs(g), np.abs(w)), dtype)).max()),
         "rel_l2": float(np.linalg.norm(g - w) / max(np.linalg.norm(w), 1e-30)),
-        "exact": float(np.mean(np.asarray(got_bits) == np.asarray(want_bits))) if diff.size else 1.0,
+        "exact": float(np.mean(np.asarray(got_bits) == np.asarray(want_bits))),
     }
 
 
 # Output tolerances of the CUDA path against the oracle on identical packed
-# inputs (both accumulate in fp32; they differ only by summation order, so
-# results are within one T ulp):
-#   bf16: rel-L2 <= 4e-3 and max-abs <= 1e-2 * max|y|
-#   f16 : rel-L2 <= 1e-3 and max-abs <= 2e-3 * max|y|
-TOL = {"bf16": (4e-3, 1e-2), "f16": (1e-3, 2e-3)}
+# inputs.  Both accumulate in fp32 and differ only in summation order (and,
+# on the batched tensor-core path, in the f16 rounding of dequantised
+# weights).  The result is rounded to T twice, as QuantizedLinear::forward_array
+# does (quantized_matmul in T, then + output bias in T): next to a rounding tie
+# each rounding can fall either way, so two correct implementations may differ
+# by up to 2 ulps of T in an element.
+#   bf16: rel-L2 <= 4e-3,  every element within 2 bf16 ulps
+#   f16 : rel-L2 <= 1e-3,  every element within 2 f16 ulps
+TOL = {"bf16": 4e-3, "f16": 1e-3}
+MAX_ULP = 2.0
 
 
 def assert_parity(got_bits, want_bits, dtype: str, min_exact: float = 0.9):
     st = parity_stats(got_bits, want_bits, dtype)
-    rel_l2, rel_max = TOL[dtype]
-    assert st["rel_l2"] <= rel_l2, st
-    assert st["max_rel_to_max"] <= rel_max, st
+    assert st["rel_l2"] <= TOL[dtype], st
+    assert st["max_ulp"] <= MAX_ULP, st
     assert st["exact"] >= min_exact, st
     return st

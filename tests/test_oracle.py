@@ -121,7 +121,7 @@ def test_c_oracle_matches_golden(oracle_mod, dtype, group):
                                group, dtype, bias, ["none", "silu", "relu"][act])
         st = parity_stats(y, z[f"{name}_y"], dtype)
         # fp32 (C) vs fp64 (numpy) contraction: equal up to one rounding flip
-        assert st["exact"] >= 0.98 and st["max_rel_to_max"] <= 1e-2, (name, st)
+        assert st["exact"] >= 0.98 and st["max_ulp"] <= 2, (name, st)
 
 
 def test_fp32_and_fp64_oracles_agree(oracle_mod):

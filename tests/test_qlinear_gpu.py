@@ -115,9 +115,9 @@ def test_call_site_shapes_f16_other_groups(cq, torch_dev, oracle_mod, n, k, grou
     assert_parity(y, oracle_mod.qmatmul(x, q, s, b, group, "f16", bias), "f16", min_exact=0.97)
 
 
-@pytest.mark.parametrize("m", [15, 16, 17, 31, 33, 100, 127])
+@pytest.mark.parametrize("m", [15, 16, 17, 31, 33, 100, 139, 255])
 def test_token_tiles_beyond_16_rows(cq, torch_dev, oracle_mod, m):
-    """16 < M < 128 spreads 16-row token tiles over CTAs (128 rows and more run the GEMM)."""
+    """16 < M < 256 spreads 16-row token tiles over CTAs (256 rows and more run the GEMM)."""
     q, s, b, x, bias = make_case(oracle_mod, 1024, 1024, m, 64, "bf16", seed=m, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, "bf16")
     assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.97)
