@@ -11,7 +11,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import assert_parity
+from conftest import GEMM_FLOOR, assert_parity
 from test_qlinear_gpu import from_dev, make_case, run_gpu, to_dev
 
 pytestmark = pytest.mark.gpu
@@ -33,7 +33,8 @@ BATCHED = [(4096, 1024), (1024, 4096), (3072, 1024), (2048, 1024), (1025, 640), 
 def test_batched_bf16_g64(cq, torch_dev, oracle_mod, n, k, m):
     q, s, b, x, bias = make_case(oracle_mod, n, k, m, 64, "bf16", seed=3 * n + k + m, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, "bf16")
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.6)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.6, floor_frac=GEMM_FLOOR,
+                  bias_bits=bias)
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
@@ -44,27 +45,27 @@ def test_batched_dtypes_groups_ragged(cq, torch_dev, oracle_mod, dtype, group):
     q, s, b, x, bias = make_case(oracle_mod, 1000, k, 300, group, dtype, seed=group, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, group, dtype, act="silu")
     assert_parity(y, oracle_mod.qmatmul(x, q, s, b, group, dtype, bias, "silu"), dtype,
-                  min_exact=0.6)
+                  min_exact=0.6, floor_frac=GEMM_FLOOR, bias_bits=bias, act="silu")
 
 
 @pytest.mark.parametrize("m", [139, 255, 256, 257, 383])
 def test_row_threshold(cq, torch_dev, oracle_mod, m):
     q, s, b, x, _ = make_case(oracle_mod, 1024, 1024, m, 64, "bf16", seed=m)
     y = run_gpu(cq, torch_dev, q, s, b, None, x, 64, "bf16")
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6, floor_frac=GEMM_FLOOR)
 
 
 def test_batched_strided_rows(cq, torch_dev, oracle_mod):
     q, s, b, x, _ = make_case(oracle_mod, 640, 1024, 300, 64, "bf16", seed=5)
     y = run_gpu(cq, torch_dev, q, s, b, None, x, 64, "bf16", ldx_pad=64, ldy_pad=8)
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6, floor_frac=GEMM_FLOOR)
 
 
 @pytest.mark.parametrize("xscale", [1e-30, 1e30])
 def test_batched_bf16_activation_range(cq, torch_dev, oracle_mod, xscale):
     q, s, b, x, _ = make_case(oracle_mod, 1024, 1024, 256, 64, "bf16", seed=9, xscale=xscale)
     y = run_gpu(cq, torch_dev, q, s, b, None, x, 64, "bf16")
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6, floor_frac=GEMM_FLOOR)
 
 
 def test_small_scales_stay_exact(cq, torch_dev, oracle_mod):
@@ -77,7 +78,8 @@ def test_small_scales_stay_exact(cq, torch_dev, oracle_mod):
     torch = torch_dev
     y = layer.forward(to_dev(torch, x, "bf16"))
     torch.cuda.synchronize()
-    assert_parity(from_dev(y), oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.9)
+    assert_parity(from_dev(y), oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.9,
+                  floor_frac=GEMM_FLOOR)
 
 
 def test_reserve_then_graph_capture(cq, torch_dev, oracle_mod):
@@ -97,7 +99,7 @@ def test_reserve_then_graph_capture(cq, torch_dev, oracle_mod):
         layer.forward(xd, y, stream=st)
     g.replay()
     torch.cuda.synchronize()
-    assert_parity(from_dev(y), oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6)
+    assert_parity(from_dev(y), oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.6, floor_frac=GEMM_FLOOR)
     del g
 
 

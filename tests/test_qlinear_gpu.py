@@ -70,7 +70,11 @@ def test_golden_vectors(cq, torch_dev, dtype, group):
         y = run_gpu(cq, torch_dev, z[f"{name}_q"], z[f"{name}_s"], z[f"{name}_b"],
                     z.get(f"{name}_bias"), z[f"{name}_x"], group, dtype,
                     ["none", "silu", "relu"][act])
-        assert_parity(y, z[f"{name}_y"], dtype, min_exact=0.97)
+        try:
+            assert_parity(y, z[f"{name}_y"], dtype, min_exact=0.97,
+                          bias_bits=z.get(f"{name}_bias"), act=["none", "silu", "relu"][act])
+        except AssertionError as e:
+            raise AssertionError(f"golden case {name}: {e}") from None
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
@@ -103,7 +107,8 @@ CALL_SITES = [
 def test_call_site_shapes_bf16_g64(cq, torch_dev, oracle_mod, n, k, m):
     q, s, b, x, bias = make_case(oracle_mod, n, k, m, 64, "bf16", seed=n + k + m, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, "bf16")
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.97)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.97,
+                  bias_bits=bias)
 
 
 @pytest.mark.parametrize("n,k", [(4096, 1024), (1024, 4096), (1025, 640), (13088, 640)])
@@ -112,7 +117,8 @@ def test_call_site_shapes_f16_other_groups(cq, torch_dev, oracle_mod, n, k, grou
     """The reference's release artifact: f16 scales, group 128 (manifest.rs:344-357)."""
     q, s, b, x, bias = make_case(oracle_mod, n, k, 14, group, "f16", seed=7 * n + k, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, group, "f16")
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, group, "f16", bias), "f16", min_exact=0.97)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, group, "f16", bias), "f16", min_exact=0.97,
+                  bias_bits=bias)
 
 
 @pytest.mark.parametrize("m", [15, 16, 17, 31, 33, 100, 139, 255])
@@ -120,7 +126,8 @@ def test_token_tiles_beyond_16_rows(cq, torch_dev, oracle_mod, m):
     """16 < M < 256 spreads 16-row token tiles over CTAs (256 rows and more run the GEMM)."""
     q, s, b, x, bias = make_case(oracle_mod, 1024, 1024, m, 64, "bf16", seed=m, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, "bf16")
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.97)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias), "bf16", min_exact=0.97,
+                  bias_bits=bias)
 
 
 @pytest.mark.parametrize("act", ["silu", "relu"])
@@ -128,7 +135,8 @@ def test_token_tiles_beyond_16_rows(cq, torch_dev, oracle_mod, m):
 def test_fused_activation(cq, torch_dev, oracle_mod, act, dtype):
     q, s, b, x, bias = make_case(oracle_mod, 4096, 1024, 14, 64, dtype, seed=11, with_bias=True)
     y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, dtype, act=act)
-    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, dtype, bias, act), dtype, min_exact=0.97)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, dtype, bias, act), dtype, min_exact=0.97,
+                  bias_bits=bias, act=act)
 
 
 def test_strided_rows(cq, torch_dev, oracle_mod):
@@ -168,7 +176,7 @@ def test_bit_identical_reruns(cq, torch_dev, oracle_mod):
 
 def test_concat_matches_separate_layers(cq, torch_dev, oracle_mod):
     torch = torch_dev
-    parts, outs = [], []
+    parts, outs, biases = [], [], []
     x = None
     for i, n in enumerate((1024, 1024, 512)):
         q, s, b, xx, bias = make_case(oracle_mod, n, 1024, 14, 64, "bf16", seed=40 + i,
@@ -176,11 +184,13 @@ def test_concat_matches_separate_layers(cq, torch_dev, oracle_mod):
         x = xx if x is None else x
         parts.append(cq.QuantizedLinear.from_packed(q, s, b, bias, 64, "bf16"))
         outs.append(oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias))
+        biases.append(bias if bias is not None else np.zeros(n, np.uint16))
     fused = cq.QuantizedLinear.concat(parts)
     assert fused.output_dims == 2560
     y = fused.forward(to_dev(torch, x, "bf16"))
     torch.cuda.synchronize()
-    assert_parity(from_dev(y), np.concatenate(outs, axis=1), "bf16", min_exact=0.97)
+    assert_parity(from_dev(y), np.concatenate(outs, axis=1), "bf16", min_exact=0.97,
+                  bias_bits=np.concatenate(biases))
 
 
 # ---------------------------------------------------------------- reference KATs
@@ -272,7 +282,8 @@ def test_from_f32_matches_oracle_quantiser(cq, torch_dev, oracle_mod):
     q, s, b = oracle_mod.quantize(w, 64, "bf16")
     want = oracle_mod.qmatmul(oracle_mod.to_t(x, "bf16"), q, s, b, 64, "bf16",
                               oracle_mod.to_t(bias, "bf16"))
-    assert_parity(oracle_mod.to_t(y, "bf16"), want, "bf16", min_exact=0.97)
+    assert_parity(oracle_mod.to_t(y, "bf16"), want, "bf16", min_exact=0.97,
+                  bias_bits=oracle_mod.to_t(bias, "bf16"))
 
 
 def test_device_status_clean(cq, torch_dev):
