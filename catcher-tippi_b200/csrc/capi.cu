@@ -137,6 +137,24 @@ cq_status cq_linear_forward_f32(cq_linear* layer, const float* input, size_t inp
   });
 }
 
+cq_status cq_linear_forward_noalloc(cq_linear* layer, const void* x, int32_t ldx, int32_t rows,
+                                   void* y, int32_t ldy, cq_act act, void* stream) {
+  return guarded([&] {
+    need_handle(layer, "layer");
+    auto& L = *layer->impl;
+    const size_t cap = nemotron_cuda::noalloc_scratch_capacity();
+    if (rows > 0 && L.scratch_bytes_for(rows) > cap)
+      nemotron_cuda::throw_invalid(
+          "rows x input_dims = " + std::to_string(rows) + "x" + std::to_string(L.input_dims()) +
+          " exceeds the no-allocation scratch of " + std::to_string(cap) + " bytes");
+    void* scratch = rows > 0 && L.scratch_bytes_for(rows) > 0
+                        ? nemotron_cuda::noalloc_scratch_address(L.device())
+                        : nullptr;
+    L.forward_array_in_scratch(x, ldx, rows, y, ldy, act, static_cast<cudaStream_t>(stream),
+                               scratch, cap);
+  });
+}
+
 cq_status cq_linear_reserve(cq_linear* layer, int32_t max_rows) {
   return guarded([&] {
     need_handle(layer, "layer");

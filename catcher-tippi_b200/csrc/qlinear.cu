@@ -257,6 +257,60 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
   check_cuda(cq::launch_gemm(dtype_, group_, amap_, qmap_gemm_, g, stream, pdl_enabled()), "qgemm");
 }
 
+size_t QuantizedLinear::scratch_bytes_for(int rows) const {
+  if (dtype_ != CQ_BF16 || !gemm_ok_ || !gemm_allowed() || rows < cq::kGemmMinRows) return 0;
+  return align_up(static_cast<size_t>(rows) * K_ * 2, 256) + static_cast<size_t>(rows) * 4;
+}
+
+void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows, void* y, int ldy,
+                                               int act, cudaStream_t stream, void* scratch,
+                                               size_t scratch_bytes) {
+  const size_t need = rows > 0 ? scratch_bytes_for(rows) : 0;
+  if (need == 0) {
+    // the GEMV, the f16 GEMM and the f32 path stage nothing
+    forward_array(x, ldx, rows, y, ldy, act, stream);
+    return;
+  }
+  if (need > scratch_bytes)
+    throw_invalid("rows x input_dims = " + std::to_string(rows) + "x" + std::to_string(K_) +
+                  " needs " + std::to_string(need) + " bytes of scratch; the no-allocation limit is " +
+                  std::to_string(scratch_bytes) + " bytes");
+  if (x == nullptr || y == nullptr || scratch == nullptr)
+    throw_invalid("input, output and scratch must not be null");
+  if (ldx < K_ || ldy < N_)
+    throw_invalid("leading dimensions (" + std::to_string(ldx) + ", " + std::to_string(ldy) +
+                  ") are smaller than the layer (" + std::to_string(K_) + ", " +
+                  std::to_string(N_) + ")");
+  if (act != CQ_ACT_NONE && act != CQ_ACT_SILU && act != CQ_ACT_RELU)
+    throw_invalid("unknown activation " + std::to_string(act));
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0)
+    throw_invalid("input rows must be 16-byte aligned (x % 16 == 0 and ldx % 8 == 0)");
+  DeviceContext& ctx = device_context(device_);
+  DeviceGuard guard(device_);
+  const size_t xbytes = align_up(static_cast<size_t>(rows) * K_ * 2, 256);
+  float* rs = reinterpret_cast<float*>(static_cast<char*>(scratch) + xbytes);
+  check_cuda(cq::launch_gemm_prepass(x, ldx, rows, K_, scratch, K_, rs, stream, pdl_enabled()),
+             "qgemm prepass");
+  if (scratch != amap_scratch_ptr_ || rows != amap_scratch_rows_) {
+    amap_scratch_ = make_map_2d(scratch, 2, rows, K_, K_, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_scratch_ptr_ = scratch;
+    amap_scratch_rows_ = rows;
+  }
+  cq::GemmArgs g{};
+  g.row_scale = rs;
+  g.sb_tiles = sb_tiles_;
+  g.bias = bias_;
+  g.y = y;
+  g.status = ctx.status;
+  g.M = rows;
+  g.N = N_;
+  g.K = K_;
+  g.ldy = ldy;
+  g.act = act;
+  check_cuda(cq::launch_gemm(dtype_, group_, amap_scratch_, qmap_gemm_, g, stream, pdl_enabled()),
+             "qgemm");
+}
+
 std::unique_ptr<QuantizedLinear> QuantizedLinear::from_packed(const uint32_t* qweight,
                                                               const void* scales,
                                                               const void* biases, const void* bias,

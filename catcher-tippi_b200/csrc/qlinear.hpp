@@ -88,6 +88,13 @@ class QuantizedLinear {
   void reserve(int max_rows);
   // True when batched calls run on the tensor-core GEMM (K2).
   bool gemm_enabled() const { return gemm_ok_; }
+  // forward_array that never allocates device memory: the batched bf16 path
+  // stages its f16 activations in the caller-provided device scratch instead
+  // of the layer's workspace; every other path needs no scratch.  Throws
+  // invalid-argument if the scratch is smaller than scratch_bytes_for(rows).
+  void forward_array_in_scratch(const void* x, int ldx, int rows, void* y, int ldy, int act,
+                                cudaStream_t stream, void* scratch, size_t scratch_bytes);
+  size_t scratch_bytes_for(int rows) const;
 
   int input_dims() const { return K_; }
   int output_dims() const { return N_; }
@@ -128,6 +135,10 @@ class QuantizedLinear {
   int amap_ld_ = 0, amap_rows_ = 0;
   void forward_gemm(const void* x, int ldx, int rows, void* y, int ldy, int act,
                     cudaStream_t stream);
+  // activation tensor map of the scratch-staged path, cached separately
+  CUtensorMap amap_scratch_{};
+  const void* amap_scratch_ptr_ = nullptr;
+  int amap_scratch_rows_ = 0;
   bool check_f16_range() const;
 
   // Scratch of the synchronous host-f32 path, grown on demand.
@@ -137,6 +148,10 @@ class QuantizedLinear {
 };
 
 size_t dtype_size(cq_dtype dtype);
+
+// Device scratch of the no-allocation entry point (noalloc.cu).
+size_t noalloc_scratch_capacity();
+void* noalloc_scratch_address(int device);
 
 // backend::quantized_matmul: quantise the f32 weight (f32 scales) on the
 // device and return input . dequant(weight)^T as f32.

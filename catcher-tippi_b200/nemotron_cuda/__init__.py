@@ -52,6 +52,7 @@ def lib() -> ctypes.CDLL:
         "cq_linear_forward_ex": ([vp, vp, i32, i32, vp, i32, i32, vp], i32),
         "cq_linear_forward_f32": ([vp, vp, sz, i32, vp, sz], i32),
         "cq_linear_reserve": ([vp, i32], i32),
+        "cq_linear_forward_noalloc": ([vp, vp, i32, i32, vp, i32, i32, vp], i32),
         "cq_linear_input_dims": ([vp], i32),
         "cq_linear_output_dims": ([vp], i32),
         "cq_linear_group_size": ([vp], i32),

@@ -130,6 +130,28 @@ cq_status cq_linear_forward_f32(cq_linear *layer, const float *input, size_t inp
  */
 cq_status cq_linear_reserve(cq_linear *layer, int32_t max_rows);
 
+/*
+ * cq_linear_forward_ex without any device allocation, for callers that
+ * cannot allocate device memory once a stream is running: a transcriber fed
+ * from a real-time audio path, or a host held to a GPU memory budget fixed at
+ * start-up, cannot afford a cudaMalloc mid-stream (it can block for
+ * milliseconds, synchronises with queued work, and can fail under memory
+ * pressure).  The only scratch the layer needs -- the f16 copy of bf16
+ * activations that calls with rows >= 256 stage before the tensor-core GEMM --
+ * comes from an 8 MiB array that is part of the library's device image, held
+ * by every GPU that loads the library until the process exits.  Limit:
+ * rows * input_dims * 2 (rounded up to 256) + rows * 4 bytes <= 8 MiB, e.g.
+ * 896 rows at input_dims 4096; larger calls fail with CQ_INVALID_ARGUMENT and
+ * a message naming the limit.  The first such call on a device looks the
+ * array's device address up (once per device), so make it before any stream
+ * capture.  All calls share the array and it keeps the last call's contents
+ * (every call overwrites what it reads); calls that overlap on the GPU race,
+ * so serialise them (one stream, or events).
+ * No counterpart in the reference: MLX allocates inside its own graph.
+ */
+cq_status cq_linear_forward_noalloc(cq_linear *layer, const void *x, int32_t ldx, int32_t rows,
+                                    void *y, int32_t ldy, cq_act act, void *stream);
+
 /* Dimensions and type of a layer (layers.rs:312-318). */
 int32_t cq_linear_input_dims(const cq_linear *layer);
 int32_t cq_linear_output_dims(const cq_linear *layer);
