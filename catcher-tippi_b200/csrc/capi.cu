@@ -7,54 +7,28 @@
 #include <string>
 #include <vector>
 
+#include "capi_guard.hpp"
 #include "cqlinear.h"
 #include "qlinear.hpp"
 #include "qops.hpp"
 
-struct cq_linear {
-  std::unique_ptr<nemotron_cuda::QuantizedLinear> impl;
-};
-
 namespace {
 
-thread_local std::string g_last_error;
-
-template <class F>
-cq_status guarded(F&& f) {
-  try {
-    f();
-    g_last_error.clear();
-    return CQ_OK;
-  } catch (const nemotron_cuda::Error& e) {
-    g_last_error = e.what();
-    return e.status();
-  } catch (const std::bad_alloc&) {
-    g_last_error = "host allocation failed";
-    return CQ_RUNTIME_ERROR;
-  } catch (const std::exception& e) {
-    g_last_error = e.what();
-    return CQ_RUNTIME_ERROR;
-  } catch (...) {
-    g_last_error = "unknown error";
-    return CQ_RUNTIME_ERROR;
-  }
-}
+using nemotron_cuda::guarded;
+using nemotron_cuda::need_handle;
 
 cq_linear* wrap(std::unique_ptr<nemotron_cuda::QuantizedLinear> p) {
   cq_linear* h = new cq_linear;
-  h->impl = std::move(p);
+  h->owned = std::move(p);
+  h->impl = h->owned.get();
   return h;
-}
-
-void need_handle(const void* h, const char* what) {
-  if (h == nullptr) nemotron_cuda::throw_invalid(std::string(what) + " must not be null");
 }
 
 }  // namespace
 
 extern "C" {
 
-const char* cq_last_error(void) { return g_last_error.c_str(); }
+const char* cq_last_error(void) { return nemotron_cuda::last_error_slot().c_str(); }
 
 const char* cq_version(void) { return "cqlinear 0.1.0 (sm_100a)"; }
 
@@ -106,7 +80,7 @@ cq_status cq_linear_concat(cq_linear* const* parts, int32_t count, cq_linear** o
     std::vector<const nemotron_cuda::QuantizedLinear*> v;
     for (int i = 0; i < count; ++i) {
       need_handle(parts[i], "layer");
-      v.push_back(parts[i]->impl.get());
+      v.push_back(parts[i]->impl);
     }
     *out = wrap(nemotron_cuda::QuantizedLinear::concat(v));
   });
@@ -185,7 +159,37 @@ cq_status cq_linear_device_arrays(const cq_linear* layer, const void** qweight,
   });
 }
 
-void cq_linear_destroy(cq_linear* layer) { delete layer; }
+cq_status cq_linear_copy_arrays(const cq_linear* layer, uint32_t* qweight, void* scales,
+                                void* biases, void* bias) {
+  return guarded([&] {
+    need_handle(layer, "layer");
+    const auto& L = *layer->impl;
+    nemotron_cuda::DeviceGuard guard(L.device());
+    const size_t n = static_cast<size_t>(L.output_dims()), k = static_cast<size_t>(L.input_dims());
+    const size_t es = nemotron_cuda::dtype_size(L.dtype());
+    const size_t groups = n * (k / L.group_size());
+    if (qweight)
+      nemotron_cuda::check_cuda(cudaMemcpy(qweight, L.qweight(), n * k, cudaMemcpyDefault), "copy qweight");
+    if (scales)
+      nemotron_cuda::check_cuda(cudaMemcpy(scales, L.scales(), groups * es, cudaMemcpyDefault), "copy scales");
+    if (biases)
+      nemotron_cuda::check_cuda(cudaMemcpy(biases, L.biases(), groups * es, cudaMemcpyDefault), "copy biases");
+    if (bias) {
+      if (L.bias() != nullptr) {
+        nemotron_cuda::check_cuda(cudaMemcpy(bias, L.bias(), n * es, cudaMemcpyDefault), "copy bias");
+      } else {
+        const std::vector<unsigned char> zeros(n * es, 0);  // host or device destination
+        nemotron_cuda::check_cuda(cudaMemcpy(bias, zeros.data(), n * es, cudaMemcpyDefault),
+                                  "zero bias");
+      }
+    }
+  });
+}
+
+void cq_linear_destroy(cq_linear* layer) {
+  // borrowed handles (cq_encoder_linear) belong to their encoder
+  if (layer != nullptr && !layer->borrowed) delete layer;
+}
 
 cq_status cq_quantized_matmul(const float* input, size_t input_len, size_t rows,
                               size_t input_dims, const float* weight, size_t weight_len,

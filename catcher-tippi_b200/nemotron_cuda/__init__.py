@@ -58,11 +58,30 @@ def lib() -> ctypes.CDLL:
         "cq_linear_group_size": ([vp], i32),
         "cq_linear_dtype": ([vp], i32),
         "cq_linear_device_arrays": ([vp, pp, pp, pp, pp], i32),
+        "cq_linear_copy_arrays": ([vp, vp, vp, vp, vp], i32),
         "cq_linear_destroy": ([vp], None),
         "cq_quantized_matmul": ([vp, sz, sz, sz, vp, sz, sz, sz, vp, sz], i32),
         "cq_quantize": ([vp, i32, i32, i32, i32, i32, vp, vp, vp, vp], i32),
         "cq_dequantize": ([vp, vp, vp, i32, i32, i32, i32, vp, vp], i32),
         "cq_device_status": ([i32, ctypes.POINTER(ctypes.c_int32)], i32),
+        # streaming encoder (include/cqencoder.h)
+        "cq_encoder_default_config": ([vp], None),
+        "cq_encoder_create": ([vp, i32, i32, pp], i32),
+        "cq_encoder_set_linear": ([vp, ctypes.c_char_p, vp, vp, vp, vp, i32, i32, i32], i32),
+        "cq_encoder_set_tensor": ([vp, ctypes.c_char_p, vp, sz], i32),
+        "cq_encoder_get_tensor": ([vp, ctypes.c_char_p, vp, sz], i32),
+        "cq_encoder_linear": ([vp, ctypes.c_char_p], vp),
+        "cq_encoder_init_random": ([vp, ctypes.c_uint64], i32),
+        "cq_encoder_tensor_count": ([vp], i32),
+        "cq_encoder_tensor_name": ([vp, i32], ctypes.c_char_p),
+        "cq_encoder_destroy": ([vp], None),
+        "cq_encoder_state_create": ([vp, i32, i32, pp], i32),
+        "cq_encoder_state_set_prompts": ([vp, vp, i32], i32),
+        "cq_encoder_state_output_frames": ([vp, i32], i32),
+        "cq_encoder_encode_chunk": ([vp, vp, i32, vp, vp], i32),
+        "cq_encoder_state_chunks": ([vp], i32),
+        "cq_encoder_state_reset": ([vp], i32),
+        "cq_encoder_state_destroy": ([vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

@@ -162,7 +162,15 @@ cq_dtype cq_linear_dtype(const cq_linear *layer);
 cq_status cq_linear_device_arrays(const cq_linear *layer, const void **qweight,
                                   const void **scales, const void **biases, const void **bias);
 
-/* Frees the layer and its device arrays.  NULL is a no-op. */
+/* Copies the layer's packed arrays into caller memory (host or device; any
+ * pointer may be NULL): qweight u32 [N, K/4], scales/biases T [N, K/g], bias
+ * T [N] (zeros when the layer has none).  Synchronous.  The inverse of
+ * cq_linear_create, e.g. to write an artifact (weights/artifact.rs:222-240). */
+cq_status cq_linear_copy_arrays(const cq_linear *layer, uint32_t *qweight, void *scales,
+                                void *biases, void *bias);
+
+/* Frees the layer and its device arrays.  NULL, and handles borrowed from an
+ * encoder (cq_encoder_linear), are a no-op. */
 void cq_linear_destroy(cq_linear *layer);
 
 /*

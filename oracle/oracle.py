@@ -108,6 +108,8 @@ def quantize(w: np.ndarray, group: int, dtype: str, round_input: bool = True):
     """Affine 8-bit quantisation -> (q u32 [N, K/4], scales T [N, K/g], biases T [N, K/g])."""
     w = np.ascontiguousarray(w, dtype=np.float32)
     n, k = w.shape
+    if group <= 0 or k % group:
+        raise ValueError(f"input dimension {k} is not divisible by group size {group}")
     q = np.empty((n, k), dtype=np.uint8)
     s = np.empty((n, k // group), dtype=_tbits(dtype))
     b = np.empty_like(s)

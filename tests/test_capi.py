@@ -119,3 +119,21 @@ def test_quantize_entry_validates_before_device_work(cq):
     assert lib.cq_quantize(None, 4, 100, 64, 0, 1, None, None, None, None) == cq.CQ_INVALID_ARGUMENT
     assert "group size 64" in cq.last_error()
     assert lib.cq_dequantize(None, None, None, 4, 128, 24, 0, None, None) == cq.CQ_INVALID_ARGUMENT
+
+
+def test_encoder_abi_rejects_null_arguments_without_a_device(cq):
+    """cqencoder.h entry points validate their handles before any CUDA call."""
+    from nemotron_cuda.encoder import EncoderConfig
+    cfg = EncoderConfig.default()
+    assert cfg.as_dict() == dict(hidden=1024, ff=4096, layers=24, heads=8, conv_kernel=9,
+                                 sliding_window=57, mel_bins=128, sub_channels=256,
+                                 num_prompts=128, prompt_hidden=2048, group_size=64)
+    L = cq.lib()
+    h = ctypes.c_void_p()
+    assert L.cq_encoder_create(None, 1, 0, ctypes.byref(h)) == cq.CQ_INVALID_ARGUMENT
+    assert "config must not be null" in cq.last_error()
+    assert L.cq_encoder_set_tensor(None, b"x", None, 0) == cq.CQ_INVALID_ARGUMENT
+    assert L.cq_encoder_encode_chunk(None, None, 112, None, None) == cq.CQ_INVALID_ARGUMENT
+    assert L.cq_encoder_state_output_frames(None, 112) == 0
+    assert L.cq_encoder_tensor_count(None) == -1
+    assert L.cq_encoder_linear(None, b"x") is None
