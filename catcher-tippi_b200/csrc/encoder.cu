@@ -291,6 +291,9 @@ void Encoder::finalize() {
   DeviceGuard guard(device_);
   fused_qkv_.clear();
   blocks_.clear();
+  dw_wt_.clear();
+  const int D = cfg_.hidden, K = cfg_.conv_kernel;
+  std::vector<float> w(static_cast<size_t>(D) * K), wt(w.size());
   for (int i = 0; i < cfg_.layers; ++i) {
     const std::string p = "encoder.layers." + std::to_string(i);
     // one N = 3 * hidden projection: output columns are independent, so the
@@ -320,7 +323,16 @@ void Encoder::finalize() {
     b.norm_out_b = tensor(p + ".norm_out.bias");
     b.conv_norm_w = tensor(p + ".conv.norm.weight");
     b.conv_norm_b = tensor(p + ".conv.norm.bias");
-    b.dw_w = tensor(p + ".conv.depthwise_conv.weight");
+    // [D, 1, K] -> [K][D]: the conv kernel reads eight channels of one tap per load
+    get_tensor(p + ".conv.depthwise_conv.weight", w.data(), w.size());
+    for (int c = 0; c < D; ++c)
+      for (int k = 0; k < K; ++k) wt[static_cast<size_t>(k) * D + c] = w[static_cast<size_t>(c) * K + k];
+    DeviceBuffer f32(wt.size() * 4), tbuf(wt.size() * 2);
+    check_cuda(cudaMemcpy(f32.get(), wt.data(), wt.size() * 4, cudaMemcpyHostToDevice), "upload kernel");
+    check_cuda(cq::launch_f32_to_t(dtype_, f32.as<float>(), wt.size(), tbuf.get(), nullptr), "round kernel");
+    check_cuda(cudaDeviceSynchronize(), "transpose depthwise kernel");
+    dw_wt_.push_back(std::move(tbuf));
+    b.dw_wt = dw_wt_.back().get();
     b.dw_b = zero_dw_bias_.get();
     b.bias_u = static_cast<const float*>(tensor(p + ".self_attn.bias_u"));
     b.bias_v = static_cast<const float*>(tensor(p + ".self_attn.bias_v"));
@@ -366,6 +378,7 @@ EncoderState::EncoderState(Encoder& enc, int streams, int max_mel_frames)
     throw_invalid("attention window of " + std::to_string(vmax_) + " frames exceeds shared memory");
 
   DeviceGuard guard(enc_.device());
+  num_sms_ = device_context(enc_.device()).num_sms;
   const size_t S = S_, D = c.hidden, C = c.sub_channels, L = c.layers, Q = qmax_;
   const size_t es = 2;
   hid_width_ = std::max<size_t>({static_cast<size_t>(c.ff), 2 * D, static_cast<size_t>(c.prompt_hidden)});
@@ -596,6 +609,7 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
     at.ring = ring_;
     at.cache_frames = cache_frames;
     at.vmax = vmax_;
+    at.qsplit = cq::attention_qsplit(S, c.heads, Q, num_sms_);
     at.scale = 1.0f / std::sqrt(static_cast<float>(hd));
     check_cuda(cq::launch_attention(dt, at, st, pdl), "attention");
     linear(b.o, att_.get(), D, rows, y_.get(), D, CQ_ACT_NONE, st);
@@ -605,7 +619,7 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
     cq::ConvArgs cv{};
     cv.pw1 = hid_.get();
     cv.ldp = 2 * D;
-    cv.dw_w = b.dw_w;
+    cv.dw_wt = b.dw_wt;
     cv.dw_b = b.dw_b;
     cv.ln_w = b.conv_norm_w;
     cv.ln_b = b.conv_norm_b;

@@ -57,7 +57,7 @@ class Encoder {
     QuantizedLinear *ff1a, *ff1b, *qkv, *o, *pos, *pw1, *pw2, *ff2a, *ff2b;
     const void *norm_ff1_w, *norm_ff1_b, *norm_att_w, *norm_att_b, *norm_conv_w, *norm_conv_b;
     const void *norm_ff2_w, *norm_ff2_b, *norm_out_w, *norm_out_b;
-    const void *conv_norm_w, *conv_norm_b, *dw_w, *dw_b;
+    const void *conv_norm_w, *conv_norm_b, *dw_wt, *dw_b;  // dw_wt: [K][D]
     const float *bias_u, *bias_v;
   };
 
@@ -93,6 +93,7 @@ class Encoder {
   std::map<std::string, DeviceBuffer> dense_;
   std::vector<std::unique_ptr<QuantizedLinear>> fused_qkv_;
   DeviceBuffer zero_dw_bias_;
+  std::vector<DeviceBuffer> dw_wt_;  // depthwise kernels transposed to [K][D]
   std::vector<Block> blocks_;
   bool finalized_ = false;
 };
@@ -136,6 +137,7 @@ class EncoderState {
   DeviceBuffer sub_cache_[3];
   DeviceBuffer scratch_;
   size_t hid_width_ = 0;
+  int num_sms_ = 148;
 
   struct GraphEntry {
     int mel_frames;

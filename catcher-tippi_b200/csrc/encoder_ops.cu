@@ -11,9 +11,12 @@
 //   residual_add / silu_in_place      encoder.rs:538-558
 //   mask_invalid_time, channel_frequency_flatten  encoder.rs:805-833
 //   AttentionKvCache / CausalConv*Cache           crates/nemotron-mlx/src/model/cache.rs
-// Everything here is small next to the quantized linears (HBM-bound at one
-// stream, tensor-bound at many); the kernels are written for coalesced 2- and
-// 16-byte accesses and a short dependent chain (PDL) rather than peak FLOPs.
+//
+// These ops move little data next to the quantized linears, so what bounds
+// them is latency: every kernel reads its rows with 16-byte loads issued
+// together (eight T values per thread and load), keeps weights it reuses in
+// shared memory transposed for conflict-free vector reads, and sizes its grid
+// so a single stream still spreads over many SMs.
 #include "common.cuh"
 #include "encoder_ops.hpp"
 
@@ -21,7 +24,6 @@ namespace cq {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kMaxPerThread = 16;  // rows up to 16 * 256 = 4096 wide
 
 template <typename Kern, typename... Args>
 cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -41,6 +43,48 @@ cudaError_t launch_ex(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// ------------------------------------------------------------------ 8-wide T vectors
+
+template <int DT>
+__device__ __forceinline__ float t_bits_to_f(uint16_t v) {
+  if constexpr (DT == kBF16) return __uint_as_float(static_cast<uint32_t>(v) << 16);
+  else return __half2float(__ushort_as_half(v));
+}
+
+template <int DT>
+__device__ __forceinline__ uint16_t f_to_t_bits(float v) {
+  if constexpr (DT == kBF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  else return __half_as_ushort(__float2half_rn(v));
+}
+
+template <int DT>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    x[2 * i] = t_bits_to_f<DT>(static_cast<uint16_t>(w[i] & 0xFFFFu));
+    x[2 * i + 1] = t_bits_to_f<DT>(static_cast<uint16_t>(w[i] >> 16));
+  }
+}
+
+// Rounds each value to T.
+template <int DT>
+__device__ __forceinline__ uint4 pack8(const float (&x)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    w[i] = f_to_t_bits<DT>(x[2 * i]) | (static_cast<uint32_t>(f_to_t_bits<DT>(x[2 * i + 1])) << 16);
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+__device__ __forceinline__ uint4 ld16(const void* base, size_t elem) {
+  return *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + elem);
+}
+
+__device__ __forceinline__ void st16(void* base, size_t elem, uint4 v) {
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + elem) = v;
+}
+
 // Sum over the block; every thread returns the same value (same order).
 __device__ __forceinline__ float block_sum(float v, float* red) {
 #pragma unroll
@@ -54,101 +98,93 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-// LayerNorm of one row held in registers (v[k] for column threadIdx.x + k*256,
-// already T values); returns T-rounded outputs in o[].
+// LayerNorm of one row spread 8 values per thread (thread i holds columns
+// 8i..8i+7, `active` when inside the row); v are T values, o the T-rounded output.
 template <int DT>
-__device__ __forceinline__ void layernorm_regs(const float (&v)[kMaxPerThread], float (&o)[kMaxPerThread],
-                                               int D, const void* w, const void* b, float eps,
-                                               float* red) {
+__device__ __forceinline__ void layernorm8(const float (&v)[8], float (&o)[8], bool active, int c0,
+                                           int D, const void* w, const void* b, float eps,
+                                           float* red) {
   float s = 0.0f;
+  if (active) {
 #pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    if (i < D) s += v[k];
+    for (int k = 0; k < 8; ++k) s += v[k];
   }
   const float mean = block_sum(s, red) / static_cast<float>(D);
   float sq = 0.0f;
+  if (active) {
 #pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    if (i < D) {
+    for (int k = 0; k < 8; ++k) {
       const float d = v[k] - mean;
       sq += d * d;
     }
   }
   const float var = block_sum(sq, red) / static_cast<float>(D);
   const float rstd = 1.0f / sqrtf(var + eps);
+  if (active) {
+    float wv[8], bv[8];
+    unpack8<DT>(ld16(w, c0), wv);
+    unpack8<DT>(ld16(b, c0), bv);
 #pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    if (i < D) o[k] = round_t<DT>((v[k] - mean) * rstd * ld_t<DT>(w, i) + ld_t<DT>(b, i));
+    for (int k = 0; k < 8; ++k) o[k] = round_t<DT>((v[k] - mean) * rstd * wv[k] + bv[k]);
   }
 }
+
+int row_threads(int D) { return ((D / 8 + 31) / 32) * 32; }
 
 // ------------------------------------------------------------------ LayerNorm
 
 template <int DT>
-__global__ void __launch_bounds__(kThreads) layernorm_kernel(const LnArgs a) {
+__global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
   __shared__ float red[32];
   pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x;
   const int D = a.D;
+  const int c0 = threadIdx.x * 8;
+  const bool active = c0 < D;
   float* res = a.res + static_cast<size_t>(row) * D;
-  float r[kMaxPerThread], t[kMaxPerThread], o[kMaxPerThread];
+  float r[8] = {}, t[8] = {}, o[8] = {};
+  if (active) {
+    float yv[8] = {};
+    if (a.mode != 2) unpack8<DT>(ld16(a.y, static_cast<size_t>(row) * a.ldy + c0), yv);
+    if (a.mode == 1) {
 #pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    r[k] = 0.0f;
-    if (i < D) {
-      if (a.mode == 1) {
-        r[k] = ld_t<DT>(a.y, static_cast<size_t>(row) * a.ldy + i);
-      } else {
-        r[k] = res[i];
-        // residual_add: left + scale * right in f32 (scale 0.5 or 1: the
-        // product is exact, so a fused multiply-add rounds identically)
-        if (a.mode == 0) r[k] = r[k] + a.scale * ld_t<DT>(a.y, static_cast<size_t>(row) * a.ldy + i);
+      for (int k = 0; k < 8; ++k) r[k] = yv[k];
+    } else {
+      const float4 r0 = *reinterpret_cast<const float4*>(res + c0);
+      const float4 r1 = *reinterpret_cast<const float4*>(res + c0 + 4);
+      r[0] = r0.x; r[1] = r0.y; r[2] = r0.z; r[3] = r0.w;
+      r[4] = r1.x; r[5] = r1.y; r[6] = r1.z; r[7] = r1.w;
+      // residual_add: left + scale * right in f32 (scale 0.5 or 1: the
+      // product is exact, so a fused multiply-add rounds identically)
+      if (a.mode == 0) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r[k] = r[k] + a.scale * yv[k];
       }
     }
-    t[k] = round_t<DT>(r[k]);  // LayerNorm casts its f32 input to T
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t[k] = round_t<DT>(r[k]);  // LayerNorm casts its input to T
   }
-  layernorm_regs<DT>(t, o, D, a.w1, a.b1, a.eps, red);
+  layernorm8<DT>(t, o, active, c0, D, a.w1, a.b1, a.eps, red);
   const bool second = a.w2 != nullptr || a.out_kind == 1;
-  if (!second) {
-#pragma unroll
-    for (int k = 0; k < kMaxPerThread; ++k) {
-      const int i = threadIdx.x + k * kThreads;
-      if (i < D) {
-        if (a.mode != 2) res[i] = r[k];
-        st_t<DT>(a.out, static_cast<size_t>(row) * a.ldo + i, o[k]);
-      }
+  // the residual stream keeps r, or the block output o after norm_out
+  const float* keep = second ? o : r;
+  if (active && (second || a.mode != 2)) {
+    *reinterpret_cast<float4*>(res + c0) = make_float4(keep[0], keep[1], keep[2], keep[3]);
+    *reinterpret_cast<float4*>(res + c0 + 4) = make_float4(keep[4], keep[5], keep[6], keep[7]);
+  }
+  if (!second || a.out_kind == 1) {
+    if (active) st16(a.out, static_cast<size_t>(row) * a.ldo + c0, pack8<DT>(o));
+    if (a.out_kind == 1) {
+      const int prompt = a.prompt_ids[row / a.rows_per_stream];
+      for (int j = threadIdx.x; j < a.num_prompts; j += blockDim.x)
+        st_t<DT>(a.out, static_cast<size_t>(row) * a.ldo + D + j, j == prompt ? 1.0f : 0.0f);
     }
     return;
   }
-  // o is the block output (norm_out): it becomes the residual stream
-#pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    if (i < D) res[i] = o[k];
-  }
-  if (a.out_kind == 1) {
-#pragma unroll
-    for (int k = 0; k < kMaxPerThread; ++k) {
-      const int i = threadIdx.x + k * kThreads;
-      if (i < D) st_t<DT>(a.out, static_cast<size_t>(row) * a.ldo + i, o[k]);
-    }
-    const int prompt = a.prompt_ids[row / a.rows_per_stream];
-    for (int j = threadIdx.x; j < a.num_prompts; j += kThreads)
-      st_t<DT>(a.out, static_cast<size_t>(row) * a.ldo + D + j, j == prompt ? 1.0f : 0.0f);
-    return;
-  }
-  float o2[kMaxPerThread];
-  layernorm_regs<DT>(o, o2, D, a.w2, a.b2, a.eps, red);
-#pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    if (i < D) st_t<DT>(a.out, static_cast<size_t>(row) * a.ldo + i, o2[k]);
-  }
+  float o2[8] = {};
+  layernorm8<DT>(o, o2, active, c0, D, a.w2, a.b2, a.eps, red);
+  if (active) st16(a.out, static_cast<size_t>(row) * a.ldo + c0, pack8<DT>(o2));
 }
 
 // ------------------------------------------------------------------ attention
@@ -157,86 +193,140 @@ struct AttnSmem {
   float *qu, *qv, *k, *v, *r, *p;
 };
 
-__host__ __device__ inline size_t attn_floats(int Q, int vmax, int hd, AttnSmem* s, float* base) {
-  const int hdp = hd + 1;  // padded rows: row-parallel dot products hit distinct banks
+// Rows of K and R are padded to head_dim + 4 floats: 16-byte aligned rows
+// whose starts fall in different banks, so a warp's float4 reads of 32
+// consecutive rows run at the shared-memory peak.
+__host__ __device__ inline size_t attn_floats(int rows_q, int vmax, int hd, AttnSmem* s, float* base) {
+  const size_t hp = static_cast<size_t>(hd) + 4;
+  const size_t sizes[6] = {rows_q * hp, rows_q * hp, vmax * hp, static_cast<size_t>(vmax) * hd,
+                           (vmax + rows_q - 1) * hp, static_cast<size_t>(rows_q) * vmax};
   size_t off = 0;
-  auto take = [&](float** dst, size_t n) {
-    if (s != nullptr) *dst = base + off;
-    off += n;
-  };
-  float* dummy = nullptr;
-  take(s ? &s->qu : &dummy, static_cast<size_t>(Q) * hd);
-  take(s ? &s->qv : &dummy, static_cast<size_t>(Q) * hd);
-  take(s ? &s->k : &dummy, static_cast<size_t>(vmax) * hdp);
-  take(s ? &s->v : &dummy, static_cast<size_t>(vmax) * hd);
-  take(s ? &s->r : &dummy, static_cast<size_t>(vmax + Q - 1) * hdp);
-  take(s ? &s->p : &dummy, static_cast<size_t>(Q) * vmax);
+  float** dst[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  if (s != nullptr) {
+    dst[0] = &s->qu; dst[1] = &s->qv; dst[2] = &s->k; dst[3] = &s->v; dst[4] = &s->r; dst[5] = &s->p;
+  }
+  for (int i = 0; i < 6; ++i) {
+    if (s != nullptr) *dst[i] = base + off;
+    off += (sizes[i] + 3) / 4 * 4;  // keep every array 16-byte aligned
+  }
   return off;
 }
 
-// One CTA per (stream, head).  With V visible frames (cached + current) and
-// position rows ordered from V-1 down to -(V-1), the reference's relative
-// shift (pad, flatten, drop Q entries) reads raw[q][key + Q - 1 - q]; the
-// kernel reads that row directly.  Position rows depend only on the position
-// value, so one table of vmax + Q - 1 rows serves every V.
+// Copies `rows` rows of hd T values into f32 shared memory (row stride ld_s
+// floats); src(j) gives the element offset of row j.  Eight 16-byte loads are
+// in flight per thread before any store.
+template <int DT, class Src>
+__device__ __forceinline__ void stage_rows(float* dst, int ld_s, int rows, int hd, Src src) {
+  const int per_row = hd / 8;
+  const int n = rows * per_row;
+  constexpr int kBatch = 8;
+  for (int base = threadIdx.x; base < n; base += blockDim.x * kBatch) {
+    uint4 u[kBatch];
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int i = base + b * blockDim.x;
+      if (i < n) {
+        const int j = i / per_row, c = (i % per_row) * 8;
+        u[b] = *reinterpret_cast<const uint4*>(src(j) + c);
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kBatch; ++b) {
+      const int i = base + b * blockDim.x;
+      if (i < n) {
+        const int j = i / per_row, c = (i % per_row) * 8;
+        float x[8];
+        unpack8<DT>(u[b], x);
+        float4* d = reinterpret_cast<float4*>(dst + static_cast<size_t>(j) * ld_s + c);
+        d[0] = make_float4(x[0], x[1], x[2], x[3]);
+        d[1] = make_float4(x[4], x[5], x[6], x[7]);
+      }
+    }
+  }
+}
+
+// One CTA per (stream, head, query group).  With V visible frames (cached +
+// current) and position rows ordered from V-1 down to -(V-1), the reference's
+// relative shift (pad, flatten, drop Q entries) reads raw[q][key + Q - 1 - q];
+// the kernel reads that row directly.  Position rows depend only on the
+// position value, so one table of vmax + Q - 1 rows serves every V.
 template <int DT>
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
-  extern __shared__ float smem[];
-  const int s = blockIdx.x / a.heads;
-  const int h = blockIdx.x % a.heads;
-  const int hd = a.head_dim, hdp = hd + 1, Q = a.Q, D = a.D, vmax = a.vmax;
+  extern __shared__ __align__(16) float smem[];
+  const int qsplit = a.qsplit;
+  const int sh = blockIdx.x / qsplit, qg = blockIdx.x % qsplit;
+  const int s = sh / a.heads, h = sh % a.heads;
+  const int hd = a.head_dim, hp = hd + 4, Q = a.Q, D = a.D, vmax = a.vmax;
+  const int qn_max = (Q + qsplit - 1) / qsplit;
+  const int q0 = qg * qn_max;
+  const int qn = min(Q, q0 + qn_max) - q0;
   AttnSmem sm;
-  attn_floats(Q, vmax, hd, &sm, smem);
+  attn_floats(qn_max, vmax, hd, &sm, smem);
   pdl_wait();
   pdl_launch_dependents();
+  if (qn <= 0) return;
   const int n_prev = a.counters[kCtrFramesSeen];
   const int cached = min(n_prev, a.cache_frames);
   const int V = cached + Q;
   const int col = h * hd;
   const size_t row0 = static_cast<size_t>(s) * Q;
+  const uint16_t* qkv = static_cast<const uint16_t*>(a.qkv);
+  const uint16_t* kring = static_cast<const uint16_t*>(a.kring);
+  const uint16_t* vring = static_cast<const uint16_t*>(a.vring);
+  const uint16_t* relk = static_cast<const uint16_t*>(a.relk);
+  const int ring = a.ring;
+  const int ldqkv = a.ldqkv;
 
-  for (int i = threadIdx.x; i < Q * hd; i += kThreads) {
+  // keys / values: cached frames from the ring, then this chunk's projections
+  auto key_row = [&](int j) -> const uint16_t* {
+    if (j < cached) return kring + (static_cast<size_t>(s) * ring + (n_prev - cached + j) % ring) * D + col;
+    return qkv + (row0 + (j - cached)) * ldqkv + D + col;
+  };
+  auto value_row = [&](int j) -> const uint16_t* {
+    if (j < cached) return vring + (static_cast<size_t>(s) * ring + (n_prev - cached + j) % ring) * D + col;
+    return qkv + (row0 + (j - cached)) * ldqkv + 2 * D + col;
+  };
+  // position rows for queries q0..q0+qn-1: smem row i is reference row
+  // p = i + Q - q0 - qn (the smallest p these queries use), i.e. table row
+  // vmax - V + p
+  const int p_lo = Q - q0 - qn;
+  const int rbase = vmax - V + p_lo;
+  auto rel_row = [&](int i) -> const uint16_t* { return relk + static_cast<size_t>(rbase + i) * D + col; };
+  auto query_row = [&](int i) -> const uint16_t* { return qkv + (row0 + q0 + i) * ldqkv + col; };
+
+  stage_rows<DT>(sm.k, hp, V, hd, key_row);
+  stage_rows<DT>(sm.v, hd, V, hd, value_row);
+  stage_rows<DT>(sm.r, hp, V + qn - 1, hd, rel_row);
+  stage_rows<DT>(sm.qu, hp, qn, hd, query_row);
+  __syncthreads();
+  for (int i = threadIdx.x; i < qn * hd; i += blockDim.x) {
     const int q = i / hd, d = i % hd;
-    const float x = ld_t<DT>(a.qkv, (row0 + q) * a.ldqkv + col + d);
-    sm.qu[i] = x + a.bias_u[col + d];
-    sm.qv[i] = x + a.bias_v[col + d];
-  }
-  for (int i = threadIdx.x; i < V * hd; i += kThreads) {
-    const int j = i / hd, d = i % hd;
-    float kx, vx;
-    if (j < cached) {
-      const int slot = (n_prev - cached + j) % a.ring;
-      const size_t off = (static_cast<size_t>(s) * a.ring + slot) * D + col + d;
-      kx = ld_t<DT>(a.kring, off);
-      vx = ld_t<DT>(a.vring, off);
-    } else {
-      const size_t off = (row0 + (j - cached)) * a.ldqkv + col + d;
-      kx = ld_t<DT>(a.qkv, off + D);
-      vx = ld_t<DT>(a.qkv, off + 2 * static_cast<size_t>(D));
-    }
-    sm.k[j * hdp + d] = kx;
-    sm.v[j * hd + d] = vx;
-  }
-  const int np = V + Q - 1;
-  const int rbase = vmax - V;  // table row of position V-1
-  for (int i = threadIdx.x; i < np * hd; i += kThreads) {
-    const int p = i / hd, d = i % hd;
-    sm.r[p * hdp + d] = ld_t<DT>(a.relk, static_cast<size_t>(rbase + p) * D + col + d);
+    const float x = sm.qu[q * hp + d];
+    sm.qu[q * hp + d] = x + a.bias_u[col + d];
+    sm.qv[q * hp + d] = x + a.bias_v[col + d];
   }
   __syncthreads();
 
   // scores[q][key] = ((q + bias_u) . k + (q + bias_v) . rel[key + Q - 1 - q]) * scale
-  for (int pr = threadIdx.x; pr < Q * V; pr += kThreads) {
+  for (int pr = threadIdx.x; pr < qn * V; pr += blockDim.x) {
     const int q = pr / V, j = pr % V;
-    const float* qu = sm.qu + q * hd;
-    const float* qv = sm.qv + q * hd;
-    const float* kr = sm.k + j * hdp;
-    const float* rr = sm.r + (j + Q - 1 - q) * hdp;
+    const float4* qu = reinterpret_cast<const float4*>(sm.qu + q * hp);
+    const float4* qv = reinterpret_cast<const float4*>(sm.qv + q * hp);
+    const float4* kr = reinterpret_cast<const float4*>(sm.k + j * hp);
+    // reference row j + Q - 1 - (q0 + q)  ->  smem row (that) - p_lo
+    const float4* rr = reinterpret_cast<const float4*>(sm.r + (j + qn - 1 - q) * hp);
     float c = 0.0f, r = 0.0f;
 #pragma unroll 8
-    for (int d = 0; d < hd; ++d) {
-      c = fmaf(qu[d], kr[d], c);
-      r = fmaf(qv[d], rr[d], r);
+    for (int d4 = 0; d4 < hd / 4; ++d4) {
+      const float4 a4 = qu[d4], k4 = kr[d4], b4 = qv[d4], r4 = rr[d4];
+      c = fmaf(a4.x, k4.x, c);
+      c = fmaf(a4.y, k4.y, c);
+      c = fmaf(a4.z, k4.z, c);
+      c = fmaf(a4.w, k4.w, c);
+      r = fmaf(b4.x, r4.x, r);
+      r = fmaf(b4.y, r4.y, r);
+      r = fmaf(b4.z, r4.z, r);
+      r = fmaf(b4.w, r4.w, r);
     }
     sm.p[q * vmax + j] = (c + r) * a.scale;
   }
@@ -244,7 +334,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
 
   // softmax_in_place per query row (encoder.rs:278-288)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int q = warp; q < Q; q += kThreads / 32) {
+  for (int q = warp; q < qn; q += blockDim.x / 32) {
     float* row = sm.p + q * vmax;
     float m = -INFINITY;
     for (int j = lane; j < V; j += 32) m = fmaxf(m, row[j]);
@@ -262,83 +352,111 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
   }
   __syncthreads();
 
-  for (int o = threadIdx.x; o < Q * hd; o += kThreads) {
+  for (int o = threadIdx.x; o < qn * hd; o += blockDim.x) {
     const int q = o / hd, d = o % hd;
     const float* pr = sm.p + q * vmax;
     float acc = 0.0f;
     for (int j = 0; j < V; ++j) acc = fmaf(pr[j], sm.v[j * hd + d], acc);
-    st_t<DT>(a.out, (row0 + q) * D + col + d, acc);
+    st_t<DT>(a.out, (row0 + q0 + q) * D + col + d, acc);
   }
 
   // Append this chunk's keys and values to the window (AttentionKvCache::update).
-  // The ring holds cache_frames + Q frames, so these slots are not the ones read above.
-  const uint16_t* src = reinterpret_cast<const uint16_t*>(a.qkv);
-  uint16_t* kr = reinterpret_cast<uint16_t*>(a.kring);
-  uint16_t* vr = reinterpret_cast<uint16_t*>(a.vring);
-  for (int i = threadIdx.x; i < Q * hd; i += kThreads) {
-    const int t = i / hd, d = i % hd;
-    const int slot = (n_prev + t) % a.ring;
-    const size_t dst = (static_cast<size_t>(s) * a.ring + slot) * D + col + d;
-    const size_t off = (row0 + t) * a.ldqkv + col + d;
-    kr[dst] = src[off + D];
-    vr[dst] = src[off + 2 * static_cast<size_t>(D)];
+  // The ring holds cache_frames + Q frames, so these slots are not among the
+  // ones read above; the first query group of each (stream, head) writes them.
+  if (qg == 0) {
+    uint16_t* kw = static_cast<uint16_t*>(a.kring);
+    uint16_t* vw = static_cast<uint16_t*>(a.vring);
+    const int per_row = hd / 8;
+    for (int i = threadIdx.x; i < Q * per_row; i += blockDim.x) {
+      const int t = i / per_row, c = (i % per_row) * 8;
+      const size_t dst = (static_cast<size_t>(s) * ring + (n_prev + t) % ring) * D + col + c;
+      const size_t src = (row0 + t) * ldqkv + col + c;
+      st16(kw, dst, ld16(qkv, src + D));
+      st16(vw, dst, ld16(qkv, src + 2 * static_cast<size_t>(D)));
+    }
   }
 }
 
 // ------------------------------------------------------------------ conv module
 
-template <int DT>
-__global__ void __launch_bounds__(kThreads) conv_module_kernel(const ConvArgs a) {
+// One CTA per (stream, frame), eight channels per thread.  KT > 0 fixes the
+// kernel width at compile time so every tap's loads are in flight together
+// (27 16-byte loads per thread: rows up to 2048 wide keep them in registers).
+template <int DT, int KT>
+__global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const ConvArgs a) {
   __shared__ float red[32];
   pdl_wait();
   pdl_launch_dependents();
   const int row = blockIdx.x;
   const int s = row / a.Q, t = row % a.Q;
-  const int D = a.D, K = a.K, Q = a.Q;
+  const int D = a.D, Q = a.Q;
+  const int K = KT > 0 ? KT : a.K;
+  const int c0 = threadIdx.x * 8;
+  const bool active = c0 < D;
   const int par = a.counters[kCtrChunk] & 1;
   const size_t per_stream = static_cast<size_t>(K - 1) * D;
   const uint16_t* old_c =
-      reinterpret_cast<const uint16_t*>(a.cache) + (static_cast<size_t>(par) * a.S + s) * per_stream;
-  uint16_t* new_c =
-      reinterpret_cast<uint16_t*>(a.cache) + (static_cast<size_t>(1 - par) * a.S + s) * per_stream;
-  float dv[kMaxPerThread], o[kMaxPerThread];
+      static_cast<const uint16_t*>(a.cache) + (static_cast<size_t>(par) * a.S + s) * per_stream;
+  uint16_t* new_c = static_cast<uint16_t*>(a.cache) + (static_cast<size_t>(1 - par) * a.S + s) * per_stream;
+  float dv[8] = {}, o[8] = {};
+  if (active) {
+    float acc[8] = {}, g_t[8] = {};
+    constexpr int kUnroll = KT > 0 ? KT : 1;
+    for (int tap0 = 0; tap0 < K; tap0 += kUnroll) {
+      uint4 u0[kUnroll], u1[kUnroll], uw[kUnroll];
 #pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    dv[k] = 0.0f;
-    if (i < D) {
-      float acc = 0.0f, g_t = 0.0f;
-      for (int tap = 0; tap < K; ++tap) {
+      for (int i = 0; i < kUnroll; ++i) {
+        const int tap = tap0 + i;
         const int f = t - (K - 1) + tap;
-        float g;
+        uw[i] = ld16(a.dw_wt, static_cast<size_t>(tap) * D + c0);
+        if (f >= 0) {
+          const size_t off = (static_cast<size_t>(s) * Q + f) * a.ldp + c0;
+          u0[i] = ld16(a.pw1, off);
+          u1[i] = ld16(a.pw1, off + D);
+        } else {
+          u0[i] = ld16(old_c, static_cast<size_t>(K - 1 + f) * D + c0);
+          u1[i] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kUnroll; ++i) {
+        const int tap = tap0 + i;
+        const int f = t - (K - 1) + tap;
+        float x0[8], x1[8], w[8], g[8];
+        unpack8<DT>(u0[i], x0);
+        unpack8<DT>(uw[i], w);
         if (f >= 0) {
           // GLU: first / (1 + exp(-gate)) in f32, cast to T by the convolution
-          const size_t off = (static_cast<size_t>(s) * Q + f) * a.ldp;
-          const float first = ld_t<DT>(a.pw1, off + i);
-          const float gate = ld_t<DT>(a.pw1, off + D + i);
-          g = round_t<DT>(first / (1.0f + expf(-gate)));
-        } else {
-          g = ld_t<DT>(old_c, static_cast<size_t>(K - 1 + f) * D + i);
-        }
-        acc = fmaf(ld_t<DT>(a.dw_w, static_cast<size_t>(i) * K + tap), g, acc);
-        g_t = g;
-      }
-      dv[k] = round_t<DT>(round_t<DT>(acc) + ld_t<DT>(a.dw_b, i));
-      // new cache = last K-1 frames of (old cache ++ this chunk)
-      if (t >= Q - (K - 1)) st_t<DT>(new_c, static_cast<size_t>(t - Q + K - 1) * D + i, g_t);
-      if (t == 0)
-        for (int j = 0; j < K - 1 - Q; ++j)
-          new_c[static_cast<size_t>(j) * D + i] = old_c[static_cast<size_t>(Q + j) * D + i];
-    }
-  }
-  layernorm_regs<DT>(dv, o, D, a.ln_w, a.ln_b, a.eps, red);
+          unpack8<DT>(u1[i], x1);
 #pragma unroll
-  for (int k = 0; k < kMaxPerThread; ++k) {
-    const int i = threadIdx.x + k * kThreads;
-    if (i < D) {
-      const float n = o[k];
-      st_t<DT>(a.out, static_cast<size_t>(row) * D + i, n / (1.0f + expf(-n)));
+          for (int k = 0; k < 8; ++k) g[k] = round_t<DT>(x0[k] / (1.0f + expf(-x1[k])));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k) g[k] = x0[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          acc[k] = fmaf(w[k], g[k], acc[k]);
+          g_t[k] = g[k];
+        }
+      }
     }
+    float bias[8];
+    unpack8<DT>(ld16(a.dw_b, c0), bias);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dv[k] = round_t<DT>(round_t<DT>(acc[k]) + bias[k]);
+    // new cache = last K-1 frames of (old cache ++ this chunk)
+    if (t >= Q - (K - 1)) st16(new_c, static_cast<size_t>(t - Q + K - 1) * D + c0, pack8<DT>(g_t));
+    if (t == 0)
+      for (int j = 0; j < K - 1 - Q; ++j)
+        st16(new_c, static_cast<size_t>(j) * D + c0, ld16(old_c, static_cast<size_t>(Q + j) * D + c0));
+  }
+  layernorm8<DT>(dv, o, active, c0, D, a.ln_w, a.ln_b, a.eps, red);
+  if (active) {
+    float y[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y[k] = o[k] / (1.0f + expf(-o[k]));  // SiLU, cast to T for pw2
+    st16(a.out, static_cast<size_t>(row) * D + c0, pack8<DT>(y));
   }
 }
 
@@ -354,182 +472,179 @@ __device__ __forceinline__ int time_source(int jc, bool first) {
   return jc == 0 ? -1 : jc - 1;
 }
 
+// Loads a [C][9] T kernel into shared memory as f32 [9][C] plus the bias.
+template <int DT>
+__device__ __forceinline__ void stage_conv_weights(float* wt, float* bias, const void* w,
+                                                   const void* b, int C) {
+  for (int i = threadIdx.x; i < C * 9; i += blockDim.x) {
+    const int c = i / 9, tap = i % 9;
+    wt[tap * C + c] = ld_t<DT>(w, i);
+  }
+  for (int c = threadIdx.x; c < C; c += blockDim.x) bias[c] = ld_t<DT>(b, c);
+}
+
+// One CTA per (output frame, stream).  The three input frames it reads are
+// staged (rounded to T, frequency zero-padded 2 left and 1 right) in shared
+// memory; each thread then produces eight channels of one frequency bin.
 template <int DT>
 __global__ void __launch_bounds__(kThreads) stem_conv_kernel(const Conv2dArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  const int t = blockIdx.x, s = blockIdx.y;
+  const int C = a.C, Fin = a.Fin, Fp = Fin + 3;
+  float* wt = smem;               // [9][C]
+  float* bias = wt + 9 * C;       // [C]
+  float* xs = bias + C;           // [3][Fp]
+  stage_conv_weights<DT>(wt, bias, a.w, a.b, C);
   pdl_wait();
   pdl_launch_dependents();
   const int chunk = a.counters[kCtrChunk];
   const bool first = chunk == 0;
   const int par = chunk & 1;
-  const int CG = a.C / 8;
   const float* mel = static_cast<const float*>(a.in);
-  const size_t total = static_cast<size_t>(a.S) * a.Tout * a.Fout * CG;
-  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += stride) {
-    const int cg = static_cast<int>(idx % CG);
-    size_t rest = idx / CG;
-    const int f = static_cast<int>(rest % a.Fout);
-    rest /= a.Fout;
-    const int t = static_cast<int>(rest % a.Tout);
-    const int s = static_cast<int>(rest / a.Tout);
-    float x[9];
+  for (int i = threadIdx.x; i < 3 * Fp; i += blockDim.x) {
+    const int kt = i / Fp, pb = i % Fp, bin = pb - 2;
+    const int src = time_source(2 * t + kt, first);
+    float v = 0.0f;
+    if (src != -2 && bin >= 0 && bin < Fin) {
+      if (src == -1) v = ld_t<DT>(a.cache, (static_cast<size_t>(par) * a.S + s) * Fin + bin);
+      else if (src < a.valid_in) v = round_t<DT>(mel[(static_cast<size_t>(s) * a.Tin + src) * Fin + bin]);
+    }
+    xs[i] = v;
+  }
+  __syncthreads();
+  const int CG = C / 8;
+  const bool masked = t >= a.valid_out;  // mask_invalid_time, then ReLU
+  for (int item = threadIdx.x; item < a.Fout * CG; item += blockDim.x) {
+    const int f = item / CG, c0 = (item % CG) * 8;
+    float acc[8] = {};
 #pragma unroll
     for (int kt = 0; kt < 3; ++kt) {
-      const int src = time_source(2 * t + kt, first);
 #pragma unroll
       for (int kf = 0; kf < 3; ++kf) {
-        const int bin = 2 * f + kf - 2;  // frequency padded 2 left, 1 right
-        float v = 0.0f;
-        if (src != -2 && bin >= 0 && bin < a.Fin) {
-          if (src == -1) {
-            v = ld_t<DT>(a.cache, (static_cast<size_t>(par) * a.S + s) * a.Fin + bin);
-          } else if (src < a.valid_in) {
-            v = round_t<DT>(mel[(static_cast<size_t>(s) * a.Tin + src) * a.Fin + bin]);
-          }
-        }
-        x[kt * 3 + kf] = v;
+        const float x = xs[kt * Fp + 2 * f + kf];
+        const float4 w0 = *reinterpret_cast<const float4*>(wt + (kt * 3 + kf) * C + c0);
+        const float4 w1 = *reinterpret_cast<const float4*>(wt + (kt * 3 + kf) * C + c0 + 4);
+        acc[0] = fmaf(w0.x, x, acc[0]);
+        acc[1] = fmaf(w0.y, x, acc[1]);
+        acc[2] = fmaf(w0.z, x, acc[2]);
+        acc[3] = fmaf(w0.w, x, acc[3]);
+        acc[4] = fmaf(w1.x, x, acc[4]);
+        acc[5] = fmaf(w1.y, x, acc[5]);
+        acc[6] = fmaf(w1.z, x, acc[6]);
+        acc[7] = fmaf(w1.w, x, acc[7]);
       }
     }
-    const int c0 = cg * 8;
-    uint16_t packed[8];
+    float o[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      float acc = 0.0f;
-#pragma unroll
-      for (int tap = 0; tap < 9; ++tap)
-        acc = fmaf(ld_t<DT>(a.w, static_cast<size_t>(c0 + c) * 9 + tap), x[tap], acc);
-      float o = round_t<DT>(round_t<DT>(acc) + ld_t<DT>(a.b, c0 + c));
-      if (t >= a.valid_out) o = 0.0f;  // mask_invalid_time, then ReLU
-      o = o > 0.0f ? o : 0.0f;
-      if constexpr (DT == kBF16) packed[c] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
-      else packed[c] = __half_as_ushort(__float2half_rn(o));
+    for (int k = 0; k < 8; ++k) {
+      const float v = round_t<DT>(round_t<DT>(acc[k]) + bias[c0 + k]);
+      o[k] = masked ? 0.0f : fmaxf(v, 0.0f);
     }
-    uint4 w;
-    w.x = packed[0] | (static_cast<uint32_t>(packed[1]) << 16);
-    w.y = packed[2] | (static_cast<uint32_t>(packed[3]) << 16);
-    w.z = packed[4] | (static_cast<uint32_t>(packed[5]) << 16);
-    w.w = packed[6] | (static_cast<uint32_t>(packed[7]) << 16);
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) +
-                              ((static_cast<size_t>(s) * a.Tout + t) * a.Fout + f) * a.C + c0) = w;
+    st16(a.out, ((static_cast<size_t>(s) * a.Tout + t) * a.Fout + f) * C + c0, pack8<DT>(o));
   }
-  // next chunk's cache: the last input frame
-  const size_t ncache = static_cast<size_t>(a.S) * a.Fin;
-  for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < ncache;
-       idx += stride) {
-    const int s = static_cast<int>(idx / a.Fin), bin = static_cast<int>(idx % a.Fin);
+  // the next chunk's cache: the last input frame
+  if (t == 0) {
     const int fr = a.Tin - 1;
-    const float v = fr < a.valid_in ? round_t<DT>(mel[(static_cast<size_t>(s) * a.Tin + fr) * a.Fin + bin]) : 0.0f;
-    st_t<DT>(a.cache, (static_cast<size_t>(1 - par) * a.S + s) * a.Fin + bin, v);
-  }
-}
-
-__device__ __forceinline__ void unpack8(const uint4& u, float (&x)[8], int DT) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint16_t lo = static_cast<uint16_t>(w[i] & 0xFFFFu), hi = static_cast<uint16_t>(w[i] >> 16);
-    if (DT == kBF16) {
-      x[2 * i] = __uint_as_float(static_cast<uint32_t>(lo) << 16);
-      x[2 * i + 1] = __uint_as_float(static_cast<uint32_t>(hi) << 16);
-    } else {
-      x[2 * i] = __half2float(__ushort_as_half(lo));
-      x[2 * i + 1] = __half2float(__ushort_as_half(hi));
+    for (int bin = threadIdx.x; bin < Fin; bin += blockDim.x) {
+      const float v = fr < a.valid_in ? round_t<DT>(mel[(static_cast<size_t>(s) * a.Tin + fr) * Fin + bin]) : 0.0f;
+      st_t<DT>(a.cache, (static_cast<size_t>(1 - par) * a.S + s) * Fin + bin, v);
     }
   }
 }
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads) depthwise_conv2d_kernel(const Conv2dArgs a) {
+  extern __shared__ __align__(16) float smem[];
+  const int t = blockIdx.x, s = blockIdx.y;
+  const int C = a.C, CG = C / 8;
+  float* wt = smem;          // [9][C]
+  float* bias = wt + 9 * C;  // [C]
+  stage_conv_weights<DT>(wt, bias, a.w, a.b, C);
   pdl_wait();
   pdl_launch_dependents();
   const int chunk = a.counters[kCtrChunk];
   const bool first = chunk == 0;
   const int par = chunk & 1;
-  const int C = a.C, CG = C / 8;
   const uint16_t* in = static_cast<const uint16_t*>(a.in);
   uint16_t* cache = static_cast<uint16_t*>(a.cache);
-  const size_t total = static_cast<size_t>(a.S) * a.Tout * a.Fout * CG;
-  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
-  for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
-       idx += stride) {
-    const int cg = static_cast<int>(idx % CG);
-    size_t rest = idx / CG;
-    const int f = static_cast<int>(rest % a.Fout);
-    rest /= a.Fout;
-    const int t = static_cast<int>(rest % a.Tout);
-    const int s = static_cast<int>(rest / a.Tout);
-    const int c0 = cg * 8;
-    float acc[8];
+  int src[3];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = 0.0f;
+  for (int kt = 0; kt < 3; ++kt) {
+    src[kt] = time_source(2 * t + kt, first);
+    if (src[kt] >= a.valid_in) src[kt] = -2;  // masked input frames read as zero
+  }
+  __syncthreads();
+  for (int item = threadIdx.x; item < a.Fout * CG; item += blockDim.x) {
+    const int f = item / CG, c0 = (item % CG) * 8;
+    uint4 u[9];
 #pragma unroll
     for (int kt = 0; kt < 3; ++kt) {
-      const int src = time_source(2 * t + kt, first);
 #pragma unroll
       for (int kf = 0; kf < 3; ++kf) {
         const int bin = 2 * f + kf - 2;
-        if (src == -2 || bin < 0 || bin >= a.Fin) continue;
-        const uint16_t* p;
-        if (src == -1) {
-          p = cache + ((static_cast<size_t>(par) * a.S + s) * a.Fin + bin) * C + c0;
-        } else if (src < a.valid_in) {
-          p = in + ((static_cast<size_t>(s) * a.Tin + src) * a.Fin + bin) * C + c0;
-        } else {
-          continue;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (src[kt] != -2 && bin >= 0 && bin < a.Fin) {
+          if (src[kt] == -1) v = ld16(cache, ((static_cast<size_t>(par) * a.S + s) * a.Fin + bin) * C + c0);
+          else v = ld16(in, ((static_cast<size_t>(s) * a.Tin + src[kt]) * a.Fin + bin) * C + c0);
         }
-        float x[8];
-        unpack8(*reinterpret_cast<const uint4*>(p), x, DT);
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          acc[c] = fmaf(ld_t<DT>(a.w, static_cast<size_t>(c0 + c) * 9 + kt * 3 + kf), x[c], acc[c]);
+        u[kt * 3 + kf] = v;
       }
     }
-    uint16_t packed[8];
+    float acc[8] = {};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const float o = round_t<DT>(round_t<DT>(acc[c]) + ld_t<DT>(a.b, c0 + c));
-      if constexpr (DT == kBF16) packed[c] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
-      else packed[c] = __half_as_ushort(__float2half_rn(o));
+    for (int tap = 0; tap < 9; ++tap) {
+      float x[8];
+      unpack8<DT>(u[tap], x);
+      const float4 w0 = *reinterpret_cast<const float4*>(wt + tap * C + c0);
+      const float4 w1 = *reinterpret_cast<const float4*>(wt + tap * C + c0 + 4);
+      acc[0] = fmaf(w0.x, x[0], acc[0]);
+      acc[1] = fmaf(w0.y, x[1], acc[1]);
+      acc[2] = fmaf(w0.z, x[2], acc[2]);
+      acc[3] = fmaf(w0.w, x[3], acc[3]);
+      acc[4] = fmaf(w1.x, x[4], acc[4]);
+      acc[5] = fmaf(w1.y, x[5], acc[5]);
+      acc[6] = fmaf(w1.z, x[6], acc[6]);
+      acc[7] = fmaf(w1.w, x[7], acc[7]);
     }
-    uint4 w;
-    w.x = packed[0] | (static_cast<uint32_t>(packed[1]) << 16);
-    w.y = packed[2] | (static_cast<uint32_t>(packed[3]) << 16);
-    w.z = packed[4] | (static_cast<uint32_t>(packed[5]) << 16);
-    w.w = packed[6] | (static_cast<uint32_t>(packed[7]) << 16);
-    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) +
-                              ((static_cast<size_t>(s) * a.Tout + t) * a.Fout + f) * C + c0) = w;
+    float o[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = round_t<DT>(round_t<DT>(acc[k]) + bias[c0 + k]);
+    st16(a.out, ((static_cast<size_t>(s) * a.Tout + t) * a.Fout + f) * C + c0, pack8<DT>(o));
   }
-  // next chunk's cache: the last input frame (zero if masked)
-  const size_t ncache = static_cast<size_t>(a.S) * a.Fin * CG;
-  for (size_t idx = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < ncache;
-       idx += stride) {
-    const int cg = static_cast<int>(idx % CG);
-    const size_t sb = idx / CG;  // s * Fin + bin
-    const int s = static_cast<int>(sb / a.Fin), bin = static_cast<int>(sb % a.Fin);
+  // the next chunk's cache: the last input frame (zero if masked)
+  if (t == 0) {
     const int fr = a.Tin - 1;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (fr < a.valid_in)
-      v = *reinterpret_cast<const uint4*>(in + ((static_cast<size_t>(s) * a.Tin + fr) * a.Fin + bin) * C +
-                                          cg * 8);
-    *reinterpret_cast<uint4*>(cache + ((static_cast<size_t>(1 - par) * a.S + s) * a.Fin + bin) * C +
-                              cg * 8) = v;
+    for (int i = threadIdx.x; i < a.Fin * CG; i += blockDim.x) {
+      const int bin = i / CG, c0 = (i % CG) * 8;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (fr < a.valid_in) v = ld16(in, ((static_cast<size_t>(s) * a.Tin + fr) * a.Fin + bin) * C + c0);
+      st16(cache, ((static_cast<size_t>(1 - par) * a.S + s) * a.Fin + bin) * C + c0, v);
+    }
   }
 }
 
+// One CTA per output row (stream, frame): [F][C] of the input row -> [C][F].
+// Tile rows are padded by 8 elements (16 bytes) so the transposed reads of
+// consecutive frequency bins fall in different banks.
 __global__ void __launch_bounds__(kThreads)
-    flatten_cf_kernel(const uint16_t* in, uint16_t* out, int S, int T, int F, int C, int valid) {
+    flatten_cf_kernel(const uint16_t* in, uint16_t* out, int T, int F, int C, int valid) {
+  extern __shared__ __align__(16) uint16_t tile[];  // [F][C + 8]
   pdl_wait();
   pdl_launch_dependents();
-  const size_t width = static_cast<size_t>(C) * F;
-  const size_t total = static_cast<size_t>(S) * T * width;
-  for (size_t o = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; o < total;
-       o += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t row = o / width;
-    const int col = static_cast<int>(o % width);
-    const int c = col / F, f = col % F;
-    const int t = static_cast<int>(row % T);
-    out[o] = t < valid ? in[(row * F + f) * C + c] : static_cast<uint16_t>(0);
+  const size_t row = blockIdx.x;
+  const int t = static_cast<int>(row % T);
+  const int n = F * C, ld = C + 8;
+  const uint16_t* src = in + row * n;
+  for (int i = threadIdx.x * 8; i < n; i += blockDim.x * 8) {
+    const int f = i / C, c = i % C;
+    *reinterpret_cast<uint4*>(tile + f * ld + c) =
+        t < valid ? *reinterpret_cast<const uint4*>(src + i) : make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+  uint16_t* dst = out + row * n;
+  for (int o = threadIdx.x; o < n; o += blockDim.x) {
+    const int c = o / F, f = o % F;
+    dst[o] = tile[f * ld + c];
   }
 }
 
@@ -564,53 +679,80 @@ int grid_for(size_t work) {
   return static_cast<int>(blocks < 148 * 16 ? (blocks == 0 ? 1 : blocks) : 148 * 16);
 }
 
+template <class K>
+cudaError_t allow_smem(K kern, size_t bytes) {
+  if (bytes <= 48 * 1024) return cudaSuccess;
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+}
+
 }  // namespace
 
 cudaError_t launch_layernorm(int dtype, const LnArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.D > kMaxPerThread * kThreads || a.rows <= 0) return cudaErrorInvalidValue;
+  if (a.D % 8 != 0 || a.D > 8192 || a.rows <= 0 || a.ldy % 8 != 0 || a.ldo % 8 != 0)
+    return cudaErrorInvalidValue;
   auto k = dtype == kBF16 ? layernorm_kernel<kBF16> : layernorm_kernel<kF16>;
-  return launch_ex(k, dim3(a.rows), dim3(kThreads), 0, stream, pdl, a);
+  return launch_ex(k, dim3(a.rows), dim3(row_threads(a.D)), 0, stream, pdl, a);
 }
 
-size_t attention_smem_bytes(int Q, int vmax, int head_dim) {
-  return attn_floats(Q, vmax, head_dim, nullptr, nullptr) * sizeof(float);
+size_t attention_smem_bytes(int rows_q, int vmax, int head_dim) {
+  return attn_floats(rows_q, vmax, head_dim, nullptr, nullptr) * sizeof(float);
+}
+
+int attention_qsplit(int streams, int heads, int Q, int num_sms) {
+  const int ctas = streams * heads;
+  if (ctas >= num_sms) return 1;
+  const int want = (2 * num_sms + ctas - 1) / ctas;
+  return want < Q ? want : Q;
 }
 
 cudaError_t launch_attention(int dtype, const AttnArgs& a, cudaStream_t stream, bool pdl) {
-  const size_t smem = attention_smem_bytes(a.Q, a.vmax, a.head_dim);
+  if (a.head_dim % 8 != 0 || a.D % 8 != 0 || a.ldqkv % 8 != 0 || a.qsplit < 1) return cudaErrorInvalidValue;
+  const int qn = (a.Q + a.qsplit - 1) / a.qsplit;
+  const size_t smem = attention_smem_bytes(qn, a.vmax, a.head_dim);
   auto k = dtype == kBF16 ? attention_kernel<kBF16> : attention_kernel<kF16>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
+  cudaError_t e = allow_smem(k, smem);
   if (e != cudaSuccess) return e;
-  return launch_ex(k, dim3(a.S * a.heads), dim3(kThreads), smem, stream, pdl, a);
+  return launch_ex(k, dim3(a.S * a.heads * a.qsplit), dim3(kThreads), smem, stream, pdl, a);
 }
 
 cudaError_t launch_conv_module(int dtype, const ConvArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.D > kMaxPerThread * kThreads) return cudaErrorInvalidValue;
-  auto k = dtype == kBF16 ? conv_module_kernel<kBF16> : conv_module_kernel<kF16>;
-  return launch_ex(k, dim3(a.S * a.Q), dim3(kThreads), 0, stream, pdl, a);
+  if (a.D % 8 != 0 || a.D > 8192 || a.ldp % 8 != 0 || a.K < 2) return cudaErrorInvalidValue;
+  const dim3 grid(a.S * a.Q), block(row_threads(a.D));
+  if (a.K == 9 && a.D <= 2048) {
+    auto k = dtype == kBF16 ? conv_module_kernel<kBF16, 9> : conv_module_kernel<kF16, 9>;
+    return launch_ex(k, grid, block, 0, stream, pdl, a);
+  }
+  auto k = dtype == kBF16 ? conv_module_kernel<kBF16, 0> : conv_module_kernel<kF16, 0>;
+  return launch_ex(k, grid, block, 0, stream, pdl, a);
 }
 
 cudaError_t launch_stem_conv(int dtype, const Conv2dArgs& a, cudaStream_t stream, bool pdl) {
   if (a.C % 8) return cudaErrorInvalidValue;
   auto k = dtype == kBF16 ? stem_conv_kernel<kBF16> : stem_conv_kernel<kF16>;
-  const size_t work = static_cast<size_t>(a.S) * a.Tout * a.Fout * (a.C / 8);
-  return launch_ex(k, dim3(grid_for(work)), dim3(kThreads), 0, stream, pdl, a);
+  const size_t smem = (static_cast<size_t>(10) * a.C + 3 * (a.Fin + 3) + 4) * sizeof(float);
+  cudaError_t e = allow_smem(k, smem);
+  if (e != cudaSuccess) return e;
+  return launch_ex(k, dim3(a.Tout, a.S), dim3(kThreads), smem, stream, pdl, a);
 }
 
 cudaError_t launch_depthwise_conv2d(int dtype, const Conv2dArgs& a, cudaStream_t stream, bool pdl) {
   if (a.C % 8) return cudaErrorInvalidValue;
   auto k = dtype == kBF16 ? depthwise_conv2d_kernel<kBF16> : depthwise_conv2d_kernel<kF16>;
-  const size_t work = static_cast<size_t>(a.S) * a.Tout * a.Fout * (a.C / 8);
-  return launch_ex(k, dim3(grid_for(work)), dim3(kThreads), 0, stream, pdl, a);
+  const size_t smem = static_cast<size_t>(10) * a.C * sizeof(float);
+  cudaError_t e = allow_smem(k, smem);
+  if (e != cudaSuccess) return e;
+  return launch_ex(k, dim3(a.Tout, a.S), dim3(kThreads), smem, stream, pdl, a);
 }
 
 cudaError_t launch_flatten_cf(int dtype, const void* in, void* out, int S, int T, int F, int C,
                               int valid, cudaStream_t stream, bool pdl) {
-  (void)dtype;  // a 16-bit copy: the element type does not matter
-  const size_t work = static_cast<size_t>(S) * T * F * C;
-  return launch_ex(flatten_cf_kernel, dim3(grid_for(work)), dim3(kThreads), 0, stream, pdl,
-                   static_cast<const uint16_t*>(in), static_cast<uint16_t*>(out), S, T, F, C, valid);
+  (void)dtype;  // a 16-bit permutation: the element type does not matter
+  if (C % 8 != 0) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(F) * (C + 8) * 2;
+  cudaError_t e = allow_smem(flatten_cf_kernel, smem);
+  if (e != cudaSuccess) return e;
+  return launch_ex(flatten_cf_kernel, dim3(S * T), dim3(kThreads), smem, stream, pdl,
+                   static_cast<const uint16_t*>(in), static_cast<uint16_t*>(out), T, F, C, valid);
 }
 
 cudaError_t launch_advance_counters(int* counters, int frames, cudaStream_t stream, bool pdl) {

@@ -59,9 +59,14 @@ struct AttnArgs {
   void* out;             // [S*Q, D] T
   const int* counters;
   int S, Q, D, heads, head_dim, ring, cache_frames, vmax;
+  int qsplit;  // CTAs per (stream, head), each taking ceil(Q / qsplit) queries
   float scale;
 };
-size_t attention_smem_bytes(int Q, int vmax, int head_dim);
+// Dynamic shared memory of one attention CTA holding `rows_q` queries.
+size_t attention_smem_bytes(int rows_q, int vmax, int head_dim);
+// Query split that fills the GPU: one CTA per (stream, head) when there are
+// enough of them, otherwise up to one CTA per query.
+int attention_qsplit(int streams, int heads, int Q, int num_sms);
 cudaError_t launch_attention(int dtype, const AttnArgs& a, cudaStream_t stream, bool pdl);
 
 // Conformer convolution core: GLU -> causal depthwise conv (K taps, cache of
@@ -69,7 +74,7 @@ cudaError_t launch_attention(int dtype, const AttnArgs& a, cudaStream_t stream, 
 struct ConvArgs {
   const void* pw1;  // [S*Q, 2D] T
   int ldp;
-  const void* dw_w;  // [D][K] T
+  const void* dw_wt;  // [K][D] T (the artifact's [D, 1, K] kernel transposed)
   const void* dw_b;  // [D] T
   const void* ln_w;
   const void* ln_b;

@@ -349,32 +349,64 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // bf16 -> f16 activations with a per-row power-of-two scale: the row maximum
-// lands in [2^14, 2^15); row_scale[m] = 2^e undoes it in the epilogue.
-__global__ void __launch_bounds__(256)
+// lands in [2^14, 2^15); row_scale[m] = 2^e undoes it in the epilogue.  One
+// CTA per row; each thread keeps up to kPrepassChunks 16-byte chunks of the
+// row in registers, so the row is read once with all loads in flight.
+constexpr int kPrepassThreads = 128;
+constexpr int kPrepassChunks = 8;  // rows up to 128 * 8 * 8 = 8192 wide
+
+__global__ void __launch_bounds__(kPrepassThreads)
     qgemm_prepass_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int M, int K,
                          __half* __restrict__ xo, int ldo, float* __restrict__ row_scale) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
   if (m >= M) return;
-  const __nv_bfloat16* xr = x + static_cast<size_t>(m) * ldx;
+  const uint16_t* xr = reinterpret_cast<const uint16_t*>(x) + static_cast<size_t>(m) * ldx;
+  uint4 u[kPrepassChunks];
   float amax = 0.f;
-  for (int k = threadIdx.x; k < K; k += blockDim.x) amax = fmaxf(amax, fabsf(__bfloat162float(xr[k])));
-  __shared__ float red[8];
+#pragma unroll
+  for (int i = 0; i < kPrepassChunks; ++i) {
+    const int k = (threadIdx.x + i * kPrepassThreads) * 8;
+    if (k < K) {
+      u[i] = *reinterpret_cast<const uint4*>(xr + k);
+      const uint32_t w[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        amax = fmaxf(amax, fabsf(__uint_as_float(w[j] << 16)));
+        amax = fmaxf(amax, fabsf(__uint_as_float(w[j] & 0xFFFF0000u)));
+      }
+    }
+  }
+  __shared__ float red[kPrepassThreads / 32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = 0.f;
-  for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) amax = fmaxf(amax, red[w]);
+#pragma unroll
+  for (int w = 0; w < kPrepassThreads / 32; ++w) amax = fmaxf(amax, red[w]);
   const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
   int sh = e == 0 ? 0 : 141 - e;
   sh = max(-126, min(126, sh));
   const float scale = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
   if (threadIdx.x == 0) row_scale[m] = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-  __half* orow = xo + static_cast<size_t>(m) * ldo;
-  for (int k = threadIdx.x; k < K; k += blockDim.x)
-    orow[k] = __float2half_rn(__bfloat162float(xr[k]) * scale);
+  uint16_t* orow = reinterpret_cast<uint16_t*>(xo) + static_cast<size_t>(m) * ldo;
+#pragma unroll
+  for (int i = 0; i < kPrepassChunks; ++i) {
+    const int k = (threadIdx.x + i * kPrepassThreads) * 8;
+    if (k < K) {
+      const uint32_t w[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint16_t lo = __half_as_ushort(__float2half_rn(__uint_as_float(w[j] << 16) * scale));
+        const uint16_t hi = __half_as_ushort(__float2half_rn(__uint_as_float(w[j] & 0xFFFF0000u) * scale));
+        o[j] = lo | (static_cast<uint32_t>(hi) << 16);
+      }
+      *reinterpret_cast<uint4*>(orow + k) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
 }
 
 template <int DT, int G, int BN>
@@ -430,9 +462,11 @@ cudaError_t launch_gemm(int dtype, int group, const CUtensorMap& amap, const CUt
 cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, int ldo,
                                 float* row_scale, cudaStream_t stream, bool pdl) {
   if (M == 0) return cudaSuccess;
+  if (K % 8 != 0 || K > kPrepassThreads * kPrepassChunks * 8 || ldx % 8 != 0 || ldo % 8 != 0)
+    return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(M, 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
+  cfg.blockDim = dim3(kPrepassThreads, 1, 1);
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
