@@ -241,6 +241,138 @@ LINEAR_WORKLOAD = ("single INT8 affine quantized linear x bf16 [14,1024] . W[409
                    "group 64, 40 independent back-to-back launches over distinct weight copies")
 
 
+CHUNK_MEL = 112          # log-mel frames per chunk (lookahead 13: 8 * (13 + 1))
+CHUNK_AUDIO_S = 1.12     # 112 frames at the 10 ms hop
+ENC_STREAMS = 64         # concurrent streams per GPU (64 x 14 = 896 rows per linear)
+
+
+def encoder_flops_per_chunk(streams: int) -> int:
+    """Algorithmic FLOPs (2 * rows * N * K) of every quantized linear in one
+    chunk of `streams` streams: 24 blocks, subsampling and prompt projector.
+    The position projection (83 rows) is shared by the streams of a state."""
+    q = 14
+    block = (2 * 4096 * 1024 * 2 + 3072 * 1024 + 1024 * 1024 + 2048 * 1024 + 1024 * 1024)
+    f = streams * q * block * N_BLOCKS
+    f += (56 + 14 + 14 - 1) * 1024 * 1024 * N_BLOCKS  # relative_k_proj
+    f += streams * (28 * 33 * 256 * 256 + 14 * 17 * 256 * 256 + q * 4352 * 1024)
+    f += streams * q * (1152 * 2048 + 2048 * 1024)
+    return 2 * f
+
+
+def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: int,
+                  chunks: int, with_e2e: bool = True) -> dict:
+    """Streaming encoder (subsampling + 24 FastConformer blocks + prompt
+    projector) over `streams` lock-step streams, one 112-frame chunk per step,
+    through the C ABI (cq_encoder_encode_chunk replays one CUDA graph per chunk)."""
+    from nemotron_cuda.encoder import Encoder
+    enc = Encoder.random(None, seed=7, dtype="bf16", device=local_rank)
+    st = enc.state(streams, CHUNK_MEL)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(11 + local_rank)
+    mel = torch.randn((streams, CHUNK_MEL, 128), generator=gen, device="cuda")
+    out = st.encode_chunk(mel)  # first chunk (eager; later chunks replay a graph)
+    stream = torch.cuda.Stream()
+    host_mel = torch.empty(tuple(mel.shape), dtype=torch.float32).pin_memory()
+    host_mel.copy_(mel.cpu())
+    host_out = torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory()
+    torch.cuda.synchronize()
+
+    def run(n: int, e2e: bool) -> None:
+        for _ in range(n):
+            if e2e:
+                mel.copy_(host_mel, non_blocking=True)
+            st.encode_chunk(mel, out, stream=stream)
+            if e2e:
+                host_out.copy_(out, non_blocking=True)
+
+    def timed(e2e: bool) -> float:
+        with torch.cuda.stream(stream):
+            run(args.warmup, e2e)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s.record(stream)
+            run(chunks, e2e)
+            e.record(stream)
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    ms = timed(False)
+    clock_info = clocks.stop()
+    ms_e2e = timed(True) if with_e2e else None
+    kernels = st.kernels_per_chunk
+    status = cq.device_status(local_rank)
+    if status != 0:
+        raise RuntimeError(f"device watchdog reported status {status}")
+    per_chunk = ms / chunks
+    audio = world * streams * CHUNK_AUDIO_S * chunks
+    flops = encoder_flops_per_chunk(streams)
+    tpeak, tkind = measured_tensor_peak()
+    tflops = flops / (per_chunk * 1e-3) / 1e12
+    res = {
+        "metric": "encoder audio-sec/sec", "value": round(audio / (ms * 1e-3), 1),
+        "unit": "audio-s/s", "streams_per_gpu": streams, "chunks": chunks,
+        "ms_per_chunk": round(per_chunk, 4), "chunk_audio_s": CHUNK_AUDIO_S,
+        "workload": (f"streaming FastConformer encoder (Conv2D subsampling, 24 blocks d=1024 "
+                     f"ff=4096 8 heads, attention window 56+14 frames, conv kernel 9 cache, "
+                     f"prompt projector), {streams} lock-step streams per GPU, 112 log-mel frames "
+                     f"x 128 bins per chunk, random-init INT8 group 64 bf16"),
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": tpeak,
+                     "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4),
+                     "peak_kind": f"{tkind} dense bf16 (sustained)",
+                     "note": "linear FLOPs of the whole chunk / chunk time (lower bound on "
+                             "the GEMMs' own rate)"},
+        "clocks": clock_info,
+        "gpu_launches": kernels * chunks, "kernels_per_chunk": kernels,
+    }
+    if ms_e2e is not None:
+        res["e2e"] = {"value": round(audio / (ms_e2e * 1e-3), 1), "unit": "audio-s/s",
+                      "h2d_bytes_per_step": host_mel.numel() * 4,
+                      "d2h_bytes_per_step": host_out.numel() * 2,
+                      "path": "pinned host log-mel -> device, cq_encoder_encode_chunk, encoder "
+                              "output -> pinned host, every chunk inside the timed region"}
+    del st, enc
+    return res
+
+
+def cpu_encoder_baseline(target_s: float = 8.0) -> dict:
+    """The CPU restatement of the encoder (oracle/encoder_oracle.py, numpy +
+    the OpenMP C linear) on one stream: a bounded sample of chunks."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import encoder_oracle as eo
+    import oracle
+    cfg = eo.EncoderConfig()
+    params = eo.random_params(cfg, 3, "bf16")
+    enc = eo.Encoder(cfg, params, "bf16")
+    cache = enc.new_cache()
+    rng = np.random.default_rng(0)
+    mel = rng.standard_normal((CHUNK_MEL, 128)).astype(np.float32)
+    enc.encode_chunk(mel, 101, cache)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        enc.encode_chunk(mel, 101, cache)
+        n += 1
+        if time.perf_counter() - t0 >= target_s and n >= 2:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(n * CHUNK_AUDIO_S / dt, 3), "unit": "audio-s/s",
+            "cores": oracle.max_threads(), "kind": "port",
+            "sample": f"{n} chunks of one stream (112 mel frames each), {dt:.1f} s, numpy + "
+                      f"OpenMP C restatement of the streaming encoder (oracle/)"}
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     import torch
     import nemotron_cuda as cq
@@ -251,6 +383,25 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+    if args.workload == "encoder":
+        res = bench_encoder(torch, cq, args, world, local_rank, dist, args.streams, args.steps)
+        if dist:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        line = {"metric": METRIC, "value": res["value"], "unit": res["unit"], "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": res["ms_per_chunk"],
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init INT8 weights quantised on device; log-mel ~ N(0,1))",
+                "config": {"workload": res["workload"], "group_size": GROUP,
+                           "streams_per_gpu": args.streams,
+                           "parallelism": f"dp{world} (replicated weights, independent streams)",
+                           "l2": "inputs larger than L2 (640 MB of weights per chunk)"},
+                "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
+                "gpu_launches": res["gpu_launches"]}
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds)
+        return line
     step_flops = None
     if args.workload == "linear":
         enc = SingleLinear(torch, cq, local_rank)
@@ -317,6 +468,14 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     status = cq.device_status(local_rank)
 
     del graph, graph_e2e
+    encoder = None
+    if args.workload == "block" and not args.no_encoder:
+        encoder = bench_encoder(torch, cq, args, world, local_rank, dist, ENC_STREAMS,
+                                args.encoder_chunks)
+        encoder["batch1"] = bench_encoder(torch, cq, args, world, local_rank, dist, 1,
+                                          args.encoder_chunks, with_e2e=False)
+        for k in ("clocks",):
+            encoder["batch1"].pop(k, None)
     if dist:
         dist.destroy_process_group()
     if rank != 0:
@@ -366,6 +525,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         line["tflops"] = round(step_flops / (ms_step * 1e-3) / 1e12 * world, 2)
     if world == 1 and not args.no_cpu_baseline and args.workload != "batched":
         line["cpu_baseline"] = cpu_baseline(target_s=args.cpu_seconds, workload=args.workload)
+    if encoder is not None:
+        if world == 1 and not args.no_cpu_baseline:
+            encoder["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds)
+        line["encoder"] = encoder
     return line
 
 
@@ -433,7 +596,9 @@ def run_reference(args, rank: int) -> dict | None:
         ob.run_block(i)
     dt = time.perf_counter() - t0
     value = args.steps * reps * ob.bytes / dt / 1e9
+    enc = None if args.no_encoder else cpu_encoder_baseline(args.cpu_seconds)
     return {
+        "encoder": enc,
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
@@ -457,10 +622,19 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "linear", "batched"], default="block",
-                    help="block: the 24-block M=14 linear chain (default); linear: one "
-                         "4096x1024 linear, independent back-to-back launches; batched: the "
-                         "24-block chain at M=896 (64 streams), tensor-core path")
+    ap.add_argument("--workload", choices=["block", "linear", "batched", "encoder"],
+                    default="block",
+                    help="block: the 24-block M=14 linear chain (default, plus the full "
+                         "encoder at 64 streams and at 1 stream as the line's 'encoder' "
+                         "object); linear: one 4096x1024 linear, independent back-to-back "
+                         "launches; batched: the 24-block chain at M=896 (64 streams), "
+                         "tensor-core path; encoder: the full streaming encoder alone "
+                         "(value in audio-s/s)")
+    ap.add_argument("--streams", type=int, default=ENC_STREAMS,
+                    help="streams per GPU of the encoder workload")
+    ap.add_argument("--encoder-chunks", type=int, default=20,
+                    help="timed chunks of the encoder measurement in the default run")
+    ap.add_argument("--no-encoder", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()

@@ -153,6 +153,10 @@ cq_status cq_encoder_encode_chunk(cq_encoder_state* st, const float* mel, int32_
 
 int32_t cq_encoder_state_chunks(const cq_encoder_state* st) { return st ? st->impl->chunks() : -1; }
 
+int32_t cq_encoder_state_kernels_per_chunk(const cq_encoder_state* st) {
+  return st ? st->impl->launches_per_chunk() : -1;
+}
+
 cq_status cq_encoder_state_reset(cq_encoder_state* st) {
   return guarded([&] {
     need_handle(st, "state");

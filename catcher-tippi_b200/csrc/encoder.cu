@@ -699,6 +699,8 @@ void EncoderState::encode_chunk(const float* mel, int mel_frames, void* out, cud
         throw;
       }
       check_cuda(cudaStreamEndCapture(capture_stream_, &graph), "end capture");
+      size_t nodes = 0;
+      if (cudaGraphGetNodes(graph, nullptr, &nodes) == cudaSuccess) launches_ = static_cast<int>(nodes);
       cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
       cudaGraphDestroy(graph);
       check_cuda(e, "instantiate chunk graph");

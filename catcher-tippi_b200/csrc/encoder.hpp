@@ -111,6 +111,9 @@ class EncoderState {
   void encode_chunk(const float* mel, int mel_frames, void* out, cudaStream_t stream);
   void reset();
   int chunks() const { return chunks_; }
+  // Kernel launches of one chunk (the node count of the last captured chunk
+  // graph, or the launches of the last eager chunk).
+  int launches_per_chunk() const { return launches_; }
   int streams() const { return S_; }
 
   // Frame counts of one chunk through the subsampling (encoder.rs:767-802).
@@ -130,6 +133,7 @@ class EncoderState {
   Encoder& enc_;
   int S_, max_mel_, qmax_, ring_, vmax_, pmax_;
   int chunks_ = 0;
+  int launches_ = 0;
   DeviceBuffer counters_, prompts_;
   DeviceBuffer res_, xn_, hid_, y_, att_, qkv_, pin_, relk_, pos_table_;
   DeviceBuffer kring_, vring_, conv_cache_;

@@ -80,6 +80,7 @@ def lib() -> ctypes.CDLL:
         "cq_encoder_state_output_frames": ([vp, i32], i32),
         "cq_encoder_encode_chunk": ([vp, vp, i32, vp, vp], i32),
         "cq_encoder_state_chunks": ([vp], i32),
+        "cq_encoder_state_kernels_per_chunk": ([vp], i32),
         "cq_encoder_state_reset": ([vp], i32),
         "cq_encoder_state_destroy": ([vp], None),
     }

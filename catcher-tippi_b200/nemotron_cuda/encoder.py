@@ -143,6 +143,10 @@ class EncoderState:
     def chunks(self) -> int:
         return int(lib().cq_encoder_state_chunks(self._h))
 
+    @property
+    def kernels_per_chunk(self) -> int:
+        return int(lib().cq_encoder_state_kernels_per_chunk(self._h))
+
     def reset(self) -> None:
         _check(lib().cq_encoder_state_reset(self._h))
 

@@ -130,6 +130,10 @@ cq_status cq_encoder_encode_chunk(cq_encoder_state *st, const float *mel, int32_
 /* Chunks encoded so far. */
 int32_t cq_encoder_state_chunks(const cq_encoder_state *st);
 
+/* Kernels one chunk launches (nodes of the captured chunk graph; 0 before the
+ * first graph is captured). */
+int32_t cq_encoder_state_kernels_per_chunk(const cq_encoder_state *st);
+
 /* Zeroes every cache (a new utterance on every stream). Synchronous. */
 cq_status cq_encoder_state_reset(cq_encoder_state *st);
 
