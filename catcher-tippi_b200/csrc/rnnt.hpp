@@ -1,0 +1,108 @@
+// C++ host layer of the batched RNNT greedy decoder: the counterpart of the
+// reference's StreamingRnntDecoder, PredictionNetwork, LstmCell,
+// QuantizedEmbedding and JointNetwork (crates/nemotron-mlx/src/model/rnnt.rs).
+// The C ABI in include/cqrnnt.h wraps these classes.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "cqrnnt.h"
+#include "device_buffer.hpp"
+#include "qlinear.hpp"
+
+namespace nemotron_cuda {
+
+class RnntDecoder {
+ public:
+  struct Spec {
+    std::string name;
+    bool linear;
+    int out = 0, in = 0;
+    bool has_bias = false;
+    size_t len = 0;
+  };
+
+  RnntDecoder(const cq_rnnt_config& cfg, cq_dtype dtype, int device);
+
+  const cq_rnnt_config& config() const { return cfg_; }
+  cq_dtype dtype() const { return dtype_; }
+  int device() const { return device_; }
+  const std::vector<Spec>& specs() const { return specs_; }
+
+  void set_linear(const std::string& name, const uint32_t* q, const void* scales,
+                  const void* biases, const void* bias, int out, int in, int group);
+  void set_tensor(const std::string& name, const float* values, size_t len);
+  void get_tensor(const std::string& name, float* values, size_t len) const;
+  QuantizedLinear* linear(const std::string& name) const;
+  void init_random(uint64_t seed);
+
+  // Checks every tensor is bound; dequantises the embedding and adds the LSTM
+  // bias pairs.
+  void finalize();
+  QuantizedLinear* enc_proj() const { return linear("encoder_projector.weight"); }
+  QuantizedLinear* dec_proj() const { return linear("decoder.decoder_projector.weight"); }
+  QuantizedLinear* head() const { return linear("joint.head.weight"); }
+  QuantizedLinear* ih(int l) const;
+  QuantizedLinear* hh(int l) const;
+  const void* embedding() const { return embedding_.get(); }  // T [vocab, pred_hidden]
+  const void* lstm_bias(int l) const { return lstm_bias_[l].get(); }  // T [4 * pred_hidden]
+
+ private:
+  const Spec& spec(const std::string& name, bool linear) const;
+  void bind_dense_device(const Spec& s, const float* dvalues);
+
+  cq_rnnt_config cfg_;
+  cq_dtype dtype_;
+  int device_;
+  std::vector<Spec> specs_;
+  std::map<std::string, size_t> index_;
+  std::map<std::string, std::unique_ptr<QuantizedLinear>> linears_;
+  std::map<std::string, DeviceBuffer> dense_;  // f32 copies of the LSTM biases
+  DeviceBuffer embedding_;
+  std::vector<DeviceBuffer> lstm_bias_;
+  bool finalized_ = false;
+};
+
+class RnntState {
+ public:
+  RnntState(RnntDecoder& dec, int streams, int max_frames);
+  ~RnntState();
+  RnntState(const RnntState&) = delete;
+  RnntState& operator=(const RnntState&) = delete;
+
+  int capacity() const { return max_frames_ * dec_.config().max_symbols; }
+  void reset();
+  void decode_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,
+                    int* counts, cudaStream_t stream);
+  int launches_per_chunk() const { return launches_; }
+
+ private:
+  void launch_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,
+                    int* counts, cudaStream_t stream);
+  void prediction_step(bool all, cudaStream_t stream);
+  void linear(QuantizedLinear* L, const void* x, int ldx, int rows, void* y, int ldy, int act,
+              cudaStream_t stream);
+
+  RnntDecoder& dec_;
+  int S_, max_frames_;
+  int launches_ = 0;
+  DeviceBuffer ep_, dec_out_, dec_new_, fused_, logits_, x_, gi_, gh_, active_;
+  std::vector<DeviceBuffer> h_, c_;
+  DeviceBuffer scratch_;
+
+  struct GraphEntry {
+    const void* encoded;
+    int ld, frames;
+    const int *tokens, *token_frames, *counts;
+    cudaGraphExec_t exec;
+  };
+  std::vector<GraphEntry> graphs_;
+  cudaStream_t capture_stream_ = nullptr;
+};
+
+}  // namespace nemotron_cuda

@@ -83,6 +83,23 @@ def lib() -> ctypes.CDLL:
         "cq_encoder_state_kernels_per_chunk": ([vp], i32),
         "cq_encoder_state_reset": ([vp], i32),
         "cq_encoder_state_destroy": ([vp], None),
+        # batched RNNT decoder (include/cqrnnt.h)
+        "cq_rnnt_default_config": ([vp], None),
+        "cq_rnnt_create": ([vp, i32, i32, pp], i32),
+        "cq_rnnt_set_linear": ([vp, ctypes.c_char_p, vp, vp, vp, vp, i32, i32, i32], i32),
+        "cq_rnnt_set_tensor": ([vp, ctypes.c_char_p, vp, sz], i32),
+        "cq_rnnt_get_tensor": ([vp, ctypes.c_char_p, vp, sz], i32),
+        "cq_rnnt_linear": ([vp, ctypes.c_char_p], vp),
+        "cq_rnnt_init_random": ([vp, ctypes.c_uint64], i32),
+        "cq_rnnt_tensor_count": ([vp], i32),
+        "cq_rnnt_tensor_name": ([vp, i32], ctypes.c_char_p),
+        "cq_rnnt_destroy": ([vp], None),
+        "cq_rnnt_state_create": ([vp, i32, i32, pp], i32),
+        "cq_rnnt_state_capacity": ([vp], i32),
+        "cq_rnnt_decode_chunk": ([vp, vp, i32, i32, vp, vp, vp, vp], i32),
+        "cq_rnnt_state_kernels_per_chunk": ([vp], i32),
+        "cq_rnnt_state_reset": ([vp], i32),
+        "cq_rnnt_state_destroy": ([vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

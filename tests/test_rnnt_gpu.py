@@ -1,0 +1,115 @@
+"""Batched RNNT greedy decoder on the GPU (include/cqrnnt.h) against the CPU
+restatement in oracle/rnnt_oracle.py.
+
+Greedy decisions are compared by teacher forcing: the oracle replays the GPU's
+tokens and checks every decision against its own argmax.  A differing choice
+must be a near tie (its logit within 8 T ulps of the oracle's maximum: the two
+sides sum in different orders, so logits can differ in their last bits) and
+such ties must stay rare; every other decision must be identical.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import rnnt_oracle as ro
+
+pytestmark = pytest.mark.gpu
+
+SMALL = dict(enc_hidden=256, pred_hidden=128, joint_hidden=128, vocab=65, max_symbols=3,
+             group_size=64)
+
+
+def _ocfg(d):
+    return ro.RnntConfig(enc_hidden=d["enc_hidden"], pred_hidden=d["pred_hidden"],
+                         joint_hidden=d["joint_hidden"], vocab=d["vocab"],
+                         max_symbols=d["max_symbols"], group=d["group_size"])
+
+
+def _dev(torch, x_f32, dtype):
+    import oracle
+    bits = oracle.to_t(x_f32, dtype).view(np.int16)
+    return torch.from_numpy(bits).cuda().view(torch.bfloat16 if dtype == "bf16" else torch.float16)
+
+
+def _check_streams(torch, state, ref, caches, enc_f32, streams, frames, dtype, totals):
+    paths = state.decode_chunk(_dev(torch, enc_f32.reshape(streams * frames, -1), dtype), frames)
+    for s in range(streams):
+        stats = ro.check_path(ref, enc_f32[s], caches[s], paths[s])
+        assert stats["mismatch"] == 0, (s, stats, paths[s])
+        totals["decisions"] += stats["decisions"]
+        totals["differ"] += stats["differ"]
+    return paths
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_small_decoder_greedy_paths_match_oracle(cq, oracle_mod, dtype):
+    import torch
+    from nemotron_cuda.rnnt import Rnnt, RnntConfig
+    cfg = _ocfg(SMALL)
+    params = ro.random_params(cfg, 21, dtype)
+    dec = Rnnt(RnntConfig.default(**SMALL), dtype)
+    for name, (n, k, has_bias) in ro.linear_names(cfg).items():
+        q, s, b, bias = params[name]
+        dec.set_linear(name, q, s, b, bias if has_bias else None, cfg.group)
+    for name in ro.dense_names(cfg):
+        dec.set_tensor(name, params[name])
+    ref = ro.RnntDecoder(cfg, params, dtype)
+    streams, frames = 3, 5
+    state = dec.state(streams, frames)
+    assert state.capacity == frames * cfg.max_symbols
+    caches = [ref.new_state() for _ in range(streams)]
+    rng = np.random.default_rng(3)
+    totals = {"decisions": 0, "differ": 0}
+    for _ in range(3):
+        enc = rng.standard_normal((streams, frames, cfg.enc_hidden)).astype(np.float32)
+        paths = _check_streams(torch, state, ref, caches, enc, streams, frames, dtype, totals)
+        for p in paths:
+            assert all(t != cfg.blank and 0 <= t < cfg.vocab for t, _ in p)
+            assert max(np.bincount([f for _, f in p], minlength=frames)) <= cfg.max_symbols
+    assert totals["differ"] <= max(1, totals["decisions"] // 20), totals
+    assert state.kernels_per_chunk > 0
+    assert cq.device_status(0) == 0
+
+
+def test_full_size_decoder_device_weights(cq, oracle_mod):
+    """Hidden 640, encoder 1024, vocab 1025, ten symbols per frame, two LSTM
+    layers; device-generated weights read back for the oracle."""
+    import torch
+    from nemotron_cuda.rnnt import Rnnt
+    dtype = "bf16"
+    dec = Rnnt.random(None, seed=5, dtype=dtype)
+    cfg = ro.RnntConfig()
+    params = dec.export_params(ro.linear_names(cfg), ro.dense_names(cfg))
+    ref = ro.RnntDecoder(cfg, params, dtype)
+    streams, frames = 2, 14
+    state = dec.state(streams, frames)
+    caches = [ref.new_state() for _ in range(streams)]
+    rng = np.random.default_rng(8)
+    totals = {"decisions": 0, "differ": 0}
+    enc = (rng.standard_normal((streams, frames, 1024)) * 0.5).astype(np.float32)
+    _check_streams(torch, state, ref, caches, enc, streams, frames, dtype, totals)
+    assert totals["differ"] <= max(2, totals["decisions"] // 20), totals
+
+
+def test_reset_replays_the_same_tokens(cq):
+    import torch
+    from nemotron_cuda.rnnt import Rnnt, RnntConfig
+    dec = Rnnt.random(RnntConfig.default(**SMALL), seed=9, dtype="bf16")
+    state = dec.state(4, 6)
+    enc = torch.randn((4 * 6, SMALL["enc_hidden"]), device="cuda").to(torch.bfloat16)
+    first = [state.decode_chunk(enc, 6) for _ in range(2)]
+    state.reset()
+    again = [state.decode_chunk(enc, 6) for _ in range(2)]
+    assert first == again
+
+
+def test_rnnt_binding_errors(cq):
+    from nemotron_cuda import CQError
+    from nemotron_cuda.rnnt import Rnnt, RnntConfig
+    dec = Rnnt(RnntConfig.default(**SMALL), "f16")
+    with pytest.raises(CQError, match="unknown RNNT tensor"):
+        dec.set_tensor("decoder.lstm.bias_ih_l7", np.zeros(512))
+    with pytest.raises(CQError, match="is not bound"):
+        dec.state(1, 4)
+    assert "decoder.embedding.weight" in dec.tensor_names()
