@@ -260,43 +260,81 @@ def encoder_flops_per_chunk(streams: int) -> int:
 
 
 def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: int,
-                  chunks: int, with_e2e: bool = True) -> dict:
+                  chunks: int, with_e2e: bool = True, with_rnnt: bool = False) -> dict:
     """Streaming encoder (subsampling + 24 FastConformer blocks + prompt
     projector) over `streams` lock-step streams, one 112-frame chunk per step,
-    through the C ABI (cq_encoder_encode_chunk replays one CUDA graph per chunk)."""
+    through the C ABI (cq_encoder_encode_chunk replays one CUDA graph per
+    chunk).  With `with_rnnt`, every chunk's encoder output is also decoded by
+    the batched RNNT greedy decoder (cq_rnnt_decode_chunk), pipelined on a
+    second CUDA stream: RNNT of chunk c overlaps the encoder of chunk c + 1."""
     from nemotron_cuda.encoder import Encoder
     enc = Encoder.random(None, seed=7, dtype="bf16", device=local_rank)
     st = enc.state(streams, CHUNK_MEL)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(11 + local_rank)
     mel = torch.randn((streams, CHUNK_MEL, 128), generator=gen, device="cuda")
-    out = st.encode_chunk(mel)  # first chunk (eager; later chunks replay a graph)
-    stream = torch.cuda.Stream()
+    outs = [st.encode_chunk(mel)]  # first chunk (eager; later chunks replay a graph)
+    frames = outs[0].shape[0] // streams
+    s_enc = torch.cuda.Stream()
     host_mel = torch.empty(tuple(mel.shape), dtype=torch.float32).pin_memory()
     host_mel.copy_(mel.cpu())
-    host_out = torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory()
+    rn = rst = None
+    if with_rnnt:
+        from nemotron_cuda.rnnt import Rnnt
+        outs.append(torch.empty_like(outs[0]))
+        rn = Rnnt.random(None, seed=13, dtype="bf16", device=local_rank)
+        rst = rn.state(streams, frames)
+        # the decoder's short dependent launches are the critical path: give them
+        # priority over the encoder's GEMMs when both have CTAs waiting for SMs
+        lo, hi = torch.cuda.Stream.priority_range() if hasattr(torch.cuda.Stream, "priority_range") \
+            else (0, -1)
+        s_dec = torch.cuda.Stream(priority=min(lo, hi))
+        tok = [torch.empty((streams, rst.capacity), dtype=torch.int32, device="cuda") for _ in range(2)]
+        tfr = [torch.empty_like(t) for t in tok]
+        cnt = [torch.empty((streams,), dtype=torch.int32, device="cuda") for _ in range(2)]
+        host_tok = torch.empty((streams, rst.capacity), dtype=torch.int32).pin_memory()
+        host_cnt = torch.empty((streams,), dtype=torch.int32).pin_memory()
+        enc_done = [torch.cuda.Event() for _ in range(2)]
+        dec_done = [torch.cuda.Event() for _ in range(2)]
+    host_out = torch.empty(tuple(outs[0].shape), dtype=outs[0].dtype).pin_memory()
     torch.cuda.synchronize()
 
     def run(n: int, e2e: bool) -> None:
-        for _ in range(n):
-            if e2e:
-                mel.copy_(host_mel, non_blocking=True)
-            st.encode_chunk(mel, out, stream=stream)
-            if e2e:
-                host_out.copy_(out, non_blocking=True)
+        for i in range(n):
+            b = i % 2 if with_rnnt else 0
+            with torch.cuda.stream(s_enc):
+                if e2e:
+                    mel.copy_(host_mel, non_blocking=True)
+                if with_rnnt:
+                    s_enc.wait_event(dec_done[b])  # the decoder has read this buffer
+                st.encode_chunk(mel, outs[b], stream=s_enc)
+                if e2e and not with_rnnt:
+                    host_out.copy_(outs[b], non_blocking=True)
+                if with_rnnt:
+                    enc_done[b].record(s_enc)
+            if with_rnnt:
+                with torch.cuda.stream(s_dec):
+                    s_dec.wait_event(enc_done[b])
+                    rst.decode_chunk_raw(outs[b], frames, tok[b], tfr[b], cnt[b], stream=s_dec)
+                    if e2e:
+                        host_cnt.copy_(cnt[b], non_blocking=True)
+                        host_tok.copy_(tok[b], non_blocking=True)
+                    dec_done[b].record(s_dec)
 
     def timed(e2e: bool) -> float:
-        with torch.cuda.stream(stream):
-            run(args.warmup, e2e)
+        run(args.warmup, e2e)
         torch.cuda.synchronize()
         if dist:
             dist.barrier()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            s.record(stream)
-            run(chunks, e2e)
-            e.record(stream)
+        s.record(s_enc)
+        if with_rnnt:
+            s_dec.wait_stream(s_enc)
+        run(chunks, e2e)
+        if with_rnnt:
+            s_enc.wait_stream(s_dec)
+        e.record(s_enc)
         torch.cuda.synchronize()
         ms = s.elapsed_time(e)
         if dist:
@@ -310,7 +348,7 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
     ms = timed(False)
     clock_info = clocks.stop()
     ms_e2e = timed(True) if with_e2e else None
-    kernels = st.kernels_per_chunk
+    kernels = st.kernels_per_chunk + (rst.kernels_per_chunk if with_rnnt else 0)
     status = cq.device_status(local_rank)
     if status != 0:
         raise RuntimeError(f"device watchdog reported status {status}")
@@ -319,58 +357,78 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
     flops = encoder_flops_per_chunk(streams)
     tpeak, tkind = measured_tensor_peak()
     tflops = flops / (per_chunk * 1e-3) / 1e12
+    what = ("streaming FastConformer encoder (Conv2D subsampling, 24 blocks d=1024 ff=4096 8 heads, "
+            "attention window 56+14 frames, conv kernel 9 cache, prompt projector)")
+    if with_rnnt:
+        what += (" + batched RNNT greedy decode (2-layer LSTM 640, joint 640 -> vocab 1025, at most "
+                 "10 symbols per frame; random weights emit the maximum), RNNT of chunk c pipelined "
+                 "with the encoder of chunk c+1 on a second CUDA stream")
     res = {
         "metric": "encoder audio-sec/sec", "value": round(audio / (ms * 1e-3), 1),
         "unit": "audio-s/s", "streams_per_gpu": streams, "chunks": chunks,
         "ms_per_chunk": round(per_chunk, 4), "chunk_audio_s": CHUNK_AUDIO_S,
-        "workload": (f"streaming FastConformer encoder (Conv2D subsampling, 24 blocks d=1024 "
-                     f"ff=4096 8 heads, attention window 56+14 frames, conv kernel 9 cache, "
-                     f"prompt projector), {streams} lock-step streams per GPU, 112 log-mel frames "
-                     f"x 128 bins per chunk, random-init INT8 group 64 bf16"),
+        "workload": (f"{what}; {streams} lock-step streams per GPU, 112 log-mel frames x 128 bins "
+                     f"per chunk, random-init INT8 group 64 bf16"),
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": tpeak,
                      "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4),
                      "peak_kind": f"{tkind} dense bf16 (sustained)",
-                     "note": "linear FLOPs of the whole chunk / chunk time (lower bound on "
-                             "the GEMMs' own rate)"},
+                     "note": "encoder linear FLOPs of the whole chunk / chunk time (lower bound "
+                             "on the GEMMs' own rate)"},
         "clocks": clock_info,
         "gpu_launches": kernels * chunks, "kernels_per_chunk": kernels,
     }
     if ms_e2e is not None:
         res["e2e"] = {"value": round(audio / (ms_e2e * 1e-3), 1), "unit": "audio-s/s",
                       "h2d_bytes_per_step": host_mel.numel() * 4,
-                      "d2h_bytes_per_step": host_out.numel() * 2,
-                      "path": "pinned host log-mel -> device, cq_encoder_encode_chunk, encoder "
-                              "output -> pinned host, every chunk inside the timed region"}
-    del st, enc
+                      "d2h_bytes_per_step": (host_tok.numel() + host_cnt.numel()) * 4
+                      if with_rnnt else host_out.numel() * 2,
+                      "path": "pinned host log-mel -> device, cq_encoder_encode_chunk"
+                              + (", cq_rnnt_decode_chunk, token ids and counts" if with_rnnt
+                                 else ", encoder output") +
+                              " -> pinned host, every chunk inside the timed region"}
+    del st, enc, rst, rn
     return res
 
 
-def cpu_encoder_baseline(target_s: float = 8.0) -> dict:
+def cpu_encoder_baseline(target_s: float = 8.0, with_rnnt: bool = True) -> dict:
     """The CPU restatement of the encoder (oracle/encoder_oracle.py, numpy +
-    the OpenMP C linear) on one stream: a bounded sample of chunks."""
+    the OpenMP C linear) and, with `with_rnnt`, of the RNNT greedy decoder
+    (oracle/rnnt_oracle.py) on one stream: a bounded sample of chunks."""
     import numpy as np
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import encoder_oracle as eo
     import oracle
+    import rnnt_oracle as ro
     cfg = eo.EncoderConfig()
-    params = eo.random_params(cfg, 3, "bf16")
-    enc = eo.Encoder(cfg, params, "bf16")
+    enc = eo.Encoder(cfg, eo.random_params(cfg, 3, "bf16"), "bf16")
     cache = enc.new_cache()
+    dec = dstate = None
+    if with_rnnt:
+        rcfg = ro.RnntConfig()
+        dec = ro.RnntDecoder(rcfg, ro.random_params(rcfg, 4, "bf16"), "bf16")
+        dstate = dec.new_state()
     rng = np.random.default_rng(0)
     mel = rng.standard_normal((CHUNK_MEL, 128)).astype(np.float32)
-    enc.encode_chunk(mel, 101, cache)  # warm
+
+    def chunk():
+        y = enc.encode_chunk(mel, 101, cache)
+        if dec is not None:
+            dec.decode_frames(y, dstate)
+
+    chunk()  # warm
     t0 = time.perf_counter()
     n = 0
     while True:
-        enc.encode_chunk(mel, 101, cache)
+        chunk()
         n += 1
         if time.perf_counter() - t0 >= target_s and n >= 2:
             break
     dt = time.perf_counter() - t0
     return {"value": round(n * CHUNK_AUDIO_S / dt, 3), "unit": "audio-s/s",
             "cores": oracle.max_threads(), "kind": "port",
-            "sample": f"{n} chunks of one stream (112 mel frames each), {dt:.1f} s, numpy + "
-                      f"OpenMP C restatement of the streaming encoder (oracle/)"}
+            "sample": f"{n} chunks of one stream (112 mel frames each), {dt:.1f} s, numpy + OpenMP "
+                      f"C restatement of the streaming encoder"
+                      + (" and the RNNT greedy decoder" if with_rnnt else "") + " (oracle/)"}
 
 
 def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
@@ -384,7 +442,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     if args.workload == "encoder":
-        res = bench_encoder(torch, cq, args, world, local_rank, dist, args.streams, args.steps)
+        res = bench_encoder(torch, cq, args, world, local_rank, dist, args.streams, args.steps,
+                            with_rnnt=not args.no_rnnt)
         if dist:
             dist.destroy_process_group()
         if rank != 0:
@@ -400,7 +459,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
                 "gpu_launches": res["gpu_launches"]}
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds)
+            line["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds, not args.no_rnnt)
         return line
     step_flops = None
     if args.workload == "linear":
@@ -471,11 +530,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     encoder = None
     if args.workload == "block" and not args.no_encoder:
         encoder = bench_encoder(torch, cq, args, world, local_rank, dist, ENC_STREAMS,
-                                args.encoder_chunks)
-        encoder["batch1"] = bench_encoder(torch, cq, args, world, local_rank, dist, 1,
-                                          args.encoder_chunks, with_e2e=False)
-        for k in ("clocks",):
-            encoder["batch1"].pop(k, None)
+                                args.encoder_chunks, with_rnnt=True)
+        for key, streams in (("encoder_only", ENC_STREAMS), ("batch1", 1)):
+            sub = bench_encoder(torch, cq, args, world, local_rank, dist, streams,
+                                args.encoder_chunks, with_e2e=False)
+            sub.pop("clocks", None)
+            encoder[key] = sub
     if dist:
         dist.destroy_process_group()
     if rank != 0:
@@ -635,6 +695,8 @@ def main() -> None:
     ap.add_argument("--encoder-chunks", type=int, default=20,
                     help="timed chunks of the encoder measurement in the default run")
     ap.add_argument("--no-encoder", action="store_true")
+    ap.add_argument("--no-rnnt", action="store_true",
+                    help="encoder workload without the RNNT decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()

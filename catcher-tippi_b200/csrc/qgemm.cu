@@ -28,6 +28,7 @@
 #include "qgemm.hpp"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace cq {
 
@@ -148,6 +149,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
   const int KT = (a.K + kBK - 1) / kBK;
+  // this CTA's k tiles: all of them, or its slice of a cluster's K split
+  // (the host guarantees every slice is non-empty)
+  const int nsplit = gridDim.z, split = blockIdx.z;
+  const int per = (KT + nsplit - 1) / nsplit;
+  const int kt0 = split * per;
+  const int NKT = min(KT, kt0 + per) - kt0;
 
   if (threadIdx.x == 0) {
     prefetch_tensormap(&amap);
@@ -180,9 +187,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint64_t pol = l2_policy_evict_normal();
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % kStages;
-        const uint32_t ph = (kt / kStages) & 1;
+      for (int i = 0; i < NKT; ++i) {
+        const int kt = kt0 + i;
+        const int s = i % kStages;
+        const uint32_t ph = (i / kStages) & 1;
         ok = mbar_wait_bounded(&empty[s], ph ^ 1, a.status) && ok;
         uint8_t* st = smem + s * L::kStage;
         mbar_arrive_expect_tx(&full[s], L::kA + L::kQ + L::kSB);
@@ -199,10 +207,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32<BN>();
-      for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % kStages, b = kt % kBBufs;
-        ok = mbar_wait_bounded(&full[s], (kt / kStages) & 1, a.status) && ok;
-        ok = mbar_wait_bounded(&bfull[b], (kt / kBBufs) & 1, a.status) && ok;
+      for (int i = 0; i < NKT; ++i) {
+        const int s = i % kStages, b = i % kBBufs;
+        ok = mbar_wait_bounded(&full[s], (i / kStages) & 1, a.status) && ok;
+        ok = mbar_wait_bounded(&bfull[b], (i / kBBufs) & 1, a.status) && ok;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem + s * L::kStage);
         const uint32_t b_addr = smem_u32(smem + L::kBOff + b * L::kB);
@@ -210,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int ks = 0; ks < kBK / 16; ++ks) {
           // advancing K by 16 f16 = 32 bytes inside the swizzle atom
           tc_mma_f16(tmem_d, sw128_kmajor_desc(a_addr + 32 * ks), sw128_kmajor_desc(b_addr + 32 * ks),
-                     idesc, (kt | ks) != 0);
+                     idesc, (i | ks) != 0);
         }
         tc_commit(&empty[s]);   // x tile consumed
         tc_commit(&bempty[b]);  // dequantised tile consumed
@@ -227,10 +235,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       bias_s[t + kDT * rr] = (a.bias != nullptr && n < a.N) ? ld_t<DT>(a.bias, n) : 0.0f;
     }
     const __half2 k1024 = __float2half2_rn(1024.0f);
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % kStages, b = kt % kBBufs;
-      ok = mbar_wait_bounded(&full[s], (kt / kStages) & 1, a.status) && ok;
-      ok = mbar_wait_bounded(&bempty[b], ((kt / kBBufs) & 1) ^ 1, a.status) && ok;
+    for (int i = 0; i < NKT; ++i) {
+      const int s = i % kStages, b = i % kBBufs;
+      ok = mbar_wait_bounded(&full[s], (i / kStages) & 1, a.status) && ok;
+      ok = mbar_wait_bounded(&bempty[b], ((i / kBBufs) & 1) ^ 1, a.status) && ok;
       const uint8_t* st = smem + s * L::kStage;
       const __half2* sbp = reinterpret_cast<const __half2*>(st + L::kA + L::kQ);
       uint8_t* bt = smem + L::kBOff + b * L::kB;
@@ -298,26 +306,105 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float rs = (a.row_scale != nullptr && m < a.M) ? a.row_scale[m] : 1.0f;
     const bool has_bias = a.bias != nullptr;
     const bool vec_ok = (a.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+    if (nsplit > 1) {
+      // K split: park this CTA's partial tile [128][BN] in the (now idle)
+      // stage buffers, rows padded by 4 floats so a warp's 16-byte writes of
+      // 32 rows spread over all banks; the cluster reduces it below.
+      float* part = reinterpret_cast<float*>(smem);
+      const int row = quarter * 32 + lane;
 #pragma unroll 1
-    for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
-      tmem_wait_ld();
-      if (m < a.M) {
-        float o[32];
+      for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
+        tmem_wait_ld();
+        float4* dst = reinterpret_cast<float4*>(part + row * (BN + 4) + c0);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float v = round_t<DT>(__uint_as_float(r[j]) * rs);
-          if (has_bias) v = round_t<DT>(v + bias_s[c0 + j]);
+        for (int v = 0; v < 8; ++v)
+          dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+      }
+    } else {
+#pragma unroll 1
+      for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
+        tmem_wait_ld();
+        if (m < a.M) {
+          float o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float v = round_t<DT>(__uint_as_float(r[j]) * rs);
+            if (has_bias) v = round_t<DT>(v + bias_s[c0 + j]);
+            if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
+            else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
+            o[j] = v;
+          }
+          const int nb = n0 + c0;
+          if (vec_ok && nb + 32 <= a.N) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              if constexpr (DT == kBF16) {
+                const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
+                pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+              } else {
+                const __half2 h = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+                pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+              }
+            }
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.y) +
+                                                  static_cast<size_t>(m) * a.ldy + nb);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (nb + j < a.N) st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + nb + j, o[j]);
+          }
+        }
+      }
+    }
+  }
+
+  if (nsplit > 1) {
+    // every thread of every CTA in the cluster: the partial tiles are written
+    cluster_sync_all();
+    if (warp >= kDequantWarp0) {
+      // this CTA reduces columns [rank * W, (rank + 1) * W) of the tile over
+      // the cluster's partials in rank order, then applies the epilogue
+      const int t = threadIdx.x - kDequantWarp0 * 32;
+      const int W = BN / nsplit, groups = W / 4;
+      const int cbase = static_cast<int>(cluster_ctarank()) * W;
+      const uint32_t part_s = smem_u32(smem);
+      const bool vec4 = (a.ldy % 4) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 7) == 0;
+      for (int item = t; item < kBM * groups; item += kDequantWarps * 32) {
+        const int row = item / groups, col = cbase + (item % groups) * 4;
+        const uint32_t off = static_cast<uint32_t>(row * (BN + 4) + col) * 4u;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < nsplit; ++r) {
+          const float4 v = ld_dsmem_v4(mapa_shared(part_s + off, static_cast<uint32_t>(r)));
+          acc[0] += v.x;
+          acc[1] += v.y;
+          acc[2] += v.z;
+          acc[3] += v.w;
+        }
+        const int m = m0 + row;
+        if (m >= a.M) continue;
+        const float rs = a.row_scale != nullptr ? a.row_scale[m] : 1.0f;
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float v = round_t<DT>(acc[j] * rs);
+          if (a.bias != nullptr) v = round_t<DT>(v + bias_s[col + j]);
           if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
           else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
           o[j] = v;
         }
-        const int nb = n0 + c0;
-        if (vec_ok && nb + 32 <= a.N) {
-          uint32_t pk[16];
+        const int n = n0 + col;
+        if (vec4 && n + 4 <= a.N) {
+          uint32_t pk[2];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < 2; ++j) {
             if constexpr (DT == kBF16) {
               const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
               pk[j] = *reinterpret_cast<const uint32_t*>(&h);
@@ -326,17 +413,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               pk[j] = *reinterpret_cast<const uint32_t*>(&h);
             }
           }
-          uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.y) +
-                                                static_cast<size_t>(m) * a.ldy + nb);
-#pragma unroll
-          for (int v = 0; v < 4; ++v)
-            dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(a.y) + static_cast<size_t>(m) * a.ldy +
+                                    n) = make_uint2(pk[0], pk[1]);
         } else {
-          for (int j = 0; j < 32; ++j)
-            if (nb + j < a.N) st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + nb + j, o[j]);
+          for (int j = 0; j < 4; ++j)
+            if (n + j < a.N) st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n + j, o[j]);
         }
       }
     }
+    // the partials stay readable until every CTA of the cluster is done
+    cluster_sync_all();
   }
 
   tc_fence_before();
@@ -422,17 +508,31 @@ cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, 
     if (e != cudaSuccess) return e;
     configured = true;
   }
+  const int splits = a.splits > 1 ? a.splits : 1;
+  if (splits != 1 && splits != 2 && splits != 4) return cudaErrorInvalidValue;
+  if (splits > 1) {
+    // every split must own at least one k tile
+    const int KT = (a.K + kBK - 1) / kBK, per = (KT + splits - 1) / splits;
+    if ((splits - 1) * per >= KT) return cudaErrorInvalidValue;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + BN - 1) / BN, (a.M + kBM - 1) / kBM, 1);
+  cfg.gridDim = dim3((a.N + BN - 1) / BN, (a.M + kBM - 1) / kBM, splits);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   int na = 0;
   if (pdl) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    na = 1;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (splits > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = splits;
+    ++na;
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
@@ -475,6 +575,22 @@ cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, 
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, qgemm_prepass_kernel, reinterpret_cast<const __nv_bfloat16*>(x),
                             ldx, M, K, reinterpret_cast<__half*>(xo), ldo, row_scale);
+}
+
+int gemm_splits(int M, int N, int K, int num_sms) {
+  static const int forced = [] {
+    const char* e = std::getenv("CQ_GEMM_SPLITS");  // 1 disables the K split
+    return e == nullptr ? 0 : std::atoi(e);
+  }();
+  if (forced == 1) return 1;
+  const int tiles = ((N + kGemmBN - 1) / kGemmBN) * ((M + kBM - 1) / kBM);
+  const int KT = (K + kBK - 1) / kBK;
+  if (4 * tiles > num_sms) return 1;  // a quarter of the SMs or more: splitting does not pay
+  for (int s : {4, 2}) {
+    const int per = (KT + s - 1) / s;
+    if (tiles * s <= num_sms + num_sms / 4 && KT >= 2 * s && (s - 1) * per < KT) return s;
+  }
+  return 1;
 }
 
 size_t gemm_smem_bytes() { return GemmSmem<kGemmBN, 2>::kBytes + 1024; }

@@ -18,7 +18,13 @@ struct GemmArgs {
   int* status;             // device status word (watchdog)
   int M, N, K, ldy;
   int act;                 // cq::Act
+  int splits;              // K split over a (1, 1, splits) cluster: 1, 2 or 4
 };
+
+// K split that fills the GPU when the output tiles alone leave most SMs idle:
+// the CTAs of one cluster accumulate disjoint k ranges and reduce through
+// distributed shared memory (gemm_splits returns 1, 2 or 4).
+int gemm_splits(int M, int N, int K, int num_sms);
 
 // amap: f16 activations [M, K] (box 64 x 128, 128B swizzle);
 // qmap: packed weights u8 [N, K] (box 64 x kGemmBN, 64B swizzle).

@@ -254,6 +254,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
   g.K = K_;
   g.ldy = ldy;
   g.act = act;
+  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
   check_cuda(cq::launch_gemm(dtype_, group_, amap_, qmap_gemm_, g, stream, pdl_enabled()), "qgemm");
 }
 
@@ -307,6 +308,7 @@ void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows,
   g.K = K_;
   g.ldy = ldy;
   g.act = act;
+  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
   check_cuda(cq::launch_gemm(dtype_, group_, amap_scratch_, qmap_gemm_, g, stream, pdl_enabled()),
              "qgemm");
 }
