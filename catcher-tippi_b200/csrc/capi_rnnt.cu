@@ -136,6 +136,13 @@ cq_status cq_rnnt_decode_chunk(cq_rnnt_state* st, const void* encoded, int32_t l
   });
 }
 
+cq_status cq_rnnt_state_set_persistent(cq_rnnt_state* st, int32_t enable) {
+  return guarded([&] {
+    need_handle(st, "state");
+    st->impl->set_persistent(enable != 0);
+  });
+}
+
 int32_t cq_rnnt_state_kernels_per_chunk(const cq_rnnt_state* st) {
   return st ? st->impl->launches_per_chunk() : -1;
 }

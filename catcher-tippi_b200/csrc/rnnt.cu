@@ -237,6 +237,24 @@ RnntState::RnntState(RnntDecoder& dec, int streams, int max_frames)
   for (int l = 0; l < c.lstm_layers; ++l)
     need = std::max({need, dec_.ih(l)->scratch_bytes_for(S_), dec_.hh(l)->scratch_bytes_for(S_)});
   scratch_ = DeviceBuffer(std::max<size_t>(need, 256));
+
+  // One persistent launch per chunk when the shapes fit its tiling (64-wide
+  // sub-blocks, one group size >= 64 for all of its linears, <= 64 streams).
+  const int g = dec_.head()->group_size();
+  bool fits = S_ <= 64 && c.lstm_layers <= cq::kRnntMaxLayers &&
+              H % 64 == 0 && J % 64 == 0 && g % 64 == 0 && dec_.dec_proj()->group_size() == g;
+  for (int l = 0; l < c.lstm_layers && fits; ++l)
+    fits = dec_.ih(l)->group_size() == g && dec_.hh(l)->group_size() == g;
+  if (fits) {
+    const int dt = dec_.dtype() == CQ_BF16 ? cq::kBF16 : cq::kF16;
+    grid_ = cq::rnnt_chunk_grid(dt, S_, static_cast<int>(H), static_cast<int>(J), static_cast<int>(V),
+                                c.lstm_layers, device_context(dec_.device()).num_sms);
+  }
+  if (grid_ > 0) {
+    for (int l = 0; l < c.lstm_layers; ++l) h_alt_.emplace_back(S * H * 2);
+    part_ = DeviceBuffer(static_cast<size_t>((V + 15) / 16) * S * sizeof(float2));
+    barrier_ = DeviceBuffer(2 * sizeof(unsigned));
+  }
   check_cuda(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "capture stream");
   reset();
 }
@@ -292,6 +310,57 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
   const bool pdl = pdl_on();
   const int J = c.joint_hidden, V = c.vocab, H = c.pred_hidden;
   const int cap = capacity();
+  if (use_persistent_) {
+    // encoder projector over every frame of every stream, then the whole greedy
+    // loop of the chunk in one cooperative launch (rnnt_persistent.cu)
+    linear(dec_.enc_proj(), encoded, ld, S_ * frames, ep_.get(), J, CQ_ACT_NONE, st);
+    check_cuda(cq::launch_zero_ints(barrier_.as<int>(), 2, st), "zero barrier");
+    cq::RnntChunkArgs a{};
+    const QuantizedLinear* head = dec_.head();
+    const QuantizedLinear* proj = dec_.dec_proj();
+    a.head_q = static_cast<const uint8_t*>(head->qweight());
+    a.head_s = head->scales();
+    a.head_b = head->biases();
+    a.head_bias = head->bias();
+    for (int l = 0; l < c.lstm_layers; ++l) {
+      a.ih_q[l] = static_cast<const uint8_t*>(dec_.ih(l)->qweight());
+      a.ih_s[l] = dec_.ih(l)->scales();
+      a.ih_b[l] = dec_.ih(l)->biases();
+      a.hh_q[l] = static_cast<const uint8_t*>(dec_.hh(l)->qweight());
+      a.hh_s[l] = dec_.hh(l)->scales();
+      a.hh_b[l] = dec_.hh(l)->biases();
+      a.lstm_bias[l] = dec_.lstm_bias(l);
+      a.h[l][0] = h_[l].get();
+      a.h[l][1] = h_alt_[l].get();
+      a.c[l] = c_[l].get();
+    }
+    a.proj_q = static_cast<const uint8_t*>(proj->qweight());
+    a.proj_s = proj->scales();
+    a.proj_b = proj->biases();
+    a.proj_bias = proj->bias();
+    a.emb = dec_.embedding();
+    a.ep = ep_.get();
+    a.dec = dec_out_.get();
+    a.fused = fused_.get();
+    a.part = part_.as<float2>();
+    a.tokens = tokens;
+    a.token_frames = token_frames;
+    a.counts = counts;
+    a.cap = cap;
+    a.barrier = barrier_.as<unsigned>();
+    a.status = device_context(dec_.device()).status;
+    a.S = S_;
+    a.Q = frames;
+    a.H = H;
+    a.J = J;
+    a.V = V;
+    a.blank = c.blank;
+    a.max_symbols = c.max_symbols;
+    a.layers = c.lstm_layers;
+    a.group = head->group_size();
+    check_cuda(cq::launch_rnnt_chunk(dt, a, grid_, st), "persistent RNNT chunk");
+    return;
+  }
   check_cuda(cq::launch_zero_ints(counts, S_, st), "zero counts");
   // encoder projector over every frame of every stream (row = stream * frames + frame)
   linear(dec_.enc_proj(), encoded, ld, S_ * frames, ep_.get(), J, CQ_ACT_NONE, st);
@@ -312,6 +381,19 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
                  "joint input");
     }
   }
+}
+
+void RnntState::set_persistent(bool on) {
+  if (on && grid_ == 0)
+    throw_invalid("the persistent RNNT kernel does not fit this state (at most 64 streams, hidden sizes "
+                  "multiple of 64, one group size >= 64 for the head, LSTM and projector)");
+  if (on == use_persistent_) return;
+  DeviceGuard guard(dec_.device());
+  check_cuda(cudaDeviceSynchronize(), "switch RNNT path");
+  for (auto& g : graphs_) cudaGraphExecDestroy(g.exec);
+  graphs_.clear();
+  launches_ = 0;
+  use_persistent_ = on;
 }
 
 void RnntState::decode_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,

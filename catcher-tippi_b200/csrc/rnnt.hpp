@@ -80,6 +80,11 @@ class RnntState {
   void decode_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,
                     int* counts, cudaStream_t stream);
   int launches_per_chunk() const { return launches_; }
+  // Chunks as one persistent cooperative launch (true) or as a graph of one
+  // launch per op (false, the default).  Throws if the persistent kernel does
+  // not fit this state's shapes.
+  void set_persistent(bool on);
+  bool persistent() const { return use_persistent_; }
 
  private:
   void launch_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,
@@ -93,6 +98,11 @@ class RnntState {
   int launches_ = 0;
   DeviceBuffer ep_, dec_out_, dec_new_, fused_, logits_, x_, gi_, gh_, active_;
   std::vector<DeviceBuffer> h_, c_;
+  // persistent path: second hidden-state buffer per layer, head partials, barrier
+  std::vector<DeviceBuffer> h_alt_;
+  DeviceBuffer part_, barrier_;
+  int grid_ = 0;  // persistent grid size, 0 if the kernel does not fit
+  bool use_persistent_ = false;
   DeviceBuffer scratch_;
 
   struct GraphEntry {

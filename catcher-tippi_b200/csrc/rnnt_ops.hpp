@@ -2,6 +2,8 @@
 #pragma once
 
 #include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
 
 namespace cq {
 
@@ -30,5 +32,42 @@ cudaError_t launch_zero_ints(int* p, int n, cudaStream_t stream);
 // x[s] = table[row] for every stream (16-bit elements).
 cudaError_t launch_broadcast_row(const void* table, int row, int H, void* x, int S,
                                  cudaStream_t stream);
+
+// ---------------------------------------------------------------- persistent chunk kernel
+
+constexpr int kRnntMaxLayers = 4;
+
+// Everything one cooperative launch needs to decode a whole chunk
+// (rnnt_persistent.cu).  Weights in the MLX layout (u8 [N, K], T scales and
+// biases [N, K/g]); activations and state T.
+struct RnntChunkArgs {
+  const uint8_t* head_q;
+  const void *head_s, *head_b, *head_bias;  // [V, J]
+  const uint8_t* ih_q[kRnntMaxLayers];
+  const void *ih_s[kRnntMaxLayers], *ih_b[kRnntMaxLayers];  // [4H, H]
+  const uint8_t* hh_q[kRnntMaxLayers];
+  const void *hh_s[kRnntMaxLayers], *hh_b[kRnntMaxLayers];
+  const void* lstm_bias[kRnntMaxLayers];  // [4H], bias_ih + bias_hh in T
+  const uint8_t* proj_q;
+  const void *proj_s, *proj_b, *proj_bias;  // [J, H]
+  const void* emb;                          // [V, H] dequantised
+  const void* ep;                           // [S * Q, J] encoder projection of the chunk
+  void* h[kRnntMaxLayers][2];               // [S, H] ping-pong; buffer 0 holds the state between chunks
+  void* c[kRnntMaxLayers];                  // [S, H]
+  void* dec;                                // [S, J] decoder output
+  void* fused;                              // [S, J] joint input
+  float2* part;                             // [ceil(V/16), S] per-tile (max logit, index)
+  int *tokens, *token_frames, *counts;
+  int cap;
+  unsigned* barrier;  // {count, abort}, zero before the launch
+  int* status;
+  int S, Q, H, J, V, blank, max_symbols, layers, group;
+};
+
+// Grid size (CTAs) for S streams, 0 if the kernel cannot be used (shared
+// memory or co-residency); smem bytes for that grid.
+int rnnt_chunk_grid(int dtype, int S, int H, int J, int V, int layers, int num_sms);
+size_t rnnt_chunk_smem_bytes(int S, int H, int J, int V, int layers, int grid);
+cudaError_t launch_rnnt_chunk(int dtype, const RnntChunkArgs& a, int grid, cudaStream_t stream);
 
 }  // namespace cq

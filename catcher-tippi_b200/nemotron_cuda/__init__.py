@@ -98,6 +98,7 @@ def lib() -> ctypes.CDLL:
         "cq_rnnt_state_capacity": ([vp], i32),
         "cq_rnnt_decode_chunk": ([vp, vp, i32, i32, vp, vp, vp, vp], i32),
         "cq_rnnt_state_kernels_per_chunk": ([vp], i32),
+        "cq_rnnt_state_set_persistent": ([vp, i32], i32),
         "cq_rnnt_state_reset": ([vp], i32),
         "cq_rnnt_state_destroy": ([vp], None),
     }

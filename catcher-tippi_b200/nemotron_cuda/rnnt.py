@@ -122,6 +122,10 @@ class RnntState:
     def kernels_per_chunk(self) -> int:
         return int(lib().cq_rnnt_state_kernels_per_chunk(self._h))
 
+    def set_persistent(self, enable: bool = True) -> None:
+        """One persistent launch per chunk (early exit on all-blank frames)."""
+        _check(lib().cq_rnnt_state_set_persistent(self._h, int(enable)))
+
     def reset(self) -> None:
         _check(lib().cq_rnnt_state_reset(self._h))
 

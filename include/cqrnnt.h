@@ -92,6 +92,19 @@ cq_status cq_rnnt_decode_chunk(cq_rnnt_state *st, const void *encoded, int32_t l
                                int32_t *tokens, int32_t *token_frames, int32_t *counts,
                                void *stream);
 
+/*
+ * Selects how chunks run.  enable = 0 (the default): a CUDA graph of one
+ * launch per op, every frame running max_symbols iterations with per-stream
+ * masks.  enable != 0: one persistent cooperative launch per chunk (every CTA
+ * keeps its weight tiles in shared memory; bounded grid barriers between the
+ * head, LSTM and projector phases) that skips a frame's remaining iterations
+ * once every stream has emitted blank -- the faster choice when frames mostly
+ * end early (trained models), the slower one when every frame emits the
+ * maximum.  Fails with CQ_INVALID_ARGUMENT if the shapes do not fit it (more
+ * than 64 streams, hidden sizes not multiples of 64, group sizes below 64).
+ */
+cq_status cq_rnnt_state_set_persistent(cq_rnnt_state *st, int32_t enable);
+
 /* Kernels one chunk launches (nodes of the captured graph; 0 before capture). */
 int32_t cq_rnnt_state_kernels_per_chunk(const cq_rnnt_state *st);
 

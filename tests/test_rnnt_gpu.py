@@ -42,8 +42,9 @@ def _check_streams(torch, state, ref, caches, enc_f32, streams, frames, dtype, t
     return paths
 
 
+@pytest.mark.parametrize("persistent", [False, True])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-def test_small_decoder_greedy_paths_match_oracle(cq, oracle_mod, dtype):
+def test_small_decoder_greedy_paths_match_oracle(cq, oracle_mod, dtype, persistent):
     import torch
     from nemotron_cuda.rnnt import Rnnt, RnntConfig
     cfg = _ocfg(SMALL)
@@ -57,6 +58,7 @@ def test_small_decoder_greedy_paths_match_oracle(cq, oracle_mod, dtype):
     ref = ro.RnntDecoder(cfg, params, dtype)
     streams, frames = 3, 5
     state = dec.state(streams, frames)
+    state.set_persistent(persistent)
     assert state.capacity == frames * cfg.max_symbols
     caches = [ref.new_state() for _ in range(streams)]
     rng = np.random.default_rng(3)
@@ -68,11 +70,15 @@ def test_small_decoder_greedy_paths_match_oracle(cq, oracle_mod, dtype):
             assert all(t != cfg.blank and 0 <= t < cfg.vocab for t, _ in p)
             assert max(np.bincount([f for _, f in p], minlength=frames)) <= cfg.max_symbols
     assert totals["differ"] <= max(1, totals["decisions"] // 20), totals
-    assert state.kernels_per_chunk > 0
+    if persistent:  # the encoder projector, the barrier reset, one cooperative launch
+        assert 0 < state.kernels_per_chunk <= 5, state.kernels_per_chunk
+    else:
+        assert state.kernels_per_chunk > 100, state.kernels_per_chunk
     assert cq.device_status(0) == 0
 
 
-def test_full_size_decoder_device_weights(cq, oracle_mod):
+@pytest.mark.parametrize("persistent", [False, True])
+def test_full_size_decoder_device_weights(cq, oracle_mod, persistent):
     """Hidden 640, encoder 1024, vocab 1025, ten symbols per frame, two LSTM
     layers; device-generated weights read back for the oracle."""
     import torch
@@ -84,12 +90,58 @@ def test_full_size_decoder_device_weights(cq, oracle_mod):
     ref = ro.RnntDecoder(cfg, params, dtype)
     streams, frames = 2, 14
     state = dec.state(streams, frames)
+    state.set_persistent(persistent)
     caches = [ref.new_state() for _ in range(streams)]
     rng = np.random.default_rng(8)
     totals = {"decisions": 0, "differ": 0}
     enc = (rng.standard_normal((streams, frames, 1024)) * 0.5).astype(np.float32)
     _check_streams(torch, state, ref, caches, enc, streams, frames, dtype, totals)
     assert totals["differ"] <= max(2, totals["decisions"] // 20), totals
+
+
+def test_persistent_path_skips_frames_that_end_in_blank(cq, oracle_mod):
+    """A blank-favouring joint bias makes most frames end at their first
+    symbol, so the persistent kernel's early exit is taken; its greedy paths
+    still match the oracle decision by decision."""
+    import torch
+    import oracle
+    from nemotron_cuda.rnnt import Rnnt, RnntConfig
+    cfg = _ocfg(SMALL)
+    params = ro.random_params(cfg, 12, "f16")
+    q, s, b, bias = params["joint.head.weight"]
+    rng = np.random.default_rng(6)
+    encs = [rng.standard_normal((3, 6, cfg.enc_hidden)).astype(np.float32) for _ in range(3)]
+    # the smallest blank bias (from a sweep on the oracle) under which most
+    # frames end at blank before the symbol cap
+    for blank_bias in (0.05, 0.1, 0.15, 0.2, 0.3, 0.45, 0.6):
+        bias_f = oracle.from_t(bias, "f16")
+        bias_f[cfg.blank] = blank_bias
+        trial = dict(params)
+        trial["joint.head.weight"] = (q, s, b, oracle.to_t(bias_f, "f16"))
+        probe = ro.RnntDecoder(cfg, trial, "f16")
+        st = probe.new_state()
+        n = len(probe.decode_frames(encs[0][0], st))
+        if n < 6 * cfg.max_symbols // 2:
+            break
+    params = trial
+    dec = Rnnt(RnntConfig.default(**SMALL), "f16")
+    for name, (n, k, has_bias) in ro.linear_names(cfg).items():
+        q, s, b, bias = params[name]
+        dec.set_linear(name, q, s, b, bias if has_bias else None, cfg.group)
+    for name in ro.dense_names(cfg):
+        dec.set_tensor(name, params[name])
+    ref = ro.RnntDecoder(cfg, params, "f16")
+    streams, frames = 3, 6
+    state = dec.state(streams, frames)
+    state.set_persistent(True)
+    caches = [ref.new_state() for _ in range(streams)]
+    totals = {"decisions": 0, "differ": 0}
+    emitted = 0
+    for enc in encs:
+        paths = _check_streams(torch, state, ref, caches, enc, streams, frames, "f16", totals)
+        emitted += sum(len(p) for p in paths)
+    assert 0 < emitted < 3 * streams * frames * cfg.max_symbols
+    assert totals["differ"] <= max(1, totals["decisions"] // 20), totals
 
 
 def test_reset_replays_the_same_tokens(cq):
@@ -113,3 +165,6 @@ def test_rnnt_binding_errors(cq):
     with pytest.raises(CQError, match="is not bound"):
         dec.state(1, 4)
     assert "decoder.embedding.weight" in dec.tensor_names()
+    st = Rnnt.random(RnntConfig.default(**SMALL), seed=1, dtype="f16").state(65, 4)
+    with pytest.raises(CQError, match="does not fit"):
+        st.set_persistent(True)
