@@ -540,6 +540,23 @@ GemvPlan plan_gemv(int N, int K, int num_sms) {
   return best;
 }
 
+GemvPlan plan_gemv_rows(const GemvPlan& base, int N, int M) {
+  const int mtiles = (M + 15) / 16;
+  if (mtiles <= 1 || std::getenv("CQ_GEMV_PLAN") != nullptr) return base;
+  for (int rt : {1, 2, 4}) {
+    if (rt < base.rt) continue;
+    const int bands = (N + 16 * rt - 1) / (16 * rt);
+    if (bands * base.ksplit * mtiles <= 2 * base.num_sms) {
+      GemvPlan p = base;
+      p.rt = rt;
+      return p;
+    }
+  }
+  GemvPlan p = base;
+  p.rt = 4;
+  return p;
+}
+
 size_t gemv_smem_bytes(const GemvPlan& plan, int group) {
   return gemv_smem_layout(plan.rt, plan.sb_per_cta, group == 32 ? 2 : 1, plan.ksplit).total;
 }

@@ -29,6 +29,11 @@ struct GemvPlan {
 };
 
 GemvPlan plan_gemv(int N, int K, int num_sms);
+// The plan for a call with M rows: the base plan (chosen for one 16-row token
+// tile) unless several token tiles would not fit one wave of two CTAs per SM;
+// then taller weight bands (32 or 64 rows) leave room for the tiles to run
+// side by side on grid.z, so each CTA reads its tokens' activations once.
+GemvPlan plan_gemv_rows(const GemvPlan& base, int N, int M);
 size_t gemv_smem_bytes(const GemvPlan& plan, int group);
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
                         const GemvArgs& args, cudaStream_t stream, bool pdl);

@@ -170,6 +170,8 @@ void QuantizedLinear::finalize() {
   DeviceContext& ctx = device_context(device_);
   plan_ = cq::plan_gemv(N_, K_, ctx.num_sms);
   wmap_ = make_map_2d(q_, 1, N_, K_, K_, 16 * plan_.rt, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
+  for (int i = 0; i < 3; ++i)
+    wmap_rt_[i] = make_map_2d(q_, 1, N_, K_, K_, 16 << i, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
   qmap_gemm_ = make_map_2d(q_, 1, N_, K_, K_, cq::kGemmBN, 64, CU_TENSOR_MAP_SWIZZLE_64B);
   gemm_ok_ = check_f16_range();
   if (gemm_ok_) {
@@ -480,7 +482,9 @@ void QuantizedLinear::forward_array(const void* x, int ldx, int rows, void* y, i
   a.ldy = ldy;
   a.sb_per_cta = plan_.sb_per_cta;
   a.act = act;
-  check_cuda(cq::launch_gemv(dtype_, group_, plan_, wmap_, a, stream, pdl_enabled()), "qgemv");
+  const cq::GemvPlan plan = cq::plan_gemv_rows(plan_, N_, rows);
+  const CUtensorMap& wmap = plan.rt == plan_.rt ? wmap_ : wmap_rt_[plan.rt == 1 ? 0 : plan.rt == 2 ? 1 : 2];
+  check_cuda(cq::launch_gemv(dtype_, group_, plan, wmap, a, stream, pdl_enabled()), "qgemv");
 }
 
 void QuantizedLinear::forward_f32(const float* input, size_t input_len, int rows, float* output,

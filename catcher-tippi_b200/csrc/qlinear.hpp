@@ -120,6 +120,7 @@ class QuantizedLinear {
   void* bias_ = nullptr;
   cq::GemvPlan plan_{};
   CUtensorMap wmap_{};
+  CUtensorMap wmap_rt_[3]{};  // weight maps with 16, 32 and 64-row boxes (plan_gemv_rows)
   // K2: packed weights with a 64-byte swizzle; scales/biases fit f16
   CUtensorMap qmap_gemm_{};
   bool gemm_ok_ = false;
