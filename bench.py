@@ -677,6 +677,11 @@ def run_reference(args, rank: int) -> dict | None:
 
 
 def main() -> None:
+    # stdout carries exactly one JSON line (rank 0); anything else that a
+    # library prints (NCCL's banner, warnings) goes to stderr
+    json_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+    sys.stdout = sys.stderr
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
@@ -708,7 +713,8 @@ def main() -> None:
     line = run_reference(args, rank) if args.impl == "reference" else run_ours(
         args, rank, world, local_rank)
     if line is not None:
-        print(json.dumps(line), flush=True)
+        json_out.write(json.dumps(line) + "\n")
+        json_out.flush()
 
 
 if __name__ == "__main__":
