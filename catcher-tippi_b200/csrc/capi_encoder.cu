@@ -78,6 +78,15 @@ cq_status cq_encoder_set_tensor(cq_encoder* enc, const char* name, const float* 
   });
 }
 
+cq_status cq_encoder_bind_artifact(cq_encoder* enc, const cq_artifact* art) {
+  return guarded([&] {
+    need_handle(enc, "encoder");
+    need_handle(art, "artifact");
+    enc->borrowed.clear();
+    nemotron_cuda::load_encoder_artifact(*enc->impl, *art->impl);
+  });
+}
+
 cq_status cq_encoder_get_tensor(const cq_encoder* enc, const char* name, float* values, size_t len) {
   return guarded([&] {
     need_handle(enc, "encoder");

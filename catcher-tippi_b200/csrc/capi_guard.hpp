@@ -4,9 +4,13 @@
 // calls (crates/catcher-ffi/src/lib.rs:703-722, :779-786).
 #pragma once
 
+#include <memory>
 #include <new>
 #include <string>
+#include <vector>
 
+#include "artifact.hpp"
+#include "cqartifact.h"
 #include "cqlinear.h"
 #include "qlinear.hpp"
 
@@ -49,4 +53,10 @@ struct cq_linear {
   std::unique_ptr<nemotron_cuda::QuantizedLinear> owned;
   nemotron_cuda::QuantizedLinear* impl = nullptr;
   bool borrowed = false;
+};
+
+// An opened artifact and its manifest names (cq_artifact_tensor_name order).
+struct cq_artifact {
+  std::unique_ptr<nemotron_cuda::Artifact> impl;
+  std::vector<std::string> names;
 };

@@ -73,6 +73,15 @@ cq_status cq_rnnt_set_tensor(cq_rnnt* dec, const char* name, const float* values
   });
 }
 
+cq_status cq_rnnt_bind_artifact(cq_rnnt* dec, const cq_artifact* art) {
+  return guarded([&] {
+    need_handle(dec, "decoder");
+    need_handle(art, "artifact");
+    dec->borrowed.clear();
+    nemotron_cuda::load_rnnt_artifact(*dec->impl, *art->impl);
+  });
+}
+
 cq_status cq_rnnt_get_tensor(const cq_rnnt* dec, const char* name, float* values, size_t len) {
   return guarded([&] {
     need_handle(dec, "decoder");

@@ -101,6 +101,21 @@ def lib() -> ctypes.CDLL:
         "cq_rnnt_state_set_persistent": ([vp, i32], i32),
         "cq_rnnt_state_reset": ([vp], i32),
         "cq_rnnt_state_destroy": ([vp], None),
+        # release artifacts (include/cqartifact.h)
+        "cq_artifact_open": ([ctypes.c_char_p, pp], i32),
+        "cq_artifact_close": ([vp], None),
+        "cq_artifact_model_id": ([vp], ctypes.c_char_p),
+        "cq_artifact_format_version": ([vp], i32),
+        "cq_artifact_tensor_count": ([vp], i32),
+        "cq_artifact_tensor_name": ([vp, i32], ctypes.c_char_p),
+        "cq_artifact_tensor_info": ([vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int32),
+                                     ctypes.POINTER(ctypes.c_int64), i32,
+                                     ctypes.POINTER(ctypes.c_int32),
+                                     ctypes.POINTER(ctypes.c_int32)], i32),
+        "cq_artifact_f16_to_f32": ([vp, ctypes.c_char_p, vp, sz], i32),
+        "cq_linear_from_artifact": ([vp, ctypes.c_char_p, ctypes.c_char_p, i32, i32, pp], i32),
+        "cq_encoder_bind_artifact": ([vp, vp], i32),
+        "cq_rnnt_bind_artifact": ([vp, vp], i32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -181,6 +196,16 @@ class QuantizedLinear:
         h = ctypes.c_void_p()
         _check(lib().cq_linear_create(_ptr(qweight), _ptr(scales), _ptr(biases), _ptr(bias), n,
                                       k4 * 4, group_size, DTYPES[dtype], device, ctypes.byref(h)))
+        return cls(h)
+
+    @classmethod
+    def from_artifact(cls, artifact, weight_name: str, bias_name: str | None = None,
+                      dtype: str = "f16", device: int = 0) -> "QuantizedLinear":
+        """QuantizedLinear::from_artifact (layers.rs:222-256) from an opened Artifact."""
+        h = ctypes.c_void_p()
+        _check(lib().cq_linear_from_artifact(artifact._h, weight_name.encode(),
+                                             None if bias_name is None else bias_name.encode(),
+                                             DTYPES[dtype], device, ctypes.byref(h)))
         return cls(h)
 
     @classmethod
@@ -274,13 +299,9 @@ class PointwiseConv1d:
 
     @classmethod
     def from_device(cls, qweight, scales, biases, bias, group_size: int, dtype: str = "bf16",
-                    device: int = 0) -> "QuantizedLinear":
-        """Packed torch device tensors (q int32/uint32 [N, K/4]; scales/biases T) -> layer copy."""
-        n, k4 = qweight.shape
-        h = ctypes.c_void_p()
-        _check(lib().cq_linear_create(_ptr(qweight), _ptr(scales), _ptr(biases), _ptr(bias), n,
-                                      k4 * 4, group_size, DTYPES[dtype], device, ctypes.byref(h)))
-        return cls(h)
+                    device: int = 0) -> "PointwiseConv1d":
+        return cls(QuantizedLinear.from_device(qweight, scales, biases, bias, group_size, dtype,
+                                               device))
 
     @classmethod
     def from_f32(cls, weight, output_dims, input_dims, bias, group_size, dtype="f16", device=0):

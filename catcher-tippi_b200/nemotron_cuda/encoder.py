@@ -63,6 +63,16 @@ class Encoder:
         _check(lib().cq_encoder_init_random(e._h, ctypes.c_uint64(seed)))
         return e
 
+    def bind_artifact(self, artifact) -> None:
+        """Binds every tensor from an opened Artifact (from_artifact)."""
+        _check(lib().cq_encoder_bind_artifact(self._h, artifact._h))
+
+    @classmethod
+    def from_artifact(cls, artifact, cfg=None, dtype: str = "f16", device: int = 0) -> "Encoder":
+        m = cls(cfg, dtype, device)
+        m.bind_artifact(artifact)
+        return m
+
     def tensor_names(self) -> list[str]:
         n = lib().cq_encoder_tensor_count(self._h)
         return [lib().cq_encoder_tensor_name(self._h, i).decode() for i in range(n)]
