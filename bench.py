@@ -44,6 +44,7 @@ UNIT = "GB/s"
 GROUP = 64
 M_FRAMES = 14
 N_BLOCKS = 24
+ENCODER_LAYERS = 24
 POS_ROWS = 139
 
 # name, N, K, rows, act, input (name of a producer or "x0" / "pe"), input columns used
@@ -71,10 +72,22 @@ WORKLOAD = ("quantized linears of the 24-block FastConformer encoder for one 112
             "at batch 1 (M=14; pos-proj M=139), bf16, INT8 group 64, 24 distinct weight sets")
 
 
+def set_blocks(n: int) -> None:
+    """Fewer blocks for small profiling captures (the workload line says so)."""
+    global N_BLOCKS, STEP_BYTES, LAUNCHES_PER_STEP, WORKLOAD
+    N_BLOCKS = n
+    STEP_BYTES = N_BLOCKS * BLOCK_BYTES
+    LAUNCHES_PER_STEP = N_BLOCKS * len(BLOCK)
+    WORKLOAD = WORKLOAD.replace("24-block", f"{n}-block").replace("24 distinct", f"{n} distinct")
+
+
 # DRAM bytes (read + write) per algorithmic byte of K1, from one ncu capture of
 # the 4096x1024 linear at M = 14 (4.531 MB for 4.600 MB algorithmic); traffic
 # grows with the bytes a launch streams, so it is scaled to the average launch.
 K1_TRAFFIC_PER_ALGO_BYTE = 4.5312e6 / 4599808
+# The same ratio for the persistent chain kernel (qchain_kernel), from one ncu
+# capture of a 2-block chain; 1.0 until that capture is summarised.
+CHAIN_TRAFFIC_PER_ALGO_BYTE = 1.0
 
 
 def measured_tensor_peak() -> tuple[float, str]:
@@ -183,23 +196,42 @@ class EncoderLinears:
                      for nm, n, k, m, act, src in BLOCK]
         self.x0 = torch.randn((rows, 1024), generator=gen, device=dev).to(bf)
         self.pe = torch.randn((POS_ROWS, 1024), generator=gen, device=dev).to(bf)
-        self.out = {name: torch.empty((m, n), dtype=bf, device=dev)
-                    for name, n, _, m, _, _ in self.spec}
+        # the batch-1 chain keeps every block's outputs (no buffer reuse, so the
+        # persistent chain needs no completion waits); the batched workload
+        # reuses one set
+        sets = N_BLOCKS if rows == M_FRAMES else 1
+        self.outs = [{name: torch.empty((m, n), dtype=bf, device=dev)
+                      for name, n, _, m, _, _ in self.spec} for _ in range(sets)]
+        self.out = self.outs[-1]
 
-    def launch_step(self, stream_ptr: int) -> None:
-        """All 24 blocks' linears, each consuming its producer's output."""
-        for blk in self.layers:
+    def steps(self):
+        """(layer, x, y, act, rows) of every linear, in launch order."""
+        out = []
+        for b, blk in enumerate(self.layers):
+            cur = self.outs[b % len(self.outs)]
+            prev = self.outs[(b - 1) % len(self.outs)]
             for layer, (name, n, k, m, act, src) in zip(blk, self.spec):
                 if src == "x0":
-                    # block input: the previous block's output (or the chunk input)
-                    x = self.x0 if blk is self.layers[0] else self.out["ffn2_down"]
+                    x = self.x0 if b == 0 else prev["ffn2_down"]
                 elif src == "pe":
                     x = self.pe
                 else:
-                    x = self.out[src]
-                y = self.out[name]
-                layer.forward_raw(x.data_ptr(), x.stride(0), m, y.data_ptr(), y.stride(0), act,
-                                  stream_ptr)
+                    x = cur[src]
+                out.append((layer, x, cur[name], act, m))
+        return out
+
+    def use_chain(self) -> None:
+        """Run every step as one persistent launch (include/cqchain.h)."""
+        self.chain = self.cq.LinearChain(self.steps())
+
+    def launch_step(self, stream_ptr: int) -> None:
+        """All 24 blocks' linears, each consuming its producer's output."""
+        if getattr(self, "chain", None) is not None:
+            self.chain.run_raw(stream_ptr)
+            return
+        for layer, x, y, act, m in self.steps():
+            layer.forward_raw(x.data_ptr(), x.stride(0), m, y.data_ptr(), y.stride(0), act,
+                              stream_ptr)
 
 
 class SingleLinear:
@@ -252,8 +284,8 @@ def encoder_flops_per_chunk(streams: int) -> int:
     The position projection (83 rows) is shared by the streams of a state."""
     q = 14
     block = (2 * 4096 * 1024 * 2 + 3072 * 1024 + 1024 * 1024 + 2048 * 1024 + 1024 * 1024)
-    f = streams * q * block * N_BLOCKS
-    f += (56 + 14 + 14 - 1) * 1024 * 1024 * N_BLOCKS  # relative_k_proj
+    f = streams * q * block * ENCODER_LAYERS
+    f += (56 + 14 + 14 - 1) * 1024 * 1024 * ENCODER_LAYERS  # relative_k_proj
     f += streams * (28 * 33 * 256 * 256 + 14 * 17 * 256 * 256 + q * 4352 * 1024)
     f += streams * q * (1152 * 2048 + 2048 * 1024)
     return 2 * f
@@ -476,6 +508,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         enc = EncoderLinears(torch, cq, local_rank)
         step_bytes, launches, workload = STEP_BYTES, LAUNCHES_PER_STEP, WORKLOAD
         in_shape = (M_FRAMES, 1024)
+        if args.chain:
+            enc.use_chain()
+            launches = 1
 
     # eager warm-up (sets kernel attributes before capture), then capture.
     stream = torch.cuda.Stream()
@@ -554,6 +589,13 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                 "traffic_note": "bytes per launch, scaled from the ncu capture of the 4096x1024 "
                                 "linear (dram read+write / algorithmic = 0.985)",
                 "kernel": "qgemv_kernel (K1)", "avg_launch_us": round(per_launch_us, 3)}
+    chained = getattr(enc, "chain", None) is not None
+    if chained:
+        roofline.update({
+            "traffic": round(CHAIN_TRAFFIC_PER_ALGO_BYTE * step_bytes),
+            "traffic_note": "bytes per launch, scaled by blocks from the ncu capture of a "
+                            "2-block chain (dram read+write / algorithmic bytes)",
+            "kernel": "qchain_kernel (persistent linear chain, one launch per step)"})
     if step_flops is not None:
         tpeak, tkind = measured_tensor_peak()
         tflops = step_flops / (ms_step * 1e-3) / 1e12
@@ -571,12 +613,16 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                    "bytes_per_step_per_gpu": step_bytes, "launches_per_step": launches,
                    "l2": "inputs larger than L2 (distinct weights per step exceed 126 MB)",
                    "parallelism": f"dp{world} (replicated weights, independent streams)",
-                   "graph": "one CUDA graph per step, programmatic dependent launch edges"},
+                   "graph": ("one CUDA graph per step holding one persistent cooperative "
+                             "launch of all 216 linears" if chained else
+                             "one CUDA graph per step, programmatic dependent launch edges")},
         "e2e": {"value": round(value_e2e, 2), "unit": UNIT,
                 "h2d_bytes_per_step": host_in.numel() * 2,
                 "d2h_bytes_per_step": host_out.numel() * 2,
-                "path": "C-ABI cq_linear_forward_ex calls captured in a CUDA graph with the "
-                        "pinned-host input copy and output read inside the timed region"},
+                "path": ("C-ABI cq_linear_chain_run" if chained else
+                         "C-ABI cq_linear_forward_ex calls") +
+                        " captured in a CUDA graph with the pinned-host input copy and output "
+                        "read inside the timed region"},
         "gpu_launches": launches * args.steps,
         "roofline": roofline,
         "clocks": clock_info,
@@ -700,11 +746,19 @@ def main() -> None:
     ap.add_argument("--encoder-chunks", type=int, default=20,
                     help="timed chunks of the encoder measurement in the default run")
     ap.add_argument("--no-encoder", action="store_true")
+    ap.add_argument("--blocks", type=int, default=N_BLOCKS,
+                    help="FastConformer blocks in the linear workloads (24 in the encoder; "
+                         "fewer only for small profiling captures)")
+    ap.add_argument("--chain", action="store_true",
+                    help="block workload: the persistent linear chain (one launch per step) "
+                         "instead of one K1 launch per linear")
     ap.add_argument("--no-rnnt", action="store_true",
                     help="encoder workload without the RNNT decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     args = ap.parse_args()
+    if args.blocks != N_BLOCKS:
+        set_blocks(args.blocks)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -21,20 +21,12 @@
 //    fp32 partial into the leader CTA's shared memory (distributed shared
 //    memory stores), one cluster barrier, and the leader finishes the
 //    epilogue.  No global scratch, no atomics, deterministic order.
-//  * Tensor cores via mma.m16n8k16 (f16 x f16 -> f32): weight rows are the MMA
-//    M dimension, tokens the N dimension.  A weight byte q becomes the f16
-//    value 1024 + q with one PRMT (bits 0x64qq), exact; the 1024 offset is
-//    folded into the group bias term:
-//        y += s * sum(x * (1024 + q)) + (b - 1024 s) * sum(x)
-//    so the dequantised weight is never rounded.  bf16 activations are moved
-//    to f16 with a per-(token, 64-wide sub-block) power-of-two scale that is
-//    undone in fp32, which is exact for every element within 2^-28 of the
-//    block's largest magnitude.
-//  * Each lane reads 16 contiguous weight bytes per row; the k-slot order of
-//    the MMA fragments is permuted identically for A and B, so the MLX layout
-//    is consumed as is (no repacking) and shared-memory reads are
-//    conflict-free.
+//  * Tensor cores via mma.m16n8k16 on the exact f16 image 1024 + q of each
+//    weight byte, with the offset folded into the group bias term; the
+//    per-sub-block arithmetic is shared with the chain executor
+//    (gemv_core.cuh).
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "qgemv.hpp"
 
 #include <algorithm>
@@ -76,95 +68,6 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int rt, int sb_per_cta, int
   off += static_cast<size_t>(ksplit > 1 ? ksplit : 0) * rb * 16 * sizeof(float);
   L.total = off;
   return L;
-}
-
-// Raw activation loads of one token for one 64-wide sub-block (this lane's 16
-// values; zeros past M and past K):
-//   G >= 64: k = kb + 16c + [0, 16)
-//   G == 32: k = kb + 8c + [0, 8) and kb + 32 + 8c + [0, 8)
-template <int G>
-__device__ __forceinline__ void load_x_raw(const void* __restrict__ x, int ldx, int M, int K, int m,
-                                           int kb, int c, uint4& r0, uint4& r1) {
-  r0 = make_uint4(0, 0, 0, 0);
-  r1 = make_uint4(0, 0, 0, 0);
-  if (m >= M) return;
-  const uint16_t* xr = reinterpret_cast<const uint16_t*>(x) + static_cast<size_t>(m) * ldx;
-  if constexpr (G >= 64) {
-    r0 = ld_global_cg_v4(xr + kb + 16 * c);
-    r1 = ld_global_cg_v4(xr + kb + 16 * c + 8);
-  } else {
-    r0 = ld_global_cg_v4(xr + kb + 8 * c);
-    if (kb + 32 < K) r1 = ld_global_cg_v4(xr + kb + 32 + 8 * c);
-  }
-}
-
-// Converts this lane's 16 raw activation values into f16 MMA B-fragments and
-// returns the per-half sums of the converted values (reduced over the 4 lanes
-// of the quad) and the inverse of the power-of-two scale that was applied.
-template <int DT, int G>
-__device__ __forceinline__ void x_frag(const uint4& r0, const uint4& r1, uint32_t (&xb)[8],
-                                       float (&xs)[2], float& inv) {
-  const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-  float s0 = 0.f, s1 = 0.f;
-  if constexpr (DT == kF16) {
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      xb[p] = w[p];
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[p]));
-      if (p < 4) s0 += f.x + f.y;
-      else s1 += f.x + f.y;
-    }
-    inv = 1.0f;
-  } else {
-    float v[16];
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      v[2 * p] = __uint_as_float(w[p] << 16);
-      v[2 * p + 1] = __uint_as_float(w[p] & 0xFFFF0000u);
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
-    // scale = 2^(14 - floor(log2 amax)) puts the block maximum in [2^14, 2^15).
-    const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
-    int sh = e == 0 ? 0 : 141 - e;
-    sh = max(-126, min(126, sh));
-    const float scale = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
-    inv = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      const __half2 h = __floats2half2_rn(v[2 * p] * scale, v[2 * p + 1] * scale);
-      xb[p] = *reinterpret_cast<const uint32_t*>(&h);
-      const float2 f = __half22float2(h);
-      if (p < 4) s0 += f.x + f.y;
-      else s1 += f.x + f.y;
-    }
-  }
-  s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
-  s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
-  s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
-  s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
-  if constexpr (G >= 64) {
-    xs[0] = s0 + s1;
-    xs[1] = 0.f;
-  } else {
-    xs[0] = s0;
-    xs[1] = s1;
-  }
-}
-
-template <int DT>
-__device__ __forceinline__ float epilogue_value(float acc, bool has_bias, float bias, int act) {
-  float o = round_t<DT>(acc);
-  if (has_bias) o = round_t<DT>(o + bias);
-  if (act == kActSilu) {
-    o = round_t<DT>(o / (1.0f + expf(-o)));
-  } else if (act == kActRelu) {
-    o = o > 0.0f ? o : 0.0f;
-  }
-  return o;
 }
 
 __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
@@ -283,88 +186,12 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int u = 0; u < kSbPerWarp; ++u) {
       const int j = warp + u * kNW;
       if (j >= sbn) break;
-      uint32_t xb[2][8];
-      float xs[2][2], inv[2];
-      x_frag<DT, G>(xr[u][0][0], xr[u][0][1], xb[0], xs[0], inv[0]);
-      x_frag<DT, G>(xr[u][1][0], xr[u][1][1], xb[1], xs[1], inv[1]);
-      // Token-side epilogue operands for the accumulator columns 2c, 2c+1.
-      float xsA[2][SUBG], xsB[2][SUBG], ivA[2], ivB[2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-        for (int h = 0; h < SUBG; ++h) {
-          xsA[nt][h] = __shfl_sync(0xFFFFFFFFu, xs[nt][h], 8 * c);
-          xsB[nt][h] = __shfl_sync(0xFFFFFFFFu, xs[nt][h], 8 * c + 4);
-        }
-        ivA[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c);
-        ivB[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c + 4);
-      }
+      const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
 
       if (first_tile) ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
 
-      const uint8_t* wj = wt + static_cast<size_t>(j) * RB * 64;
-      const float2* sbj = sbsm + static_cast<size_t>(j) * SUBG * RB;
-#pragma unroll
-      for (int i = 0; i < RT; ++i) {
-        const int ra = 16 * i + r4, rb = ra + 8;
-        uint32_t wa[4], wb[4];
-        if constexpr (G >= 64) {
-          const uint4 va = *reinterpret_cast<const uint4*>(wj + ra * 64 + 16 * c);
-          const uint4 vb = *reinterpret_cast<const uint4*>(wj + rb * 64 + 16 * c);
-          wa[0] = va.x; wa[1] = va.y; wa[2] = va.z; wa[3] = va.w;
-          wb[0] = vb.x; wb[1] = vb.y; wb[2] = vb.z; wb[3] = vb.w;
-        } else {
-          const uint2 a0 = *reinterpret_cast<const uint2*>(wj + ra * 64 + 8 * c);
-          const uint2 a1 = *reinterpret_cast<const uint2*>(wj + ra * 64 + 32 + 8 * c);
-          const uint2 b0 = *reinterpret_cast<const uint2*>(wj + rb * 64 + 8 * c);
-          const uint2 b1 = *reinterpret_cast<const uint2*>(wj + rb * 64 + 32 + 8 * c);
-          wa[0] = a0.x; wa[1] = a0.y; wa[2] = a1.x; wa[3] = a1.y;
-          wb[0] = b0.x; wb[1] = b0.y; wb[2] = b1.x; wb[3] = b1.y;
-        }
-        float d[2][SUBG][4];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int h = 0; h < SUBG; ++h)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) d[nt][h][e] = 0.f;
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const int h = (SUBG == 2) ? (s >> 1) : 0;  // constant after unrolling
-          // bytes 4s..4s+3 of this lane's 16: (b0,b1) -> k-slots 2c,2c+1;
-          // (b2,b3) -> k-slots 2c+8, 2c+9.  0x64qq is the f16 value 1024 + q.
-          const uint32_t a0 = __byte_perm(wa[s], 0x64646464u, 0x4140);
-          const uint32_t a1 = __byte_perm(wb[s], 0x64646464u, 0x4140);
-          const uint32_t a2 = __byte_perm(wa[s], 0x64646464u, 0x4342);
-          const uint32_t a3 = __byte_perm(wb[s], 0x64646464u, 0x4342);
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
-            mma_16816_f16(d[nt][h], a0, a1, a2, a3, xb[nt][2 * s], xb[nt][2 * s + 1]);
-        }
-#pragma unroll
-        for (int h = 0; h < SUBG; ++h) {
-          const float2 sa = sbj[h * RB + ra];
-          const float2 sb = sbj[h * RB + rb];
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const float t0 = fmaf(sa.x, d[nt][h][0], sa.y * xsA[nt][h]);
-            const float t1 = fmaf(sa.x, d[nt][h][1], sa.y * xsB[nt][h]);
-            const float t2 = fmaf(sb.x, d[nt][h][2], sb.y * xsA[nt][h]);
-            const float t3 = fmaf(sb.x, d[nt][h][3], sb.y * xsB[nt][h]);
-            if constexpr (DT == kF16) {
-              acc[i][nt][0] += t0;
-              acc[i][nt][1] += t1;
-              acc[i][nt][2] += t2;
-              acc[i][nt][3] += t3;
-            } else {
-              acc[i][nt][0] = fmaf(t0, ivA[nt], acc[i][nt][0]);
-              acc[i][nt][1] = fmaf(t1, ivB[nt], acc[i][nt][1]);
-              acc[i][nt][2] = fmaf(t2, ivA[nt], acc[i][nt][2]);
-              acc[i][nt][3] = fmaf(t3, ivB[nt], acc[i][nt][3]);
-            }
-          }
-        }
-      }
+      subblock_mma<DT, G, RT>(wt + static_cast<size_t>(j) * RB * 64,
+                              sbsm + static_cast<size_t>(j) * SUBG * RB, xo, lane, acc);
     }
 
     first_tile = false;

@@ -105,6 +105,8 @@ class QuantizedLinear {
   const void* scales() const { return scales_; }
   const void* biases() const { return biases_; }
   const void* bias() const { return bias_; }
+  // K1 weight map with a (64 k x 16*rt rows) box, rt in {1, 2, 4}.
+  const CUtensorMap& gemv_map(int rt) const { return wmap_rt_[rt == 1 ? 0 : rt == 2 ? 1 : 2]; }
 
  private:
   QuantizedLinear(int N, int K, int group, cq_dtype dtype, int device);
