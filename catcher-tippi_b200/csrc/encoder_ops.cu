@@ -189,79 +189,135 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
 
 // ------------------------------------------------------------------ attention
 
-struct AttnSmem {
-  float *qu, *qv, *k, *v, *r, *p;
+// Tensor-core attention core.  One CTA (eight warps) per (stream, head, query
+// group of at most 16): the group's queries with both position biases, the
+// window's keys and values and the position rows are staged as T in shared
+// memory, and three small products run on mma.m16n8k16 with fp32 accumulation:
+//   AC = (q + bias_u) K^T,  BD = (q + bias_v) R^T,  out = softmax(...) V.
+// K, R and V are T values already (exact MMA operands); the fp32 operands
+// (q + bias, probabilities) enter as a T "hi" part plus a T "lo" remainder,
+// two MMAs each, so products keep ~16 more bits than a single rounding.
+constexpr int kAttnThreads = 256;
+constexpr int kAttnMaxQ = 16;
+
+struct AttnLayout {
+  int lds;         // T elements per staged row (head_dim + 8: conflict-free fragments)
+  int kr, rr, vr;  // padded rows of keys (x8), position rows (x8), values (x16)
+  int ldp;         // T elements per probability row (vr + 8)
+  size_t q, k, r, v, ac, bd, p, total;  // byte offsets
 };
 
-// Rows of K and R are padded to head_dim + 4 floats: 16-byte aligned rows
-// whose starts fall in different banks, so a warp's float4 reads of 32
-// consecutive rows run at the shared-memory peak.
-__host__ __device__ inline size_t attn_floats(int rows_q, int vmax, int hd, AttnSmem* s, float* base) {
-  const size_t hp = static_cast<size_t>(hd) + 4;
-  const size_t sizes[6] = {rows_q * hp, rows_q * hp, vmax * hp, static_cast<size_t>(vmax) * hd,
-                           (vmax + rows_q - 1) * hp, static_cast<size_t>(rows_q) * vmax};
-  size_t off = 0;
-  float** dst[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
-  if (s != nullptr) {
-    dst[0] = &s->qu; dst[1] = &s->qv; dst[2] = &s->k; dst[3] = &s->v; dst[4] = &s->r; dst[5] = &s->p;
-  }
-  for (int i = 0; i < 6; ++i) {
-    if (s != nullptr) *dst[i] = base + off;
-    off += (sizes[i] + 3) / 4 * 4;  // keep every array 16-byte aligned
-  }
-  return off;
+__host__ __device__ inline size_t attn_take(size_t& off, size_t bytes) {
+  const size_t o = off;
+  off += (bytes + 15) / 16 * 16;
+  return o;
 }
 
-// Copies `rows` rows of hd T values into f32 shared memory (row stride ld_s
-// floats); src(j) gives the element offset of row j.  Eight 16-byte loads are
-// in flight per thread before any store.
-template <int DT, class Src>
-__device__ __forceinline__ void stage_rows(float* dst, int ld_s, int rows, int hd, Src src) {
+__host__ __device__ inline AttnLayout attn_layout(int vmax, int hd) {
+  AttnLayout L;
+  L.lds = hd + 8;
+  L.kr = (vmax + 7) / 8 * 8;
+  L.rr = (vmax + kAttnMaxQ - 1 + 7) / 8 * 8;
+  L.vr = (vmax + 15) / 16 * 16;
+  L.ldp = L.vr + 8;
+  size_t off = 0;
+  L.q = attn_take(off, 4ull * kAttnMaxQ * L.lds * 2);  // (q+bu) hi, lo, (q+bv) hi, lo
+  L.k = attn_take(off, static_cast<size_t>(L.kr) * L.lds * 2);
+  L.r = attn_take(off, static_cast<size_t>(L.rr) * L.lds * 2);
+  L.v = attn_take(off, static_cast<size_t>(L.vr) * L.lds * 2);
+  L.ac = attn_take(off, static_cast<size_t>(kAttnMaxQ) * L.kr * 4);
+  L.bd = attn_take(off, static_cast<size_t>(kAttnMaxQ) * L.rr * 4);
+  L.p = attn_take(off, 2ull * kAttnMaxQ * L.ldp * 2);  // probabilities hi, lo
+  L.total = off;
+  return L;
+}
+
+template <int DT>
+__device__ __forceinline__ void mma_t(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                      uint32_t b1) {
+  if constexpr (DT == kBF16) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// A fragment (16 rows x 16 columns from column k0) of a row-major T tile.
+__device__ __forceinline__ void frag_a(uint32_t (&a)[4], const uint16_t* tile, int ld, int k0,
+                                       int g, int c) {
+  a[0] = *reinterpret_cast<const uint32_t*>(tile + g * ld + k0 + 2 * c);
+  a[1] = *reinterpret_cast<const uint32_t*>(tile + (g + 8) * ld + k0 + 2 * c);
+  a[2] = *reinterpret_cast<const uint32_t*>(tile + g * ld + k0 + 8 + 2 * c);
+  a[3] = *reinterpret_cast<const uint32_t*>(tile + (g + 8) * ld + k0 + 8 + 2 * c);
+}
+
+// Two 8x8 T matrices (rows r0..r0+15 of a row-major tile, columns c0..c0+7),
+// transposed into the B fragment of one k16 x n8 step.
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& b0, uint32_t& b1, const uint16_t* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(b0), "=r"(b1)
+               : "r"(smem_u32(p)));
+}
+
+// Copies `rows` rows of hd T values (src(j) gives row j) into a staged tile,
+// zero-filling rows [rows, rows_pad); eight 16-byte loads in flight per thread.
+template <class Src>
+__device__ __forceinline__ void stage_t_rows(uint16_t* dst, int ld, int rows, int rows_pad, int hd,
+                                             Src src) {
   const int per_row = hd / 8;
-  const int n = rows * per_row;
+  const int n = rows_pad * per_row;
   constexpr int kBatch = 8;
   for (int base = threadIdx.x; base < n; base += blockDim.x * kBatch) {
     uint4 u[kBatch];
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int i = base + b * blockDim.x;
-      if (i < n) {
-        const int j = i / per_row, c = (i % per_row) * 8;
-        u[b] = *reinterpret_cast<const uint4*>(src(j) + c);
-      }
+      u[b] = make_uint4(0, 0, 0, 0);
+      if (i < n && i / per_row < rows) u[b] = *reinterpret_cast<const uint4*>(src(i / per_row) + (i % per_row) * 8);
     }
 #pragma unroll
     for (int b = 0; b < kBatch; ++b) {
       const int i = base + b * blockDim.x;
-      if (i < n) {
-        const int j = i / per_row, c = (i % per_row) * 8;
-        float x[8];
-        unpack8<DT>(u[b], x);
-        float4* d = reinterpret_cast<float4*>(dst + static_cast<size_t>(j) * ld_s + c);
-        d[0] = make_float4(x[0], x[1], x[2], x[3]);
-        d[1] = make_float4(x[4], x[5], x[6], x[7]);
-      }
+      if (i < n) *reinterpret_cast<uint4*>(dst + (i / per_row) * ld + (i % per_row) * 8) = u[b];
     }
   }
 }
 
-// One CTA per (stream, head, query group).  With V visible frames (cached +
-// current) and position rows ordered from V-1 down to -(V-1), the reference's
-// relative shift (pad, flatten, drop Q entries) reads raw[q][key + Q - 1 - q];
-// the kernel reads that row directly.  Position rows depend only on the
+// With V visible frames (cached + current) and position rows ordered from V-1
+// down to -(V-1), the reference's relative shift (pad, flatten, drop Q
+// entries) reads raw[q][key + Q - 1 - q]; position rows depend only on the
 // position value, so one table of vmax + Q - 1 rows serves every V.
 template <int DT>
-__global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
-  extern __shared__ __align__(16) float smem[];
+__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
   const int qsplit = a.qsplit;
   const int sh = blockIdx.x / qsplit, qg = blockIdx.x % qsplit;
   const int s = sh / a.heads, h = sh % a.heads;
-  const int hd = a.head_dim, hp = hd + 4, Q = a.Q, D = a.D, vmax = a.vmax;
+  const int hd = a.head_dim, Q = a.Q, D = a.D, vmax = a.vmax;
   const int qn_max = (Q + qsplit - 1) / qsplit;
   const int q0 = qg * qn_max;
   const int qn = min(Q, q0 + qn_max) - q0;
-  AttnSmem sm;
-  attn_floats(qn_max, vmax, hd, &sm, smem);
+  const AttnLayout L = attn_layout(vmax, hd);
+  uint16_t* sq = reinterpret_cast<uint16_t*>(smem_raw + L.q);
+  uint16_t* quh = sq;
+  uint16_t* qul = sq + kAttnMaxQ * L.lds;
+  uint16_t* qvh = sq + 2 * kAttnMaxQ * L.lds;
+  uint16_t* qvl = sq + 3 * kAttnMaxQ * L.lds;
+  uint16_t* sk = reinterpret_cast<uint16_t*>(smem_raw + L.k);
+  uint16_t* sr = reinterpret_cast<uint16_t*>(smem_raw + L.r);
+  uint16_t* sv = reinterpret_cast<uint16_t*>(smem_raw + L.v);
+  float* ac = reinterpret_cast<float*>(smem_raw + L.ac);
+  float* bd = reinterpret_cast<float*>(smem_raw + L.bd);
+  uint16_t* ph = reinterpret_cast<uint16_t*>(smem_raw + L.p);
+  uint16_t* pl = ph + kAttnMaxQ * L.ldp;
   pdl_wait();
   pdl_launch_dependents();
   if (qn <= 0) return;
@@ -286,58 +342,92 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     if (j < cached) return vring + (static_cast<size_t>(s) * ring + (n_prev - cached + j) % ring) * D + col;
     return qkv + (row0 + (j - cached)) * ldqkv + 2 * D + col;
   };
-  // position rows for queries q0..q0+qn-1: smem row i is reference row
+  // position rows for queries q0..q0+qn-1: staged row i is reference row
   // p = i + Q - q0 - qn (the smallest p these queries use), i.e. table row
   // vmax - V + p
   const int p_lo = Q - q0 - qn;
   const int rbase = vmax - V + p_lo;
   auto rel_row = [&](int i) -> const uint16_t* { return relk + static_cast<size_t>(rbase + i) * D + col; };
-  auto query_row = [&](int i) -> const uint16_t* { return qkv + (row0 + q0 + i) * ldqkv + col; };
+  const int nrel = V + qn - 1;
 
-  stage_rows<DT>(sm.k, hp, V, hd, key_row);
-  stage_rows<DT>(sm.v, hd, V, hd, value_row);
-  stage_rows<DT>(sm.r, hp, V + qn - 1, hd, rel_row);
-  stage_rows<DT>(sm.qu, hp, qn, hd, query_row);
-  __syncthreads();
-  for (int i = threadIdx.x; i < qn * hd; i += blockDim.x) {
-    const int q = i / hd, d = i % hd;
-    const float x = sm.qu[q * hp + d];
-    sm.qu[q * hp + d] = x + a.bias_u[col + d];
-    sm.qv[q * hp + d] = x + a.bias_v[col + d];
-  }
-  __syncthreads();
-
-  // scores[q][key] = ((q + bias_u) . k + (q + bias_v) . rel[key + Q - 1 - q]) * scale
-  for (int pr = threadIdx.x; pr < qn * V; pr += blockDim.x) {
-    const int q = pr / V, j = pr % V;
-    const float4* qu = reinterpret_cast<const float4*>(sm.qu + q * hp);
-    const float4* qv = reinterpret_cast<const float4*>(sm.qv + q * hp);
-    const float4* kr = reinterpret_cast<const float4*>(sm.k + j * hp);
-    // reference row j + Q - 1 - (q0 + q)  ->  smem row (that) - p_lo
-    const float4* rr = reinterpret_cast<const float4*>(sm.r + (j + qn - 1 - q) * hp);
-    float c = 0.0f, r = 0.0f;
-#pragma unroll 8
-    for (int d4 = 0; d4 < hd / 4; ++d4) {
-      const float4 a4 = qu[d4], k4 = kr[d4], b4 = qv[d4], r4 = rr[d4];
-      c = fmaf(a4.x, k4.x, c);
-      c = fmaf(a4.y, k4.y, c);
-      c = fmaf(a4.z, k4.z, c);
-      c = fmaf(a4.w, k4.w, c);
-      r = fmaf(b4.x, r4.x, r);
-      r = fmaf(b4.y, r4.y, r);
-      r = fmaf(b4.z, r4.z, r);
-      r = fmaf(b4.w, r4.w, r);
+  stage_t_rows(sk, L.lds, V, (V + 7) / 8 * 8, hd, key_row);
+  stage_t_rows(sv, L.lds, V, (V + 15) / 16 * 16, hd, value_row);
+  stage_t_rows(sr, L.lds, nrel, (nrel + 7) / 8 * 8, hd, rel_row);
+  // (q + bias_u), (q + bias_v) in fp32, split into T hi + T lo
+  for (int i = threadIdx.x; i < kAttnMaxQ * (hd / 8); i += blockDim.x) {
+    const int q = i / (hd / 8), c8 = (i % (hd / 8)) * 8;
+    float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (q < qn) unpack8<DT>(*reinterpret_cast<const uint4*>(qkv + (row0 + q0 + q) * ldqkv + col + c8), x);
+    uint32_t wh[2][4], wl[2][4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+#pragma unroll
+      for (int uv = 0; uv < 2; ++uv) {
+        const float* bias = uv == 0 ? a.bias_u : a.bias_v;
+        const float v0 = q < qn ? x[e] + bias[col + c8 + e] : 0.0f;
+        const float v1 = q < qn ? x[e + 1] + bias[col + c8 + e + 1] : 0.0f;
+        const uint16_t h0 = f_to_t_bits<DT>(v0), h1 = f_to_t_bits<DT>(v1);
+        const uint16_t l0 = f_to_t_bits<DT>(v0 - t_bits_to_f<DT>(h0));
+        const uint16_t l1 = f_to_t_bits<DT>(v1 - t_bits_to_f<DT>(h1));
+        wh[uv][e / 2] = h0 | (static_cast<uint32_t>(h1) << 16);
+        wl[uv][e / 2] = l0 | (static_cast<uint32_t>(l1) << 16);
+      }
     }
-    sm.p[q * vmax + j] = (c + r) * a.scale;
+    const int o = q * L.lds + c8;
+    *reinterpret_cast<uint4*>(quh + o) = make_uint4(wh[0][0], wh[0][1], wh[0][2], wh[0][3]);
+    *reinterpret_cast<uint4*>(qul + o) = make_uint4(wl[0][0], wl[0][1], wl[0][2], wl[0][3]);
+    *reinterpret_cast<uint4*>(qvh + o) = make_uint4(wh[1][0], wh[1][1], wh[1][2], wh[1][3]);
+    *reinterpret_cast<uint4*>(qvl + o) = make_uint4(wl[1][0], wl[1][1], wl[1][2], wl[1][3]);
   }
   __syncthreads();
 
-  // softmax_in_place per query row (encoder.rs:278-288)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int q = warp; q < qn; q += blockDim.x / 32) {
-    float* row = sm.p + q * vmax;
+  const int g = lane >> 2, c = lane & 3;
+  // ---- AC = (q + bias_u) K^T over ceil(V/8) key tiles, BD = (q + bias_v) R^T
+  const int nk = (V + 7) / 8, nr = (nrel + 7) / 8;
+  for (int t = warp; t < nk + nr; t += kAttnThreads / 32) {
+    const bool is_k = t < nk;
+    const int n0 = (is_k ? t : t - nk) * 8;
+    const uint16_t* src = is_k ? sk : sr;
+    const uint16_t* qh = is_k ? quh : qvh;
+    const uint16_t* ql = is_k ? qul : qvl;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < hd; k0 += 16) {
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(src + (n0 + g) * L.lds + k0 + 2 * c);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(src + (n0 + g) * L.lds + k0 + 8 + 2 * c);
+      uint32_t fa[4];
+      frag_a(fa, qh, L.lds, k0, g, c);
+      mma_t<DT>(acc, fa, b0, b1);
+      frag_a(fa, ql, L.lds, k0, g, c);
+      mma_t<DT>(acc, fa, b0, b1);
+    }
+    float* dst = is_k ? ac : bd;
+    const int ld = is_k ? L.kr : L.rr;
+    dst[g * ld + n0 + 2 * c] = acc[0];
+    dst[g * ld + n0 + 2 * c + 1] = acc[1];
+    dst[(g + 8) * ld + n0 + 2 * c] = acc[2];
+    dst[(g + 8) * ld + n0 + 2 * c + 1] = acc[3];
+  }
+  __syncthreads();
+
+  // ---- scores and softmax_in_place per query row (encoder.rs:278-288);
+  // probabilities as T hi + T lo, zero past V and for padding queries
+  const int vr = (V + 15) / 16 * 16;
+  for (int q = warp; q < kAttnMaxQ; q += kAttnThreads / 32) {
+    uint16_t* rh = ph + q * L.ldp;
+    uint16_t* rl = pl + q * L.ldp;
+    if (q >= qn) {
+      for (int j = lane; j < vr; j += 32) rh[j] = rl[j] = 0;
+      continue;
+    }
+    float* row = ac + q * L.kr;
+    const float* brow = bd + q * L.rr + qn - 1 - q;
     float m = -INFINITY;
-    for (int j = lane; j < V; j += 32) m = fmaxf(m, row[j]);
+    for (int j = lane; j < V; j += 32) {
+      const float sc = (row[j] + brow[j]) * a.scale;
+      row[j] = sc;
+      m = fmaxf(m, sc);
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float tot = 0.0f;
@@ -348,16 +438,35 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttnArgs a) {
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-    for (int j = lane; j < V; j += 32) row[j] = row[j] / tot;
+    for (int j = lane; j < vr; j += 32) {
+      const float pv = j < V ? row[j] / tot : 0.0f;
+      const uint16_t hb = f_to_t_bits<DT>(pv);
+      rh[j] = hb;
+      rl[j] = f_to_t_bits<DT>(pv - t_bits_to_f<DT>(hb));
+    }
   }
   __syncthreads();
 
-  for (int o = threadIdx.x; o < qn * hd; o += blockDim.x) {
-    const int q = o / hd, d = o % hd;
-    const float* pr = sm.p + q * vmax;
-    float acc = 0.0f;
-    for (int j = 0; j < V; ++j) acc = fmaf(pr[j], sm.v[j * hd + d], acc);
-    st_t<DT>(a.out, (row0 + q0 + q) * D + col + d, acc);
+  // ---- out = P V: head_dim / 8 column tiles, k over vr keys
+  for (int nt = warp; nt < hd / 8; nt += kAttnThreads / 32) {
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int k0 = 0; k0 < vr; k0 += 16) {
+      uint32_t b0, b1;
+      ldmatrix_x2_trans(b0, b1, sv + (k0 + (lane & 15)) * L.lds + nt * 8);
+      uint32_t fa[4];
+      frag_a(fa, ph, L.ldp, k0, g, c);
+      mma_t<DT>(acc, fa, b0, b1);
+      frag_a(fa, pl, L.ldp, k0, g, c);
+      mma_t<DT>(acc, fa, b0, b1);
+    }
+    const int d = col + nt * 8 + 2 * c;
+    uint16_t* out = static_cast<uint16_t*>(a.out);
+    if (g < qn)
+      *reinterpret_cast<uint32_t*>(out + (row0 + q0 + g) * D + d) =
+          f_to_t_bits<DT>(acc[0]) | (static_cast<uint32_t>(f_to_t_bits<DT>(acc[1])) << 16);
+    if (g + 8 < qn)
+      *reinterpret_cast<uint32_t*>(out + (row0 + q0 + g + 8) * D + d) =
+          f_to_t_bits<DT>(acc[2]) | (static_cast<uint32_t>(f_to_t_bits<DT>(acc[3])) << 16);
   }
 
   // Append this chunk's keys and values to the window (AttentionKvCache::update).
@@ -695,24 +804,28 @@ cudaError_t launch_layernorm(int dtype, const LnArgs& a, cudaStream_t stream, bo
 }
 
 size_t attention_smem_bytes(int rows_q, int vmax, int head_dim) {
-  return attn_floats(rows_q, vmax, head_dim, nullptr, nullptr) * sizeof(float);
+  (void)rows_q;  // one 16-query tile per CTA
+  return attn_layout(vmax, head_dim).total;
 }
 
 int attention_qsplit(int streams, int heads, int Q, int num_sms) {
-  const int ctas = streams * heads;
-  if (ctas >= num_sms) return 1;
-  const int want = (2 * num_sms + ctas - 1) / ctas;
-  return want < Q ? want : Q;
+  // Every CTA stages the whole window whatever its query count, and its MMA
+  // tiles cover 16 queries: splitting further only repeats that work.
+  (void)streams;
+  (void)heads;
+  (void)num_sms;
+  return (Q + kAttnMaxQ - 1) / kAttnMaxQ;
 }
 
 cudaError_t launch_attention(int dtype, const AttnArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.head_dim % 8 != 0 || a.D % 8 != 0 || a.ldqkv % 8 != 0 || a.qsplit < 1) return cudaErrorInvalidValue;
-  const int qn = (a.Q + a.qsplit - 1) / a.qsplit;
-  const size_t smem = attention_smem_bytes(qn, a.vmax, a.head_dim);
+  if (a.head_dim % 16 != 0 || a.D % 8 != 0 || a.ldqkv % 8 != 0 || a.qsplit < 1 ||
+      (a.Q + a.qsplit - 1) / a.qsplit > kAttnMaxQ)
+    return cudaErrorInvalidValue;
+  const size_t smem = attn_layout(a.vmax, a.head_dim).total;
   auto k = dtype == kBF16 ? attention_kernel<kBF16> : attention_kernel<kF16>;
   cudaError_t e = allow_smem(k, smem);
   if (e != cudaSuccess) return e;
-  return launch_ex(k, dim3(a.S * a.heads * a.qsplit), dim3(kThreads), smem, stream, pdl, a);
+  return launch_ex(k, dim3(a.S * a.heads * a.qsplit), dim3(kAttnThreads), smem, stream, pdl, a);
 }
 
 cudaError_t launch_conv_module(int dtype, const ConvArgs& a, cudaStream_t stream, bool pdl) {

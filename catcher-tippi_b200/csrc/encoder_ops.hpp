@@ -64,8 +64,7 @@ struct AttnArgs {
 };
 // Dynamic shared memory of one attention CTA holding `rows_q` queries.
 size_t attention_smem_bytes(int rows_q, int vmax, int head_dim);
-// Query split that fills the GPU: one CTA per (stream, head) when there are
-// enough of them, otherwise up to one CTA per query.
+// Query groups per (stream, head): one CTA per 16 queries (the MMA row tile).
 int attention_qsplit(int streams, int heads, int Q, int num_sms);
 cudaError_t launch_attention(int dtype, const AttnArgs& a, cudaStream_t stream, bool pdl);
 
