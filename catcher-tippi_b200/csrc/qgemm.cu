@@ -6,13 +6,15 @@
 // the operation behind QuantizedLinear::forward_array
 // (crates/nemotron-mlx/src/model/layers.rs:298-310) at batched row counts.
 //
-// Per CTA: one 128 x BN output tile over the full K, 6 warps:
+// Per CTA: one 128 x BN output tile over the full K, 18 warps:
 //   warp 0   TMA producer: x tile [128 x 64] f16 (128B swizzle) and the packed
 //            weight tile [BN x 64] u8 (64B swizzle) into a 4-stage ring
 //   warp 1   tcgen05.mma issuer (one elected lane), kind::f16, M=128, N=BN,
 //            K=16 per instruction, fp32 accumulator in tensor memory; owns the
 //            tensor-memory allocation
-//   warps 2-5 dequantisers: one weight row per thread, w = s * q + b in f16
+//   warps 2-17 dequantisers: half a weight row per thread (sixteen warps, so
+//            that the PRMT -> subtract -> FMA chains of four warps per
+//            scheduler hide each other's latency), w = s * q + b in f16
 //            (the byte becomes the exact f16 1024 + q by one PRMT, 1024 is
 //            subtracted exactly, then one fused multiply-add), written into
 //            the 128B-swizzled K-major layout the MMA reads; after the last
@@ -38,7 +40,7 @@ constexpr int kBM = 128;  // MMA M (tokens)
 constexpr int kBK = 64;   // k per stage: one 128-byte swizzle atom of f16
 constexpr int kStages = 4;  // TMA ring depth
 constexpr int kBBufs = 2;   // dequantised weight tiles (double buffer)
-constexpr int kDequantWarps = 8;
+constexpr int kDequantWarps = 16;
 constexpr int kThreads = (2 + kDequantWarps) * 32;
 constexpr int kDequantWarp0 = 2;
 
@@ -131,8 +133,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap qmap,
                  const GemmArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
-  constexpr int kRowsPerThread = BN / (kDequantWarps * 32);
-  static_assert(BN % (kDequantWarps * 32) == 0, "rows per dequant thread");
+  // each dequant thread takes kChunks of the four 16-byte chunks of one row
+  constexpr int kChunks = 4 * BN / (kDequantWarps * 32);
+  static_assert(kChunks >= 1 && 4 % kChunks == 0 && (kDequantWarps * 32) % BN == 0,
+                "chunks per dequant thread");
   using L = GemmSmem<BN, SUBG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
@@ -228,11 +232,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ dequant
     constexpr int kDT = kDequantWarps * 32;
-    const int t = threadIdx.x - kDequantWarp0 * 32;  // rows t, t + kDT, ...
-#pragma unroll
-    for (int rr = 0; rr < kRowsPerThread; ++rr) {
-      const int n = n0 + t + kDT * rr;
-      bias_s[t + kDT * rr] = (a.bias != nullptr && n < a.N) ? ld_t<DT>(a.bias, n) : 0.0f;
+    const int t = threadIdx.x - kDequantWarp0 * 32;
+    const int row = t % BN, cfirst = (t / BN) * kChunks;  // chunks cfirst .. cfirst + kChunks - 1
+    for (int r = t; r < BN; r += kDT) {
+      const int n = n0 + r;
+      bias_s[r] = (a.bias != nullptr && n < a.N) ? ld_t<DT>(a.bias, n) : 0.0f;
     }
     const __half2 k1024 = __float2half2_rn(1024.0f);
     for (int i = 0; i < NKT; ++i) {
@@ -242,48 +246,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* st = smem + s * L::kStage;
       const __half2* sbp = reinterpret_cast<const __half2*>(st + L::kA + L::kQ);
       uint8_t* bt = smem + L::kBOff + b * L::kB;
+      // this row's (scale, bias) for the k-tile's group(s), f16
+      __half2 s2[2], b2[2];
 #pragma unroll
-      for (int rr = 0; rr < kRowsPerThread; ++rr) {
-        const int row = t + kDT * rr;
-        // this row's (scale, bias) for the k-tile's group(s), f16
-        __half2 s2[2], b2[2];
+      for (int h = 0; h < SUBG; ++h) {
+        const __half2 p = sbp[row * SUBG + h];
+        s2[h] = __low2half2(p);
+        b2[h] = __high2half2(p);
+      }
+      if constexpr (SUBG == 1) {
+        s2[1] = s2[0];
+        b2[1] = b2[0];
+      }
+      const uint8_t* qrow = st + L::kA + row * 64;  // 64B-swizzled u8 row
+      uint8_t* brow = bt + row * 128;               // 128B-swizzled f16 row
+      const int sw64 = (row >> 1) & 3, sw128 = row & 7;
 #pragma unroll
-        for (int h = 0; h < SUBG; ++h) {
-          const __half2 p = sbp[row * SUBG + h];
-          s2[h] = __low2half2(p);
-          b2[h] = __high2half2(p);
+      for (int cc = 0; cc < kChunks; ++cc) {
+        const int c = cfirst + cc;
+        // logical 16-byte chunk c of the packed row = k0 + 16c .. k0 + 16c + 15
+        const uint4 qv = *reinterpret_cast<const uint4*>(qrow + ((c ^ sw64) << 4));
+        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+        const int h = (G == 32) ? (c >> 1) : 0;
+        uint32_t out[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t lo = __byte_perm(qw[i], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
+          uint32_t hi = __byte_perm(qw[i], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
+          const __half2 ql = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
+          const __half2 qh = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
+          const __half2 wl = __hfma2(s2[h], ql, b2[h]);
+          const __half2 wh = __hfma2(s2[h], qh, b2[h]);
+          out[2 * i] = *reinterpret_cast<const uint32_t*>(&wl);
+          out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&wh);
         }
-        if constexpr (SUBG == 1) {
-          s2[1] = s2[0];
-          b2[1] = b2[0];
-        }
-        const uint8_t* qrow = st + L::kA + row * 64;  // 64B-swizzled u8 row
-        uint8_t* brow = bt + row * 128;               // 128B-swizzled f16 row
-        const int sw64 = (row >> 1) & 3, sw128 = row & 7;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          // logical 16-byte chunk c of the packed row = k0 + 16c .. k0 + 16c + 15
-          const uint4 qv = *reinterpret_cast<const uint4*>(qrow + ((c ^ sw64) << 4));
-          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-          const int h = (G == 32) ? (c >> 1) : 0;
-          uint32_t out[8];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t lo = __byte_perm(qw[i], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
-            uint32_t hi = __byte_perm(qw[i], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
-            const __half2 ql = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
-            const __half2 qh = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
-            const __half2 wl = __hfma2(s2[h], ql, b2[h]);
-            const __half2 wh = __hfma2(s2[h], qh, b2[h]);
-            out[2 * i] = *reinterpret_cast<const uint32_t*>(&wl);
-            out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&wh);
-          }
-          // 16 f16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row
-          *reinterpret_cast<uint4*>(brow + (((2 * c) ^ sw128) << 4)) =
-              make_uint4(out[0], out[1], out[2], out[3]);
-          *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ sw128) << 4)) =
-              make_uint4(out[4], out[5], out[6], out[7]);
-        }
+        // 16 f16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row
+        *reinterpret_cast<uint4*>(brow + (((2 * c) ^ sw128) << 4)) =
+            make_uint4(out[0], out[1], out[2], out[3]);
+        *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ sw128) << 4)) =
+            make_uint4(out[4], out[5], out[6], out[7]);
       }
       fence_proxy_async_shared();  // generic-proxy writes -> tensor-core reads
       __syncwarp();
@@ -324,42 +325,61 @@ __global__ void __launch_bounds__(kThreads, 1)
                                __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
       }
     } else {
+      // Finished T values go to a [128][BN] tile in the (idle) stage buffers,
+      // rows padded by 16 bytes so a warp's 16-byte writes of 8 rows hit all
+      // banks; the tile then leaves in whole rows (each warp writes 32
+      // consecutive 16-byte pieces of one row: fully coalesced).
+      constexpr int kRowBytes = BN * 2 + 16;
+      uint8_t* ot = smem;
+      const int row = quarter * 32 + lane;
 #pragma unroll 1
       for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
         tmem_wait_ld();
-        if (m < a.M) {
-          float o[32];
+        uint32_t pk[16];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float v = round_t<DT>(__uint_as_float(r[j]) * rs);
-            if (has_bias) v = round_t<DT>(v + bias_s[c0 + j]);
+        for (int j = 0; j < 16; ++j) {
+          float o2[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int jj = 2 * j + e;
+            float v = round_t<DT>(__uint_as_float(r[jj]) * rs);
+            if (has_bias) v = round_t<DT>(v + bias_s[c0 + jj]);
             if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
             else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
-            o[j] = v;
+            o2[e] = v;
           }
-          const int nb = n0 + c0;
-          if (vec_ok && nb + 32 <= a.N) {
-            uint32_t pk[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              if constexpr (DT == kBF16) {
-                const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
-                pk[j] = *reinterpret_cast<const uint32_t*>(&h);
-              } else {
-                const __half2 h = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
-                pk[j] = *reinterpret_cast<const uint32_t*>(&h);
-              }
-            }
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.y) +
-                                                  static_cast<size_t>(m) * a.ldy + nb);
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+          if constexpr (DT == kBF16) {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(o2[0], o2[1]);
+            pk[j] = *reinterpret_cast<const uint32_t*>(&h);
           } else {
-            for (int j = 0; j < 32; ++j)
-              if (nb + j < a.N) st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + nb + j, o[j]);
+            const __half2 h = __floats2half2_rn(o2[0], o2[1]);
+            pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+          }
+        }
+        uint4* dst = reinterpret_cast<uint4*>(ot + row * kRowBytes + c0 * 2);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
+      constexpr int kPieces = BN / 8;  // 16-byte pieces per row
+      const int t = threadIdx.x - kDequantWarp0 * 32;
+      for (int e = t; e < kBM * kPieces; e += kDequantWarps * 32) {
+        const int rr = e / kPieces, pc = e % kPieces;
+        const int mm = m0 + rr, n = n0 + pc * 8;
+        if (mm >= a.M) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>(ot + rr * kRowBytes + pc * 16);
+        if (vec_ok && n + 8 <= a.N) {
+          *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.y) + static_cast<size_t>(mm) * a.ldy + n) = v;
+        } else {
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          for (int j = 0; j < 8; ++j) {
+            const int nj = n + j;
+            if (nj < a.N) {
+              const uint16_t bits = static_cast<uint16_t>(j & 1 ? w[j / 2] >> 16 : w[j / 2] & 0xFFFFu);
+              reinterpret_cast<uint16_t*>(a.y)[static_cast<size_t>(mm) * a.ldy + nj] = bits;
+            }
           }
         }
       }
@@ -585,10 +605,12 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   if (forced == 1) return 1;
   const int tiles = ((N + kGemmBN - 1) / kGemmBN) * ((M + kBM - 1) / kBM);
   const int KT = (K + kBK - 1) / kBK;
-  if (4 * tiles > num_sms) return 1;  // a quarter of the SMs or more: splitting does not pay
+  // A CTA's k-tiles run at a fixed cadence set by its copy ring, whatever the
+  // number of CTAs in flight, so splitting K over a cluster shortens the call
+  // as long as every slice still has an SM of its own (one wave).
   for (int s : {4, 2}) {
     const int per = (KT + s - 1) / s;
-    if (tiles * s <= num_sms + num_sms / 4 && KT >= 2 * s && (s - 1) * per < KT) return s;
+    if (tiles * s <= num_sms && KT >= 2 * s && (s - 1) * per < KT) return s;
   }
   return 1;
 }
