@@ -76,14 +76,19 @@ __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
 
 template <int DT, int G, int RT>
 __global__ void __launch_bounds__(kThreads, 2)
-    qgemv_kernel(const __grid_constant__ CUtensorMap wmap, const GemvArgs a) {
+    qgemv_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ GemvGroup grp) {
   constexpr int RB = 16 * RT;
   constexpr int SUBG = (G == 32) ? 2 : 1;  // groups per 64-wide sub-block
   extern __shared__ __align__(128) uint8_t smem[];
 
   const int S = gridDim.x;  // K-split factor == cluster size along x
   const int rank = blockIdx.x;
-  const int n0 = blockIdx.y * RB;
+  // member of the group and band within it
+  const int bands = (grp.a[0].N + RB - 1) / RB;
+  const int member = blockIdx.y / bands;
+  const GemvArgs& a = grp.a[member];
+  const CUtensorMap* wmap = &maps.m[member];
+  const int n0 = (blockIdx.y - member * bands) * RB;
   const int nsb = (a.K + 63) >> 6;
   const int sb0 = rank * a.sb_per_cta;
   const int sbn = max(0, min(a.sb_per_cta, nsb - sb0));
@@ -102,14 +107,14 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   // ---- weight tile: independent of the previous kernel, issued first.
   if (tid == 0) {
-    prefetch_tensormap(&wmap);
+    prefetch_tensormap(wmap);
     for (int j = 0; j < sbn; ++j) mbar_init(&bars[j], 1);
     fence_mbar_init();
     // weights are read once, unless token tiles are spread over grid.z
     const uint64_t pol = gridDim.z == 1 ? l2_policy_evict_first() : l2_policy_evict_normal();
     for (int j = 0; j < sbn; ++j) {
       mbar_arrive_expect_tx(&bars[j], RB * 64);
-      tma_load_2d(wt + static_cast<size_t>(j) * RB * 64, &wmap, (sb0 + j) * 64, n0, &bars[j], pol);
+      tma_load_2d(wt + static_cast<size_t>(j) * RB * 64, wmap, (sb0 + j) * 64, n0, &bars[j], pol);
     }
   }
 
@@ -273,9 +278,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 }
 
 template <int DT, int G, int RT>
-cudaError_t launch_typed(const GemvPlan& plan, const CUtensorMap& wmap, const GemvArgs& args,
+cudaError_t launch_typed(const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
                          cudaStream_t stream, bool pdl) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
+  const GemvArgs& args = grp.a[0];
   const GemvSmem L = gemv_smem_layout(RT, plan.sb_per_cta, SUBG, plan.ksplit);
   auto kern = qgemv_kernel<DT, G, RT>;
   static int configured_smem = 0;
@@ -287,7 +293,7 @@ cudaError_t launch_typed(const GemvPlan& plan, const CUtensorMap& wmap, const Ge
   }
   cudaLaunchConfig_t cfg = {};
   // token tiles beyond the first spread over grid.z, within one wave
-  const int bands = (args.N + 16 * RT - 1) / (16 * RT);
+  const int bands = (args.N + 16 * RT - 1) / (16 * RT) * grp.count;
   const int mtiles = (args.M + 15) / 16;
   const int zmax = std::max(1, (2 * plan.num_sms) / std::max(1, bands * plan.ksplit));
   cfg.gridDim = dim3(plan.ksplit, bands, std::min(mtiles, zmax));
@@ -310,27 +316,27 @@ cudaError_t launch_typed(const GemvPlan& plan, const CUtensorMap& wmap, const Ge
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, wmap, args);
+  return cudaLaunchKernelEx(&cfg, kern, maps, grp);
 }
 
 template <int DT, int G>
-cudaError_t launch_rt(const GemvPlan& plan, const CUtensorMap& wmap, const GemvArgs& args,
+cudaError_t launch_rt(const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
                       cudaStream_t stream, bool pdl) {
   switch (plan.rt) {
-    case 1: return launch_typed<DT, G, 1>(plan, wmap, args, stream, pdl);
-    case 2: return launch_typed<DT, G, 2>(plan, wmap, args, stream, pdl);
-    case 4: return launch_typed<DT, G, 4>(plan, wmap, args, stream, pdl);
+    case 1: return launch_typed<DT, G, 1>(plan, maps, grp, stream, pdl);
+    case 2: return launch_typed<DT, G, 2>(plan, maps, grp, stream, pdl);
+    case 4: return launch_typed<DT, G, 4>(plan, maps, grp, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <int DT>
-cudaError_t launch_g(int group, const GemvPlan& plan, const CUtensorMap& wmap,
-                     const GemvArgs& args, cudaStream_t stream, bool pdl) {
+cudaError_t launch_g(int group, const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
+                     cudaStream_t stream, bool pdl) {
   switch (group) {
-    case 32: return launch_rt<DT, 32>(plan, wmap, args, stream, pdl);
-    case 64: return launch_rt<DT, 64>(plan, wmap, args, stream, pdl);
-    case 128: return launch_rt<DT, 128>(plan, wmap, args, stream, pdl);
+    case 32: return launch_rt<DT, 32>(plan, maps, grp, stream, pdl);
+    case 64: return launch_rt<DT, 64>(plan, maps, grp, stream, pdl);
+    case 128: return launch_rt<DT, 128>(plan, maps, grp, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -388,11 +394,26 @@ size_t gemv_smem_bytes(const GemvPlan& plan, int group) {
   return gemv_smem_layout(plan.rt, plan.sb_per_cta, group == 32 ? 2 : 1, plan.ksplit).total;
 }
 
+cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const GemvMaps& maps,
+                              const GemvGroup& g, cudaStream_t stream, bool pdl) {
+  if (g.count < 1 || g.count > kGemvMaxGroup) return cudaErrorInvalidValue;
+  for (int i = 1; i < g.count; ++i)
+    if (g.a[i].N != g.a[0].N || g.a[i].K != g.a[0].K || g.a[i].M != g.a[0].M ||
+        g.a[i].sb_per_cta != g.a[0].sb_per_cta)
+      return cudaErrorInvalidValue;
+  if (dtype == kF16) return launch_g<kF16>(group, plan, maps, g, stream, pdl);
+  if (dtype == kBF16) return launch_g<kBF16>(group, plan, maps, g, stream, pdl);
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
                         const GemvArgs& args, cudaStream_t stream, bool pdl) {
-  if (dtype == kF16) return launch_g<kF16>(group, plan, wmap, args, stream, pdl);
-  if (dtype == kBF16) return launch_g<kBF16>(group, plan, wmap, args, stream, pdl);
-  return cudaErrorInvalidValue;
+  GemvMaps maps;
+  maps.m[0] = wmap;
+  GemvGroup g{};
+  g.a[0] = args;
+  g.count = 1;
+  return launch_gemv_group(dtype, group, plan, maps, g, stream, pdl);
 }
 
 }  // namespace cq

@@ -28,6 +28,18 @@ struct GemvPlan {
   int num_sms;  // of the device the plan is for (bounds grid.z to one wave)
 };
 
+// Up to kGemvMaxGroup linears of one shape (N, K, M, group, plan) in one
+// launch: grid.y runs over the bands of every member, each member with its own
+// weights, scales, input and output (e.g. an LSTM step's independent ih / hh).
+constexpr int kGemvMaxGroup = 4;
+struct GemvMaps {
+  CUtensorMap m[kGemvMaxGroup];
+};
+struct GemvGroup {
+  GemvArgs a[kGemvMaxGroup];
+  int count;
+};
+
 GemvPlan plan_gemv(int N, int K, int num_sms);
 // The plan for a call with M rows: the base plan (chosen for one 16-row token
 // tile) unless several token tiles would not fit one wave of two CTAs per SM;
@@ -37,5 +49,7 @@ GemvPlan plan_gemv_rows(const GemvPlan& base, int N, int M);
 size_t gemv_smem_bytes(const GemvPlan& plan, int group);
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
                         const GemvArgs& args, cudaStream_t stream, bool pdl);
+cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const GemvMaps& maps,
+                              const GemvGroup& g, cudaStream_t stream, bool pdl);
 
 }  // namespace cq

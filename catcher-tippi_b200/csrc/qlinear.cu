@@ -487,6 +487,53 @@ void QuantizedLinear::forward_array(const void* x, int ldx, int rows, void* y, i
   check_cuda(cq::launch_gemv(dtype_, group_, plan, wmap, a, stream, pdl_enabled()), "qgemv");
 }
 
+void QuantizedLinear::forward_group(const GroupCall* calls, int count, int rows, int act,
+                                    cudaStream_t stream) {
+  if (calls == nullptr || count < 1 || count > cq::kGemvMaxGroup)
+    throw_invalid("a linear group holds 1.." + std::to_string(cq::kGemvMaxGroup) + " calls");
+  const QuantizedLinear& L0 = *calls[0].layer;
+  if (rows < 1 || rows >= cq::kGemmMinRows)
+    throw_invalid("grouped linears take 1.." + std::to_string(cq::kGemmMinRows - 1) + " rows");
+  if (L0.dtype_ != CQ_F16 && L0.dtype_ != CQ_BF16) throw_invalid("grouped linears run f16 or bf16");
+  if (act != CQ_ACT_NONE && act != CQ_ACT_SILU && act != CQ_ACT_RELU)
+    throw_invalid("unknown activation " + std::to_string(act));
+  DeviceContext& ctx = device_context(L0.device_);
+  DeviceGuard guard(L0.device_);
+  const cq::GemvPlan plan = cq::plan_gemv_rows(L0.plan_, L0.N_, rows);
+  cq::GemvMaps maps;
+  cq::GemvGroup g{};
+  g.count = count;
+  for (int i = 0; i < count; ++i) {
+    const GroupCall& c = calls[i];
+    if (c.layer == nullptr || c.x == nullptr || c.y == nullptr)
+      throw_invalid("grouped linear calls need a layer, an input and an output");
+    const QuantizedLinear& L = *c.layer;
+    if (L.N_ != L0.N_ || L.K_ != L0.K_ || L.group_ != L0.group_ || L.dtype_ != L0.dtype_ ||
+        L.device_ != L0.device_)
+      throw_invalid("grouped linears need one shape, group size, dtype and device");
+    if (c.ldx < L.K_ || c.ldy < L.N_) throw_invalid("leading dimensions are smaller than the layer");
+    if ((reinterpret_cast<uintptr_t>(c.x) & 15) != 0 || (c.ldx % 8) != 0)
+      throw_invalid("input rows must be 16-byte aligned (x % 16 == 0 and ldx % 8 == 0)");
+    maps.m[i] = plan.rt == L.plan_.rt ? L.wmap_ : L.wmap_rt_[plan.rt == 1 ? 0 : plan.rt == 2 ? 1 : 2];
+    cq::GemvArgs& a = g.a[i];
+    a.x = c.x;
+    a.scales = L.scales_;
+    a.biases = L.biases_;
+    a.bias = L.bias_;
+    a.y = c.y;
+    a.status = ctx.status;
+    a.M = rows;
+    a.N = L.N_;
+    a.K = L.K_;
+    a.ldx = c.ldx;
+    a.ldy = c.ldy;
+    a.sb_per_cta = L.plan_.sb_per_cta;
+    a.act = act;
+  }
+  check_cuda(cq::launch_gemv_group(L0.dtype_, L0.group_, plan, maps, g, stream, pdl_enabled()),
+             "qgemv group");
+}
+
 void QuantizedLinear::forward_f32(const float* input, size_t input_len, int rows, float* output,
                                   size_t output_len) {
   if (rows < 0 || static_cast<size_t>(rows) * static_cast<size_t>(K_) != input_len)

@@ -96,6 +96,20 @@ class QuantizedLinear {
                                 cudaStream_t stream, void* scratch, size_t scratch_bytes);
   size_t scratch_bytes_for(int rows) const;
 
+  // Several calls of same-shape layers (N, K, group, dtype, device) on the
+  // same number of rows below the GEMM threshold, as one K1 launch whose CTAs
+  // span every member's bands (e.g. the independent ih / hh products of an
+  // LSTM step).  Asynchronous on `stream`.
+  struct GroupCall {
+    const QuantizedLinear* layer;
+    const void* x;
+    int ldx;
+    void* y;
+    int ldy;
+  };
+  static void forward_group(const GroupCall* calls, int count, int rows, int act,
+                            cudaStream_t stream);
+
   int input_dims() const { return K_; }
   int output_dims() const { return N_; }
   int group_size() const { return group_; }

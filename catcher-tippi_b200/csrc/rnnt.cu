@@ -226,7 +226,7 @@ RnntState::RnntState(RnntDecoder& dec, int streams, int max_frames)
   logits_ = DeviceBuffer(S * V * 2);
   x_ = DeviceBuffer(S * H * 2);
   gi_ = DeviceBuffer(S * 4 * H * 2);
-  gh_ = DeviceBuffer(S * 4 * H * 2);
+  gh_ = DeviceBuffer(static_cast<size_t>(c.lstm_layers) * S * 4 * H * 2);  // one slice per layer
   active_ = DeviceBuffer(S * sizeof(int));
   for (int l = 0; l < c.lstm_layers; ++l) {
     h_.emplace_back(S * H * 2);
@@ -277,10 +277,20 @@ void RnntState::prediction_step(bool all, cudaStream_t st) {
   const bool pdl = pdl_on();
   const int H = c.pred_hidden;
   const void* in = x_.get();
+  auto gh = [&](int l) { return static_cast<char*>(gh_.get()) + static_cast<size_t>(l) * S_ * 4 * H * 2; };
+  // ih of layer 0 and hh of every layer read only what the previous step
+  // left: one grouped launch; ih of the later layers waits for its cell.
+  const bool grouped = S_ < cq::kGemmMinRows && c.lstm_layers + 1 <= cq::kGemvMaxGroup;
+  if (grouped) {
+    QuantizedLinear::GroupCall calls[cq::kGemvMaxGroup];
+    calls[0] = {dec_.ih(0), in, H, gi_.get(), 4 * H};
+    for (int l = 0; l < c.lstm_layers; ++l) calls[l + 1] = {dec_.hh(l), h_[l].get(), H, gh(l), 4 * H};
+    QuantizedLinear::forward_group(calls, c.lstm_layers + 1, S_, CQ_ACT_NONE, st);
+  }
   for (int l = 0; l < c.lstm_layers; ++l) {
-    linear(dec_.ih(l), in, H, S_, gi_.get(), 4 * H, CQ_ACT_NONE, st);
-    linear(dec_.hh(l), h_[l].get(), H, S_, gh_.get(), 4 * H, CQ_ACT_NONE, st);
-    check_cuda(cq::launch_lstm_cell(dt, gi_.get(), gh_.get(), dec_.lstm_bias(l), h_[l].get(), c_[l].get(),
+    if (!grouped || l > 0) linear(dec_.ih(l), in, H, S_, gi_.get(), 4 * H, CQ_ACT_NONE, st);
+    if (!grouped) linear(dec_.hh(l), h_[l].get(), H, S_, gh(l), 4 * H, CQ_ACT_NONE, st);
+    check_cuda(cq::launch_lstm_cell(dt, gi_.get(), gh(l), dec_.lstm_bias(l), h_[l].get(), c_[l].get(),
                                     active_.as<int>(), S_, H, all, st, pdl),
                "lstm cell");
     in = h_[l].get();
