@@ -389,6 +389,8 @@ EncoderState::EncoderState(Encoder& enc, int streams, int max_mel_frames)
   hid_ = DeviceBuffer(S * Q * hid_width_ * es);
   y_ = DeviceBuffer(S * Q * D * es);
   att_ = DeviceBuffer(S * Q * D * es);
+  x16_ = DeviceBuffer(S * Q * D * 2);
+  scale16_ = DeviceBuffer(S * Q * sizeof(float));
   qkv_ = DeviceBuffer(S * Q * 3 * D * es);
   pin_ = DeviceBuffer(S * Q * (D + c.num_prompts) * es);
   relk_ = DeviceBuffer(static_cast<size_t>(pmax_) * D * es);
@@ -560,6 +562,17 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
   ln.prompt_ids = prompts_.as<int>();
   ln.num_prompts = P;
   ln.rows_per_stream = Q;
+  // LayerNorm / conv outputs that feed a tensor-core GEMM also leave its f16
+  // activations, so those linears skip their prepass
+  const bool prescale = enc_.dtype() == CQ_BF16 && blocks[0].ff1a->gemm_for(rows);
+  void* x16 = prescale ? x16_.get() : nullptr;
+  float* s16 = prescale ? scale16_.as<float>() : nullptr;
+  auto block_linear = [&](QuantizedLinear* L, const void* x, int ldx, void* y, int ldy, int act) {
+    if (prescale) L->forward_prescaled(x16, s16, rows, y, ldy, act, st);
+    else linear(L, x, ldx, rows, y, ldy, act, st);
+  };
+  ln.out16 = x16;
+  ln.scale16 = s16;
   // residual stream = subsampling output; first block's feed-forward norm
   ln.mode = 1;
   ln.scale = 1.0f;
@@ -585,11 +598,11 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
       check_cuda(cq::launch_layernorm(dt, x, st, pdl), "layernorm");
     };
     // feed-forward 1 (half-step residual)
-    linear(b.ff1a, xn_.get(), D, rows, hid_.get(), c.ff, CQ_ACT_SILU, st);
+    block_linear(b.ff1a, xn_.get(), D, hid_.get(), c.ff, CQ_ACT_SILU);
     linear(b.ff1b, hid_.get(), c.ff, rows, y_.get(), D, CQ_ACT_NONE, st);
     add_ln(0.5f, b.norm_att_w, b.norm_att_b);
     // self-attention
-    linear(b.qkv, xn_.get(), D, rows, qkv_.get(), 3 * D, CQ_ACT_NONE, st);
+    block_linear(b.qkv, xn_.get(), D, qkv_.get(), 3 * D, CQ_ACT_NONE);
     linear(b.pos, pos_table_.get(), D, pmax_, relk_.get(), D, CQ_ACT_NONE, st);
     cq::AttnArgs at{};
     at.qkv = qkv_.get();
@@ -615,7 +628,7 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
     linear(b.o, att_.get(), D, rows, y_.get(), D, CQ_ACT_NONE, st);
     add_ln(1.0f, b.norm_conv_w, b.norm_conv_b);
     // convolution module
-    linear(b.pw1, xn_.get(), D, rows, hid_.get(), 2 * D, CQ_ACT_NONE, st);
+    block_linear(b.pw1, xn_.get(), D, hid_.get(), 2 * D, CQ_ACT_NONE);
     cq::ConvArgs cv{};
     cv.pw1 = hid_.get();
     cv.ldp = 2 * D;
@@ -632,11 +645,13 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
     cv.D = D;
     cv.K = c.conv_kernel;
     cv.eps = 1e-5f;
+    cv.out16 = x16;
+    cv.scale16 = s16;
     check_cuda(cq::launch_conv_module(dt, cv, st, pdl), "conv module");
-    linear(b.pw2, att_.get(), D, rows, y_.get(), D, CQ_ACT_NONE, st);
+    block_linear(b.pw2, att_.get(), D, y_.get(), D, CQ_ACT_NONE);
     add_ln(1.0f, b.norm_ff2_w, b.norm_ff2_b);
     // feed-forward 2 (half-step residual), then norm_out and the next block's first norm
-    linear(b.ff2a, xn_.get(), D, rows, hid_.get(), c.ff, CQ_ACT_SILU, st);
+    block_linear(b.ff2a, xn_.get(), D, hid_.get(), c.ff, CQ_ACT_SILU);
     linear(b.ff2b, hid_.get(), c.ff, rows, y_.get(), D, CQ_ACT_NONE, st);
     cq::LnArgs x = ln;
     x.mode = 0;
@@ -647,6 +662,8 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
     if (last) {
       x.w2 = nullptr;
       x.b2 = nullptr;
+      x.out16 = nullptr;  // the projector's input is D + prompts wide: it keeps its prepass
+      x.scale16 = nullptr;
       x.out_kind = 1;  // [block output | one-hot prompt] for the prompt projector
       x.out = pin_.get();
       x.ldo = D + P;

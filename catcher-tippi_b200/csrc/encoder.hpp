@@ -115,6 +115,10 @@ class EncoderState {
   int launches_ = 0;
   DeviceBuffer counters_, prompts_;
   DeviceBuffer res_, xn_, hid_, y_, att_, qkv_, pin_, relk_, pos_table_;
+  // f16 copy + per-row scales of the LayerNorm / conv outputs that feed a
+  // tensor-core GEMM (bf16, rows >= the GEMM threshold): the GEMM's prepass
+  // done by the producer
+  DeviceBuffer x16_, scale16_;
   DeviceBuffer kring_, vring_, conv_cache_;
   DeviceBuffer stem_out_, dw1_out_, pw1_out_, dw2_out_, pw2_out_, flat_;
   DeviceBuffer sub_cache_[3];

@@ -131,6 +131,47 @@ __device__ __forceinline__ void layernorm8(const float (&v)[8], float (&o)[8], b
 
 int row_threads(int D) { return ((D / 8 + 31) / 32) * 32; }
 
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();  // red may still be read by a previous reduction
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.0f;
+  const int nw = blockDim.x >> 5;
+  for (int i = 0; i < nw; ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// The tensor-core GEMM's view of one bf16 row (qgemm_prepass_kernel's
+// arithmetic): a power-of-two scale puts the row's largest magnitude in
+// [2^14, 2^15), the scaled values are rounded to f16 (exact for every element
+// within 2^-28 of that maximum) and the inverse scale is kept per row.
+__device__ __forceinline__ void emit_scaled_f16(const float (&o)[8], bool active, int c0,
+                                                size_t row, int ld, void* out16, float* scale16,
+                                                float* red) {
+  float amax = 0.0f;
+  if (active) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) amax = fmaxf(amax, fabsf(o[k]));
+  }
+  amax = block_max(amax, red);
+  const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
+  int sh = e == 0 ? 0 : 141 - e;
+  sh = max(-126, min(126, sh));
+  const float scale = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
+  if (threadIdx.x == 0) scale16[row] = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+  if (active) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      w[k] = __half_as_ushort(__float2half_rn(o[2 * k] * scale)) |
+             (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(o[2 * k + 1] * scale))) << 16);
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(out16) + row * ld + c0) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
 // ------------------------------------------------------------------ LayerNorm
 
 template <int DT>
@@ -175,6 +216,8 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
   }
   if (!second || a.out_kind == 1) {
     if (active) st16(a.out, static_cast<size_t>(row) * a.ldo + c0, pack8<DT>(o));
+    if (DT == kBF16 && a.out16 != nullptr && a.out_kind == 0)
+      emit_scaled_f16(o, active, c0, row, D, a.out16, a.scale16, red);
     if (a.out_kind == 1) {
       const int prompt = a.prompt_ids[row / a.rows_per_stream];
       for (int j = threadIdx.x; j < a.num_prompts; j += blockDim.x)
@@ -185,6 +228,8 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
   float o2[8] = {};
   layernorm8<DT>(o, o2, active, c0, D, a.w2, a.b2, a.eps, red);
   if (active) st16(a.out, static_cast<size_t>(row) * a.ldo + c0, pack8<DT>(o2));
+  if (DT == kBF16 && a.out16 != nullptr)
+    emit_scaled_f16(o2, active, c0, row, D, a.out16, a.scale16, red);
 }
 
 // ------------------------------------------------------------------ attention
@@ -561,12 +606,14 @@ __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const 
         st16(new_c, static_cast<size_t>(j) * D + c0, ld16(old_c, static_cast<size_t>(Q + j) * D + c0));
   }
   layernorm8<DT>(dv, o, active, c0, D, a.ln_w, a.ln_b, a.eps, red);
+  float y[8] = {};
   if (active) {
-    float y[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) y[k] = o[k] / (1.0f + expf(-o[k]));  // SiLU, cast to T for pw2
+    for (int k = 0; k < 8; ++k) y[k] = round_t<DT>(o[k] / (1.0f + expf(-o[k])));  // SiLU, cast to T for pw2
     st16(a.out, static_cast<size_t>(row) * D + c0, pack8<DT>(y));
   }
+  if (DT == kBF16 && a.out16 != nullptr)
+    emit_scaled_f16(y, active, c0, row, D, a.out16, a.scale16, red);
 }
 
 // ------------------------------------------------------------------ subsampling

@@ -43,6 +43,11 @@ struct LnArgs {
   int rows_per_stream;
   int rows, D;
   float eps;
+  // bf16 only, out_kind 0: also the f16 copy [rows, D] and per-row scales the
+  // tensor-core GEMM takes as its activations (what qgemm_prepass computes
+  // from `out`), so the next linear skips its prepass.  nullptr: none.
+  void* out16;
+  float* scale16;
 };
 cudaError_t launch_layernorm(int dtype, const LnArgs& a, cudaStream_t stream, bool pdl);
 
@@ -81,7 +86,8 @@ struct ConvArgs {
   void* out;    // [S*Q, D] T
   const int* counters;
   int S, Q, D, K;
-  float eps;
+  float eps;  void* out16;     // bf16 only: f16 copy of `out` + per-row scales for the next GEMM
+  float* scale16;  // (nullptr: none)
 };
 cudaError_t launch_conv_module(int dtype, const ConvArgs& a, cudaStream_t stream, bool pdl);
 

@@ -260,6 +260,43 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
   check_cuda(cq::launch_gemm(dtype_, group_, amap_, qmap_gemm_, g, stream, pdl_enabled()), "qgemm");
 }
 
+bool QuantizedLinear::gemm_for(int rows) const {
+  return dtype_ == CQ_BF16 && gemm_ok_ && gemm_allowed() && rows >= cq::kGemmMinRows;
+}
+
+void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale, int rows, void* y,
+                                        int ldy, int act, cudaStream_t stream) {
+  if (!gemm_for(rows)) throw_invalid("prescaled activations feed only the bf16 tensor-core GEMM");
+  if (x16 == nullptr || row_scale == nullptr || y == nullptr)
+    throw_invalid("input, row scales and output must not be null");
+  if (ldy < N_) throw_invalid("output leading dimension is smaller than the layer");
+  if ((reinterpret_cast<uintptr_t>(x16) & 15) != 0 || (K_ % 8) != 0)
+    throw_invalid("prescaled rows must be 16-byte aligned");
+  if (act != CQ_ACT_NONE && act != CQ_ACT_SILU && act != CQ_ACT_RELU)
+    throw_invalid("unknown activation " + std::to_string(act));
+  DeviceContext& ctx = device_context(device_);
+  DeviceGuard guard(device_);
+  if (x16 != amap_pre_ptr_ || rows != amap_pre_rows_) {
+    amap_pre_ = make_map_2d(x16, 2, rows, K_, K_, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_pre_ptr_ = x16;
+    amap_pre_rows_ = rows;
+  }
+  cq::GemmArgs g{};
+  g.row_scale = row_scale;
+  g.sb_tiles = sb_tiles_;
+  g.bias = bias_;
+  g.y = y;
+  g.status = ctx.status;
+  g.M = rows;
+  g.N = N_;
+  g.K = K_;
+  g.ldy = ldy;
+  g.act = act;
+  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  check_cuda(cq::launch_gemm(dtype_, group_, amap_pre_, qmap_gemm_, g, stream, pdl_enabled()),
+             "qgemm");
+}
+
 size_t QuantizedLinear::scratch_bytes_for(int rows) const {
   if (dtype_ != CQ_BF16 || !gemm_ok_ || !gemm_allowed() || rows < cq::kGemmMinRows) return 0;
   return align_up(static_cast<size_t>(rows) * K_ * 2, 256) + static_cast<size_t>(rows) * 4;

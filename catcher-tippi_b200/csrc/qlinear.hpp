@@ -100,6 +100,15 @@ class QuantizedLinear {
   // same number of rows below the GEMM threshold, as one K1 launch whose CTAs
   // span every member's bands (e.g. the independent ih / hh products of an
   // LSTM step).  Asynchronous on `stream`.
+  // True when a call on `rows` rows runs the tensor-core GEMM on f16
+  // activations converted by its prepass (bf16 layers), i.e. when
+  // forward_prescaled can take a producer's converted copy instead.
+  bool gemm_for(int rows) const;
+  // forward_array for such a call, given the activations already converted:
+  // x16 f16 [rows, K] (row stride K) and the per-row inverse scales.
+  void forward_prescaled(const void* x16, const float* row_scale, int rows, void* y, int ldy,
+                         int act, cudaStream_t stream);
+
   struct GroupCall {
     const QuantizedLinear* layer;
     const void* x;
@@ -156,6 +165,10 @@ class QuantizedLinear {
   CUtensorMap amap_scratch_{};
   const void* amap_scratch_ptr_ = nullptr;
   int amap_scratch_rows_ = 0;
+  // activation tensor map of the prescaled path, cached separately
+  CUtensorMap amap_pre_{};
+  const void* amap_pre_ptr_ = nullptr;
+  int amap_pre_rows_ = 0;
   bool check_f16_range() const;
 
   // Scratch of the synchronous host-f32 path, grown on demand.
