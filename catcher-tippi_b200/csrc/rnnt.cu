@@ -33,6 +33,36 @@ bool graphs_on() {
   return on;
 }
 
+bool lstm_fused_disabled() {
+  static const bool off = [] {
+    const char* e = std::getenv("CQ_RNNT_FUSED_LSTM");
+    return e != nullptr && std::strcmp(e, "0") == 0;
+  }();
+  return off;
+}
+
+// A copy of a [4H, K] gate weight with rows interleaved: row 4j + q holds
+// gate q of hidden unit j (source row q * H + j); same codes, scales, biases.
+std::unique_ptr<QuantizedLinear> interleave_gates(const QuantizedLinear& L, int H, cq_dtype dtype,
+                                                  int device) {
+  const int N = L.output_dims(), K = L.input_dims(), g = L.group_size();
+  const size_t gpr = static_cast<size_t>(K / g);
+  std::vector<uint8_t> q(static_cast<size_t>(N) * K), qi(q.size());
+  std::vector<uint16_t> sc(N * gpr), bi(N * gpr), sci(sc.size()), bii(bi.size());
+  check_cuda(cudaMemcpy(q.data(), L.qweight(), q.size(), cudaMemcpyDeviceToHost), "read weights");
+  check_cuda(cudaMemcpy(sc.data(), L.scales(), sc.size() * 2, cudaMemcpyDeviceToHost), "read scales");
+  check_cuda(cudaMemcpy(bi.data(), L.biases(), bi.size() * 2, cudaMemcpyDeviceToHost), "read biases");
+  for (int j = 0; j < H; ++j)
+    for (int gq = 0; gq < 4; ++gq) {
+      const size_t dst = static_cast<size_t>(4 * j + gq), src = static_cast<size_t>(gq * H + j);
+      std::memcpy(&qi[dst * K], &q[src * K], K);
+      std::memcpy(&sci[dst * gpr], &sc[src * gpr], gpr * 2);
+      std::memcpy(&bii[dst * gpr], &bi[src * gpr], gpr * 2);
+    }
+  return QuantizedLinear::from_packed(reinterpret_cast<const uint32_t*>(qi.data()), sci.data(),
+                                      bii.data(), nullptr, N, K, g, dtype, device);
+}
+
 }  // namespace
 
 RnntDecoder::RnntDecoder(const cq_rnnt_config& cfg, cq_dtype dtype, int device)
@@ -206,6 +236,28 @@ void RnntDecoder::finalize() {
     check_cuda(cudaDeviceSynchronize(), "lstm bias");
     lstm_bias_.push_back(std::move(t));
   }
+  // gate-interleaved LSTM weights for the one-launch step (rnnt_lstm.cu)
+  ih_il_.clear();
+  hh_il_.clear();
+  gate_bias_il_.clear();
+  const int g = ih(0)->group_size();
+  bool fits = cq::lstm_step_fits(H, g) && !lstm_fused_disabled();
+  for (int l = 0; l < cfg_.lstm_layers && fits; ++l)
+    fits = ih(l)->group_size() == g && hh(l)->group_size() == g && ih(l)->input_dims() == H;
+  if (fits) {
+    for (int l = 0; l < cfg_.lstm_layers; ++l) {
+      ih_il_.push_back(interleave_gates(*ih(l), H, dtype_, device_));
+      hh_il_.push_back(interleave_gates(*hh(l), H, dtype_, device_));
+      std::vector<uint16_t> b(4 * H), bi(4 * H);
+      check_cuda(cudaMemcpy(b.data(), lstm_bias_[l].get(), b.size() * 2, cudaMemcpyDeviceToHost),
+                 "read gate bias");
+      for (int j = 0; j < H; ++j)
+        for (int q = 0; q < 4; ++q) bi[4 * j + q] = b[q * H + j];
+      DeviceBuffer t(bi.size() * 2);
+      check_cuda(cudaMemcpy(t.get(), bi.data(), bi.size() * 2, cudaMemcpyHostToDevice), "gate bias");
+      gate_bias_il_.push_back(std::move(t));
+    }
+  }
   check_cuda(cudaDeviceSynchronize(), "finalize RNNT");
   finalized_ = true;
 }
@@ -232,6 +284,10 @@ RnntState::RnntState(RnntDecoder& dec, int streams, int max_frames)
     h_.emplace_back(S * H * 2);
     c_.emplace_back(S * H * 2);
   }
+  hpar_.assign(c.lstm_layers, 0);
+  lstm_fused_ = dec_.lstm_fused() && S_ < cq::kGemmMinRows;
+  if (lstm_fused_)
+    for (int l = 0; l < c.lstm_layers; ++l) h_next_.emplace_back(S * H * 2);
   size_t need = dec_.enc_proj()->scratch_bytes_for(S_ * max_frames);
   for (const QuantizedLinear* L : {dec_.head(), dec_.dec_proj()}) need = std::max(need, L->scratch_bytes_for(S_));
   for (int l = 0; l < c.lstm_layers; ++l)
@@ -276,6 +332,37 @@ void RnntState::prediction_step(bool all, cudaStream_t st) {
   const int dt = dec_.dtype() == CQ_BF16 ? cq::kBF16 : cq::kF16;
   const bool pdl = pdl_on();
   const int H = c.pred_hidden;
+  if (lstm_fused_) {
+    const void* in = x_.get();
+    const int g = dec_.ih(0)->group_size();
+    for (int l = 0; l < c.lstm_layers; ++l) {
+      const QuantizedLinear* wi = dec_.ih_interleaved(l);
+      const QuantizedLinear* wh = dec_.hh_interleaved(l);
+      cq::LstmMaps maps;
+      maps.m[0] = wi->gemv_map(4);
+      maps.m[1] = wh->gemv_map(4);
+      cq::LstmStepArgs a{};
+      a.x = in;
+      a.h_prev = h_cur(l);
+      a.h_out = h_other(l);
+      a.c = c_[l].get();
+      a.scales_ih = wi->scales();
+      a.biases_ih = wi->biases();
+      a.scales_hh = wh->scales();
+      a.biases_hh = wh->biases();
+      a.gate_bias = dec_.gate_bias_interleaved(l);
+      a.active = active_.as<int>();
+      a.all = all ? 1 : 0;
+      a.status = device_context(dec_.device()).status;
+      a.S = S_;
+      a.H = H;
+      check_cuda(cq::launch_lstm_step(dt, g, maps, a, st, pdl), "lstm step");
+      hpar_[l] ^= 1;
+      in = h_cur(l);
+    }
+    linear(dec_.dec_proj(), in, H, S_, dec_new_.get(), c.joint_hidden, CQ_ACT_NONE, st);
+    return;
+  }
   const void* in = x_.get();
   auto gh = [&](int l) { return static_cast<char*>(gh_.get()) + static_cast<size_t>(l) * S_ * 4 * H * 2; };
   // ih of layer 0 and hh of every layer read only what the previous step
@@ -298,6 +385,16 @@ void RnntState::prediction_step(bool all, cudaStream_t st) {
   linear(dec_.dec_proj(), in, H, S_, dec_new_.get(), c.joint_hidden, CQ_ACT_NONE, st);
 }
 
+void RnntState::normalize_h(cudaStream_t stream) {
+  const size_t bytes = static_cast<size_t>(S_) * dec_.config().pred_hidden * 2;
+  for (size_t l = 0; l < hpar_.size(); ++l) {
+    if (!hpar_[l]) continue;
+    check_cuda(cudaMemcpyAsync(h_[l].get(), h_next_[l].get(), bytes, cudaMemcpyDeviceToDevice, stream),
+               "hidden state");
+    hpar_[l] = 0;
+  }
+}
+
 void RnntState::reset() {
   const auto& c = dec_.config();
   DeviceGuard guard(dec_.device());
@@ -307,7 +404,9 @@ void RnntState::reset() {
   // the first PredictionNetwork::step(blank) of every stream
   check_cuda(cq::launch_broadcast_row(dec_.embedding(), c.blank, c.pred_hidden, x_.get(), S_, nullptr),
              "blank embedding");
+  std::fill(hpar_.begin(), hpar_.end(), 0);
   prediction_step(true, nullptr);
+  normalize_h(nullptr);
   check_cuda(cudaMemcpy(dec_out_.get(), dec_new_.get(), dec_out_.bytes(), cudaMemcpyDeviceToDevice),
              "initial decoder output");
   check_cuda(cudaDeviceSynchronize(), "reset");
@@ -391,6 +490,7 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
                  "joint input");
     }
   }
+  normalize_h(st);  // the chunk ends with the state in h_, whatever its step count
 }
 
 void RnntState::set_persistent(bool on) {

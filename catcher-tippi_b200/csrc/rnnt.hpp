@@ -51,6 +51,13 @@ class RnntDecoder {
   QuantizedLinear* hh(int l) const;
   const void* embedding() const { return embedding_.get(); }  // T [vocab, pred_hidden]
   const void* lstm_bias(int l) const { return lstm_bias_[l].get(); }  // T [4 * pred_hidden]
+  // Gate-interleaved copies (row 4j + q = gate q of hidden unit j) of the LSTM
+  // weights and summed biases for the one-launch LSTM step; empty when the
+  // shapes do not fit it.
+  bool lstm_fused() const { return !ih_il_.empty(); }
+  const QuantizedLinear* ih_interleaved(int l) const { return ih_il_[l].get(); }
+  const QuantizedLinear* hh_interleaved(int l) const { return hh_il_[l].get(); }
+  const void* gate_bias_interleaved(int l) const { return gate_bias_il_[l].get(); }
 
  private:
   const Spec& spec(const std::string& name, bool linear) const;
@@ -65,6 +72,8 @@ class RnntDecoder {
   std::map<std::string, DeviceBuffer> dense_;  // f32 copies of the LSTM biases
   DeviceBuffer embedding_;
   std::vector<DeviceBuffer> lstm_bias_;
+  std::vector<std::unique_ptr<QuantizedLinear>> ih_il_, hh_il_;
+  std::vector<DeviceBuffer> gate_bias_il_;
   bool finalized_ = false;
 };
 
@@ -90,6 +99,12 @@ class RnntState {
   void launch_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,
                     int* counts, cudaStream_t stream);
   void prediction_step(bool all, cudaStream_t stream);
+  // the one-launch LSTM step writes each layer's new hidden state into the
+  // other of two buffers; these give the current / other one and bring the
+  // state back into h_ (at chunk ends, so captured graphs replay alike)
+  void* h_cur(int l) { return hpar_[l] ? h_next_[l].get() : h_[l].get(); }
+  void* h_other(int l) { return hpar_[l] ? h_[l].get() : h_next_[l].get(); }
+  void normalize_h(cudaStream_t stream);
   void linear(QuantizedLinear* L, const void* x, int ldx, int rows, void* y, int ldy, int act,
               cudaStream_t stream);
 
@@ -98,6 +113,9 @@ class RnntState {
   int launches_ = 0;
   DeviceBuffer ep_, dec_out_, dec_new_, fused_, logits_, x_, gi_, gh_, active_;
   std::vector<DeviceBuffer> h_, c_;
+  bool lstm_fused_ = false;
+  std::vector<DeviceBuffer> h_next_;
+  std::vector<int> hpar_;
   // persistent path: second hidden-state buffer per layer, head partials, barrier
   std::vector<DeviceBuffer> h_alt_;
   DeviceBuffer part_, barrier_;

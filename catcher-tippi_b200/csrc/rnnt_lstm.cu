@@ -1,0 +1,255 @@
+// One LSTM layer of one prediction step for every stream in ONE launch:
+// gates = T(T(T(W_ih x) + T(W_hh h)) + bias), then the cell
+// (LstmCell::forward, crates/nemotron-mlx/src/model/rnnt.rs:86-150) -- the
+// work of two K1 launches and the cell kernel.
+//
+// The two products run as the two CTAs of a (2, 1, 1) cluster over the same
+// 64-row band: rank 0 multiplies the layer input by W_ih, rank 1 the previous
+// hidden state by W_hh, each exactly as K1 does for one band (same sub-block
+// order, same warp reduction: bit-identical partial sums).  Rank 1 pushes its
+// partial tile into rank 0's shared memory, and rank 0 rounds each product to
+// T, adds them and the gate bias in T and runs the cell.  The weight rows are
+// interleaved at load time (row 4j + q holds gate q of hidden unit j) so one
+// band holds all four gates of 16 hidden units.  The new hidden state goes to
+// a second buffer (other CTAs still read the old one); streams that are not
+// active keep their state (h copied across, c untouched).
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "rnnt_ops.hpp"
+
+namespace cq {
+
+namespace {
+
+constexpr int kRT = 4;
+constexpr int kRB = 16 * kRT;  // 64 interleaved gate rows = 16 hidden units
+constexpr int kNW = 8;
+constexpr int kThreads = kNW * 32;
+constexpr int kMaxSb = 16;  // K = hidden <= 1024
+constexpr int kSbPerWarp = kMaxSb / kNW;
+
+struct LstmSmem {
+  size_t wt, bars, sbsm, red, fin, total;
+};
+
+__host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg) {
+  LstmSmem L{};
+  size_t off = 0;
+  L.wt = off;  // [sbn][64][64] u8, TMA destination
+  off += static_cast<size_t>(sbn) * kRB * 64;
+  L.bars = off;
+  off += kMaxSb * 8;
+  L.sbsm = off;  // [sbn * subg][64] (s, b - 1024 s)
+  off += static_cast<size_t>(sbn) * subg * kRB * sizeof(float2);
+  L.red = off;  // [8][64][16] per-warp partials
+  off += static_cast<size_t>(kNW) * kRB * 16 * sizeof(float);
+  L.fin = off;  // [2][64][16]: the two products of rank 0's band
+  off += 2ull * kRB * 16 * sizeof(float);
+  L.total = off;
+  return L;
+}
+
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+template <int DT>
+__device__ __forceinline__ float sigmoid_t(float x) {
+  return round_t<DT>(1.0f / (1.0f + expf(-x)));
+}
+
+template <int DT, int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    lstm_step_kernel(const __grid_constant__ LstmMaps maps, const LstmStepArgs a) {
+  constexpr int SUBG = (G == 32) ? 2 : 1;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int rank = blockIdx.x;  // 0: W_ih x, 1: W_hh h
+  const int n0 = blockIdx.y * kRB;
+  const int mt = blockIdx.z;
+  const int H = a.H, K = a.H, N = 4 * a.H;
+  const int sbn = (K + 63) >> 6;
+  const int groups_per_row = K / G;
+  const LstmSmem L = lstm_smem_layout(sbn, SUBG);
+  uint8_t* wt = smem + L.wt;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  float2* sbsm = reinterpret_cast<float2*>(smem + L.sbsm);
+  float* red = reinterpret_cast<float*>(smem + L.red);
+  float* fin = reinterpret_cast<float*>(smem + L.fin);
+  const CUtensorMap* wmap = &maps.m[rank];
+  const void* scales = rank == 0 ? a.scales_ih : a.scales_hh;
+  const void* biases = rank == 0 ? a.biases_ih : a.biases_hh;
+  const void* x = rank == 0 ? a.x : a.h_prev;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c = lane & 3, r4 = lane >> 2;
+
+  // ---- weight tile first: it does not depend on the previous kernel
+  if (tid == 0) {
+    prefetch_tensormap(wmap);
+    for (int j = 0; j < sbn; ++j) mbar_init(&bars[j], 1);
+    fence_mbar_init();
+    const uint64_t pol = l2_policy_evict_normal();  // every token tile reads the band
+    for (int j = 0; j < sbn; ++j) {
+      mbar_arrive_expect_tx(&bars[j], kRB * 64);
+      tma_load_2d(wt + static_cast<size_t>(j) * kRB * 64, wmap, j * 64, n0, &bars[j], pol);
+    }
+  }
+  // ---- group scales / biases as (s, b - 1024 s)
+  for (int e = tid; e < sbn * SUBG * kRB; e += kThreads) {
+    const int jh = e / kRB, row = e - jh * kRB;
+    const int n = n0 + row;
+    const int kfirst = (jh / SUBG) * 64 + (jh % SUBG) * 32;
+    float sv = 0.f, bv = 0.f;
+    if (n < N && kfirst < K) {
+      const size_t gi = static_cast<size_t>(n) * groups_per_row + kfirst / G;
+      sv = ld_t<DT>(scales, gi);
+      bv = ld_t<DT>(biases, gi);
+    }
+    sbsm[e] = make_float2(sv, fmaf(-1024.0f, sv, bv));
+  }
+  pdl_launch_dependents();
+  __syncthreads();
+  pdl_wait();
+
+  // ---- activations of this token tile, all loads in flight at once
+  uint4 xr[kSbPerWarp][2][2];
+#pragma unroll
+  for (int u = 0; u < kSbPerWarp; ++u) {
+    const int j = warp + u * kNW;
+    if (j < sbn) {
+      load_x_raw<G>(x, H, a.S, K, mt * 16 + r4, j * 64, c, xr[u][0][0], xr[u][0][1]);
+      load_x_raw<G>(x, H, a.S, K, mt * 16 + 8 + r4, j * 64, c, xr[u][1][0], xr[u][1][1]);
+    }
+  }
+  float acc[kRT][2][4];
+#pragma unroll
+  for (int i = 0; i < kRT; ++i)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
+  bool ok = true;
+#pragma unroll
+  for (int u = 0; u < kSbPerWarp; ++u) {
+    const int j = warp + u * kNW;
+    if (j >= sbn) break;
+    const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
+    ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
+    subblock_mma<DT, G, kRT>(wt + static_cast<size_t>(j) * kRB * 64,
+                             sbsm + static_cast<size_t>(j) * SUBG * kRB, xo, lane, acc);
+  }
+#pragma unroll
+  for (int i = 0; i < kRT; ++i) {
+    const int ra = 16 * i + r4, rb = ra + 8;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      *reinterpret_cast<float2*>(&red[(warp * kRB + ra) * 16 + 8 * nt + 2 * c]) =
+          make_float2(acc[i][nt][0], acc[i][nt][1]);
+      *reinterpret_cast<float2*>(&red[(warp * kRB + rb) * 16 + 8 * nt + 2 * c]) =
+          make_float2(acc[i][nt][2], acc[i][nt][3]);
+    }
+  }
+  __syncthreads();
+  // this CTA's product into rank 0's slot `rank` ([row][token], warp order)
+  const uint32_t slot = mapa_shared(smem_u32(fin), 0) +
+                        static_cast<uint32_t>(rank * kRB * 16 * sizeof(float));
+  for (int e = tid; e < kRB * 16; e += kThreads) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
+    st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
+  }
+  cluster_sync_all();
+
+  if (rank == 0) {
+    // one (hidden unit, token) per thread: 16 units x 16 tokens
+    const int u = tid >> 4, t = tid & 15;
+    const int s = mt * 16 + t;
+    const int j = n0 / 4 + u;
+    if (s < a.S && j < H) {
+      const size_t hj = static_cast<size_t>(s) * H + j;
+      if (a.all || a.active[s]) {
+        float gate[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int row = 4 * u + q;
+          const float gi = round_t<DT>(fin[row * 16 + t]);
+          const float gh = round_t<DT>(fin[kRB * 16 + row * 16 + t]);
+          gate[q] = round_t<DT>(round_t<DT>(gi + gh) + ld_t<DT>(a.gate_bias, n0 + row));
+        }
+        const float ig = sigmoid_t<DT>(gate[0]);
+        const float fg = sigmoid_t<DT>(gate[1]);
+        const float gg = round_t<DT>(tanhf(gate[2]));
+        const float og = sigmoid_t<DT>(gate[3]);
+        const float c_prev = ld_t<DT>(a.c, hj);
+        const float c_new = round_t<DT>(round_t<DT>(fg * c_prev) + round_t<DT>(ig * gg));
+        const float h_new = round_t<DT>(og * round_t<DT>(tanhf(c_new)));
+        st_t<DT>(a.c, hj, c_new);
+        st_t<DT>(a.h_out, hj, h_new);
+      } else {
+        st_t<DT>(a.h_out, hj, ld_t<DT>(a.h_prev, hj));  // state kept
+      }
+    }
+  }
+  if (!ok && tid == 0)
+    for (int j = 0; j < sbn; ++j) mbar_wait_bounded(&bars[j], 0, a.status);
+}
+
+template <int DT>
+cudaError_t launch_t(int group, const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream,
+                     bool pdl) {
+  void (*kern)(const LstmMaps, const LstmStepArgs) = nullptr;
+  int subg = 1;
+  switch (group) {
+    case 32: kern = lstm_step_kernel<DT, 32>; subg = 2; break;
+    case 64: kern = lstm_step_kernel<DT, 64>; break;
+    case 128: kern = lstm_step_kernel<DT, 128>; break;
+    default: return cudaErrorInvalidValue;
+  }
+  const LstmSmem L = lstm_smem_layout((a.H + 63) / 64, subg);
+  static int configured[3] = {0, 0, 0};  // per group size
+  int& conf = configured[group == 32 ? 0 : group == 64 ? 1 : 2];
+  if (static_cast<int>(L.total) > conf) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(L.total));
+    if (e != cudaSuccess) return e;
+    conf = static_cast<int>(L.total);
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, (4 * a.H + kRB - 1) / kRB, (a.S + 15) / 16);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = L.total;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int na = 0;
+  attrs[na].id = cudaLaunchAttributeClusterDimension;
+  attrs[na].val.clusterDim.x = 2;
+  attrs[na].val.clusterDim.y = 1;
+  attrs[na].val.clusterDim.z = 1;
+  ++na;
+  if (pdl) {
+    attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, kern, maps, a);
+}
+
+}  // namespace
+
+bool lstm_step_fits(int H, int group) {
+  return H % 16 == 0 && H % 64 == 0 && H <= 64 * kMaxSb && (group == 32 || group == 64 || group == 128) &&
+         H % group == 0;
+}
+
+cudaError_t launch_lstm_step(int dtype, int group, const LstmMaps& maps, const LstmStepArgs& a,
+                             cudaStream_t stream, bool pdl) {
+  if (!lstm_step_fits(a.H, group) || a.S < 1) return cudaErrorInvalidValue;
+  if (dtype == kF16) return launch_t<kF16>(group, maps, a, stream, pdl);
+  if (dtype == kBF16) return launch_t<kBF16>(group, maps, a, stream, pdl);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace cq

@@ -1,6 +1,8 @@
 // Host-side interface of the RNNT decoder's supporting kernels (rnnt_ops.cu).
 #pragma once
 
+#include <cuda.h>
+
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -69,5 +71,30 @@ struct RnntChunkArgs {
 int rnnt_chunk_grid(int dtype, int S, int H, int J, int V, int layers, int num_sms);
 size_t rnnt_chunk_smem_bytes(int S, int H, int J, int V, int layers, int grid);
 cudaError_t launch_rnnt_chunk(int dtype, const RnntChunkArgs& a, int grid, cudaStream_t stream);
+
+// One LSTM layer of a prediction step in one launch (rnnt_lstm.cu): the ih and
+// hh products of a 64-row band of gate-interleaved weights (row 4j + q = gate
+// q of hidden unit j) on a two-CTA cluster, then the cell.
+struct LstmMaps {
+  CUtensorMap m[2];  // interleaved W_ih, W_hh: box 64 k x 64 rows
+};
+struct LstmStepArgs {
+  const void* x;       // T [S, H]: the layer input
+  const void* h_prev;  // T [S, H]: the layer's hidden state before the step
+  void* h_out;         // T [S, H]: after the step (not h_prev)
+  void* c;             // T [S, H]: cell state, updated in place
+  const void* scales_ih;  // T [4H, H/g], interleaved rows
+  const void* biases_ih;
+  const void* scales_hh;
+  const void* biases_hh;
+  const void* gate_bias;  // T [4H] interleaved, T(b_ih) + T(b_hh) rounded to T
+  const int* active;      // [S]
+  int all;                // update every stream
+  int* status;
+  int S, H;
+};
+bool lstm_step_fits(int H, int group);
+cudaError_t launch_lstm_step(int dtype, int group, const LstmMaps& maps, const LstmStepArgs& a,
+                             cudaStream_t stream, bool pdl);
 
 }  // namespace cq
