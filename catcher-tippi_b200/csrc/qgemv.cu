@@ -65,7 +65,9 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int rt, int sb_per_cta, int
   L.red = off;  // [kNW][rb][16] per-warp partials
   off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
   L.fin = off;  // [ksplit][rb][16]: CTA partials pushed into the cluster leader
-  off += static_cast<size_t>(ksplit > 1 ? ksplit : 0) * rb * 16 * sizeof(float);
+  // (at least 16 u64: the per-token maxima of the greedy epilogue)
+  off += std::max(static_cast<size_t>(ksplit > 1 ? ksplit : 0) * rb * 16 * sizeof(float),
+                  static_cast<size_t>(16 * sizeof(unsigned long long)));
   L.total = off;
   return L;
 }
@@ -74,9 +76,58 @@ __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
+// Greedy epilogue, after this CTA folded token tile mt's maxima into
+// epi.best: the last of the tile's `ctas` CTAs records the choices of its 16
+// streams (one atomic round trip) and gathers their next embedding rows.
+__device__ void greedy_finish(const RnntEpilogue& epi, int M, int mt, unsigned ctas, int* scratch,
+                              int tid) {
+  if (tid == 0) {
+    __threadfence();
+    scratch[16] = atomicAdd(&epi.done[mt], 1u) == ctas - 1 ? 1 : 0;
+    if (scratch[16]) __threadfence();
+  }
+  __syncthreads();
+  if (scratch[16] == 0) return;
+  if (tid < 16) {
+    const int s = mt * 16 + tid;
+    int out = -1;
+    if (s < M) {
+      const unsigned long long key = atomicExch(&epi.best[s], 0ull);  // read and clear
+      if (epi.active[s]) {
+        // every logit NaN: MLX returns index 0
+        const int bi = key == 0ull ? 0 : static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key));
+        if (bi == epi.blank) {
+          epi.active[s] = 0;
+        } else {
+          const int n = epi.counts[s];
+          if (n < epi.cap) {
+            epi.tokens[static_cast<size_t>(s) * epi.cap + n] = bi;
+            epi.token_frames[static_cast<size_t>(s) * epi.cap + n] = epi.frame;
+          }
+          epi.counts[s] = n + 1;
+          out = bi;
+        }
+      }
+    }
+    scratch[tid] = out;
+  }
+  __syncthreads();
+  const int per_row = epi.H / 8;
+  for (int i = tid; i < 16 * per_row; i += kThreads) {
+    const int t = i / per_row, c8 = (i - t * per_row) * 8;
+    if (scratch[t] < 0) continue;
+    *reinterpret_cast<uint4*>(static_cast<uint16_t*>(epi.x) + static_cast<size_t>(mt * 16 + t) * epi.H + c8) =
+        *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(epi.emb) +
+                                        static_cast<size_t>(scratch[t]) * epi.H + c8);
+  }
+  if (tid == 0) epi.done[mt] = 0;
+  __syncthreads();
+}
+
 template <int DT, int G, int RT>
 __global__ void __launch_bounds__(kThreads, 2)
-    qgemv_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ GemvGroup grp) {
+    qgemv_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ GemvGroup grp,
+                 const __grid_constant__ RnntEpilogue epi) {
   constexpr int RB = 16 * RT;
   constexpr int SUBG = (G == 32) ? 2 : 1;  // groups per 64-wide sub-block
   extern __shared__ __align__(128) uint8_t smem[];
@@ -231,17 +282,40 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     // element e = tok * RB + row: consecutive threads write consecutive n
     if (S == 1) {
+      unsigned long long* best_s = reinterpret_cast<unsigned long long*>(fin);  // [16], greedy mode
+      if (a.mode == kGemvGreedy && tid < 16) best_s[tid] = 0ull;
+      if (a.mode == kGemvGreedy) __syncthreads();
       for (int e = tid; e < RB * 16; e += kThreads) {
         const int row = e % RB, tok = e / RB;
         float v = 0.f;
 #pragma unroll
         for (int w = 0; w < kNW; ++w) v += red[(w * RB + row) * 16 + tok];
         const int n = n0 + row, m = mt * 16 + tok;
-        if (n < a.N && m < a.M)
-          st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n,
-                   epilogue_value<DT>(v, has_bias, biasm[row], a.act));
+        if (n < a.N && m < a.M) {
+          const float o = epilogue_value<DT>(v, has_bias, biasm[row], a.act);
+          const size_t off = static_cast<size_t>(m) * a.ldy + n;
+          st_t<DT>(a.y, off, o);
+          if (a.mode == kGemvJointInput) {
+            float d = o;
+            if (epi.active[m]) st_t<DT>(epi.dec, off, o);
+            else d = ld_t<DT>(epi.dec, off);
+            const float en = ld_t<DT>(epi.enc, static_cast<size_t>(m) * epi.ld_enc + n);
+            st_t<DT>(epi.fused, off, fmaxf(en + d, 0.0f));
+          } else if (a.mode == kGemvGreedy && !isnan(o)) {
+            // larger logit -> larger key; equal logits -> the smaller index
+            const uint32_t u = __float_as_uint(o);
+            const uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            atomicMax(&best_s[tok], (static_cast<unsigned long long>(ord) << 32) |
+                                        (0xFFFFFFFFu - static_cast<uint32_t>(n)));
+          }
+        }
       }
       __syncthreads();
+      if (a.mode == kGemvGreedy) {
+        if (tid < 16 && mt * 16 + tid < a.M && best_s[tid] != 0ull)
+          atomicMax(&epi.best[mt * 16 + tid], best_s[tid]);
+        greedy_finish(epi, a.M, mt, gridDim.x * gridDim.y, reinterpret_cast<int*>(red), tid);
+      }
     } else {
       // ... then every CTA of the cluster pushes its partial into the
       // leader's slot `rank`; one cluster barrier; the leader finishes.
@@ -279,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
 template <int DT, int G, int RT>
 cudaError_t launch_typed(const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
-                         cudaStream_t stream, bool pdl) {
+                         const RnntEpilogue& epi, cudaStream_t stream, bool pdl) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
   const GemvArgs& args = grp.a[0];
   const GemvSmem L = gemv_smem_layout(RT, plan.sb_per_cta, SUBG, plan.ksplit);
@@ -316,27 +390,27 @@ cudaError_t launch_typed(const GemvPlan& plan, const GemvMaps& maps, const GemvG
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, maps, grp);
+  return cudaLaunchKernelEx(&cfg, kern, maps, grp, epi);
 }
 
 template <int DT, int G>
 cudaError_t launch_rt(const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
-                      cudaStream_t stream, bool pdl) {
+                      const RnntEpilogue& epi, cudaStream_t stream, bool pdl) {
   switch (plan.rt) {
-    case 1: return launch_typed<DT, G, 1>(plan, maps, grp, stream, pdl);
-    case 2: return launch_typed<DT, G, 2>(plan, maps, grp, stream, pdl);
-    case 4: return launch_typed<DT, G, 4>(plan, maps, grp, stream, pdl);
+    case 1: return launch_typed<DT, G, 1>(plan, maps, grp, epi, stream, pdl);
+    case 2: return launch_typed<DT, G, 2>(plan, maps, grp, epi, stream, pdl);
+    case 4: return launch_typed<DT, G, 4>(plan, maps, grp, epi, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <int DT>
 cudaError_t launch_g(int group, const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
-                     cudaStream_t stream, bool pdl) {
+                     const RnntEpilogue& epi, cudaStream_t stream, bool pdl) {
   switch (group) {
-    case 32: return launch_rt<DT, 32>(plan, maps, grp, stream, pdl);
-    case 64: return launch_rt<DT, 64>(plan, maps, grp, stream, pdl);
-    case 128: return launch_rt<DT, 128>(plan, maps, grp, stream, pdl);
+    case 32: return launch_rt<DT, 32>(plan, maps, grp, epi, stream, pdl);
+    case 64: return launch_rt<DT, 64>(plan, maps, grp, epi, stream, pdl);
+    case 128: return launch_rt<DT, 128>(plan, maps, grp, epi, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -395,14 +469,21 @@ size_t gemv_smem_bytes(const GemvPlan& plan, int group) {
 }
 
 cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const GemvMaps& maps,
-                              const GemvGroup& g, cudaStream_t stream, bool pdl) {
+                              const GemvGroup& g, cudaStream_t stream, bool pdl,
+                              const RnntEpilogue* epi) {
   if (g.count < 1 || g.count > kGemvMaxGroup) return cudaErrorInvalidValue;
-  for (int i = 1; i < g.count; ++i)
+  for (int i = 0; i < g.count; ++i) {
     if (g.a[i].N != g.a[0].N || g.a[i].K != g.a[0].K || g.a[i].M != g.a[0].M ||
         g.a[i].sb_per_cta != g.a[0].sb_per_cta)
       return cudaErrorInvalidValue;
-  if (dtype == kF16) return launch_g<kF16>(group, plan, maps, g, stream, pdl);
-  if (dtype == kBF16) return launch_g<kBF16>(group, plan, maps, g, stream, pdl);
+    // the RNNT epilogues need the whole K in one CTA, one member, their arguments
+    if (g.a[i].mode != kGemvPlain && (epi == nullptr || plan.ksplit != 1 || g.count != 1))
+      return cudaErrorInvalidValue;
+  }
+  const RnntEpilogue none{};
+  const RnntEpilogue& e = epi != nullptr ? *epi : none;
+  if (dtype == kF16) return launch_g<kF16>(group, plan, maps, g, e, stream, pdl);
+  if (dtype == kBF16) return launch_g<kBF16>(group, plan, maps, g, e, stream, pdl);
   return cudaErrorInvalidValue;
 }
 

@@ -17,6 +17,37 @@ struct GemvArgs {
   int M, N, K, ldx, ldy;
   int sb_per_cta;      // 64-wide K sub-blocks per CTA
   int act;             // cq::Act
+  int mode;            // kGemvPlain, kGemvJointInput or kGemvGreedy (RnntEpilogue)
+};
+
+// Epilogues of the batched RNNT decoder's two per-symbol linears
+// (StreamingRnntDecoder::decode_frames, rnnt.rs:364-388), so that the joint
+// input and the greedy choice need no launches of their own:
+//  * kGemvJointInput (decoder projector, y = dec_new): active streams take
+//    dec = y, then fused = T(relu(enc + dec)) for every stream;
+//  * kGemvGreedy (vocabulary head, y = logits): each CTA folds its logits into
+//    a per-stream 64-bit maximum of (ordered value, ~index) -- the first index
+//    of the largest logit, MLX argmax -- and the last CTA to finish records the
+//    token (or retires the stream on blank) and gathers the next embedding row.
+enum GemvMode : int { kGemvPlain = 0, kGemvJointInput = 1, kGemvGreedy = 2 };
+struct RnntEpilogue {
+  int* active;  // [S] stream still emitting on this frame
+  // joint input
+  const void* enc;  // T: this frame's encoder projection, row s at enc + s * ld_enc
+  int ld_enc;
+  void* dec;    // T [S, ldy]: decoder output kept per stream
+  void* fused;  // T [S, ldy]: relu(enc + dec), the head's input
+  // greedy choice
+  unsigned long long* best;  // [S] (zero between calls)
+  unsigned* done;            // [M / 16] CTAs finished per token tile (zero between calls)
+  int blank;
+  const void* emb;  // T [V, H] dequantised embedding
+  int H;
+  void* x;  // T [S, H]: the prediction network's next input
+  int* tokens;
+  int* token_frames;
+  int* counts;
+  int cap, frame;
 };
 
 // Work decomposition: RB = 16*rt weight rows per CTA, K split across a
@@ -50,6 +81,7 @@ size_t gemv_smem_bytes(const GemvPlan& plan, int group);
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
                         const GemvArgs& args, cudaStream_t stream, bool pdl);
 cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const GemvMaps& maps,
-                              const GemvGroup& g, cudaStream_t stream, bool pdl);
+                              const GemvGroup& g, cudaStream_t stream, bool pdl,
+                              const RnntEpilogue* epi = nullptr);
 
 }  // namespace cq

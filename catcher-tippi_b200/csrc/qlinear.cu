@@ -524,6 +524,44 @@ void QuantizedLinear::forward_array(const void* x, int ldx, int rows, void* y, i
   check_cuda(cq::launch_gemv(dtype_, group_, plan, wmap, a, stream, pdl_enabled()), "qgemv");
 }
 
+bool QuantizedLinear::rnnt_epilogue_fits(int rows) const {
+  return (dtype_ == CQ_F16 || dtype_ == CQ_BF16) && rows >= 1 && rows < cq::kGemmMinRows &&
+         cq::plan_gemv_rows(plan_, N_, rows).ksplit == 1 && K_ % 8 == 0;
+}
+
+void QuantizedLinear::forward_rnnt(const void* x, int ldx, int rows, void* y, int ldy, int mode,
+                                   const cq::RnntEpilogue& epi, cudaStream_t stream) const {
+  if (!rnnt_epilogue_fits(rows)) throw_invalid("the RNNT epilogues run on the one-CTA GEMV");
+  if (x == nullptr || y == nullptr) throw_invalid("input and output must not be null");
+  if (ldx < K_ || ldy < N_) throw_invalid("leading dimensions are smaller than the layer");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0)
+    throw_invalid("input rows must be 16-byte aligned (x % 16 == 0 and ldx % 8 == 0)");
+  DeviceContext& ctx = device_context(device_);
+  DeviceGuard guard(device_);
+  const cq::GemvPlan plan = cq::plan_gemv_rows(plan_, N_, rows);
+  cq::GemvMaps maps;
+  maps.m[0] = plan.rt == plan_.rt ? wmap_ : wmap_rt_[plan.rt == 1 ? 0 : plan.rt == 2 ? 1 : 2];
+  cq::GemvGroup g{};
+  g.count = 1;
+  cq::GemvArgs& a = g.a[0];
+  a.x = x;
+  a.scales = scales_;
+  a.biases = biases_;
+  a.bias = bias_;
+  a.y = y;
+  a.status = ctx.status;
+  a.M = rows;
+  a.N = N_;
+  a.K = K_;
+  a.ldx = ldx;
+  a.ldy = ldy;
+  a.sb_per_cta = plan_.sb_per_cta;
+  a.act = CQ_ACT_NONE;
+  a.mode = mode;
+  check_cuda(cq::launch_gemv_group(dtype_, group_, plan, maps, g, stream, pdl_enabled(), &epi),
+             "qgemv (RNNT epilogue)");
+}
+
 void QuantizedLinear::forward_group(const GroupCall* calls, int count, int rows, int act,
                                     cudaStream_t stream) {
   if (calls == nullptr || count < 1 || count > cq::kGemvMaxGroup)

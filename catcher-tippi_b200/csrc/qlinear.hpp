@@ -109,6 +109,13 @@ class QuantizedLinear {
   void forward_prescaled(const void* x16, const float* row_scale, int rows, void* y, int ldy,
                          int act, cudaStream_t stream);
 
+  // forward_array on the GEMV with one of the RNNT decoder's epilogues
+  // (cq::kGemvJointInput / kGemvGreedy, see qgemv.hpp); rows below the GEMM
+  // threshold and K within one CTA, else invalid-argument.
+  void forward_rnnt(const void* x, int ldx, int rows, void* y, int ldy, int mode,
+                    const cq::RnntEpilogue& epi, cudaStream_t stream) const;
+  bool rnnt_epilogue_fits(int rows) const;
+
   struct GroupCall {
     const QuantizedLinear* layer;
     const void* x;

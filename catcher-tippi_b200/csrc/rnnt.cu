@@ -288,6 +288,14 @@ RnntState::RnntState(RnntDecoder& dec, int streams, int max_frames)
   lstm_fused_ = dec_.lstm_fused() && S_ < cq::kGemmMinRows;
   if (lstm_fused_)
     for (int l = 0; l < c.lstm_layers; ++l) h_next_.emplace_back(S * H * 2);
+  fused_epi_ = lstm_fused_ && H % 8 == 0 && dec_.head()->rnnt_epilogue_fits(S_) &&
+               dec_.dec_proj()->rnnt_epilogue_fits(S_);
+  if (fused_epi_) {
+    best_ = DeviceBuffer(S * sizeof(unsigned long long));
+    done_ = DeviceBuffer(static_cast<size_t>((S_ + 15) / 16) * sizeof(unsigned));
+    check_cuda(cudaMemset(best_.get(), 0, best_.bytes()), "greedy keys");
+    check_cuda(cudaMemset(done_.get(), 0, done_.bytes()), "greedy counter");
+  }
   size_t need = dec_.enc_proj()->scratch_bytes_for(S_ * max_frames);
   for (const QuantizedLinear* L : {dec_.head(), dec_.dec_proj()}) need = std::max(need, L->scratch_bytes_for(S_));
   for (int l = 0; l < c.lstm_layers; ++l)
@@ -327,7 +335,7 @@ void RnntState::linear(QuantizedLinear* L, const void* x, int ldx, int rows, voi
 
 // PredictionNetwork::step for the streams whose flag is set (or all): the
 // LSTM stack on x, then the decoder projector into dec_new.
-void RnntState::prediction_step(bool all, cudaStream_t st) {
+void RnntState::prediction_step(bool all, cudaStream_t st, const cq::RnntEpilogue* proj_epi) {
   const auto& c = dec_.config();
   const int dt = dec_.dtype() == CQ_BF16 ? cq::kBF16 : cq::kF16;
   const bool pdl = pdl_on();
@@ -360,7 +368,11 @@ void RnntState::prediction_step(bool all, cudaStream_t st) {
       hpar_[l] ^= 1;
       in = h_cur(l);
     }
-    linear(dec_.dec_proj(), in, H, S_, dec_new_.get(), c.joint_hidden, CQ_ACT_NONE, st);
+    if (proj_epi != nullptr)
+      dec_.dec_proj()->forward_rnnt(in, H, S_, dec_new_.get(), c.joint_hidden, cq::kGemvJointInput,
+                                    *proj_epi, st);
+    else
+      linear(dec_.dec_proj(), in, H, S_, dec_new_.get(), c.joint_hidden, CQ_ACT_NONE, st);
     return;
   }
   const void* in = x_.get();
@@ -478,7 +490,30 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
     check_cuda(cq::launch_joint_input(dt, enc_f, frames * J, nullptr, dec_out_.get(), fused_.get(),
                                       active_.as<int>(), S_, J, false, true, st, pdl),
                "joint input");
-    for (int sym = 0; sym < c.max_symbols; ++sym) {
+    for (int sym = 0; sym < c.max_symbols && fused_epi_; ++sym) {
+      // head + greedy choice, then the prediction step whose projector
+      // updates the joint input: four launches per symbol
+      cq::RnntEpilogue e{};
+      e.active = active_.as<int>();
+      e.enc = enc_f;
+      e.ld_enc = frames * J;
+      e.dec = dec_out_.get();
+      e.fused = fused_.get();
+      e.best = best_.as<unsigned long long>();
+      e.done = done_.as<unsigned>();
+      e.blank = c.blank;
+      e.emb = dec_.embedding();
+      e.H = H;
+      e.x = x_.get();
+      e.tokens = tokens;
+      e.token_frames = token_frames;
+      e.counts = counts;
+      e.cap = cap;
+      e.frame = f;
+      dec_.head()->forward_rnnt(fused_.get(), J, S_, logits_.get(), V, cq::kGemvGreedy, e, st);
+      prediction_step(false, st, &e);
+    }
+    for (int sym = 0; sym < c.max_symbols && !fused_epi_; ++sym) {
       linear(dec_.head(), fused_.get(), J, S_, logits_.get(), V, CQ_ACT_NONE, st);
       check_cuda(cq::launch_argmax_emit(dt, logits_.get(), V, V, c.blank, active_.as<int>(),
                                         dec_.embedding(), H, x_.get(), tokens, token_frames, counts, cap,

@@ -13,6 +13,7 @@
 
 #include "cqrnnt.h"
 #include "device_buffer.hpp"
+#include "qgemv.hpp"
 #include "qlinear.hpp"
 
 namespace nemotron_cuda {
@@ -98,7 +99,9 @@ class RnntState {
  private:
   void launch_chunk(const void* encoded, int ld, int frames, int* tokens, int* token_frames,
                     int* counts, cudaStream_t stream);
-  void prediction_step(bool all, cudaStream_t stream);
+  // proj_epi: the decoder projector also updates the joint input (active
+  // streams' decoder output and relu(enc + dec)) in its epilogue
+  void prediction_step(bool all, cudaStream_t stream, const cq::RnntEpilogue* proj_epi = nullptr);
   // the one-launch LSTM step writes each layer's new hidden state into the
   // other of two buffers; these give the current / other one and bring the
   // state back into h_ (at chunk ends, so captured graphs replay alike)
@@ -114,6 +117,10 @@ class RnntState {
   DeviceBuffer ep_, dec_out_, dec_new_, fused_, logits_, x_, gi_, gh_, active_;
   std::vector<DeviceBuffer> h_, c_;
   bool lstm_fused_ = false;
+  // head and projector carry the greedy choice and the joint input in their
+  // epilogues (per-stream argmax keys and a CTA counter, zero between calls)
+  bool fused_epi_ = false;
+  DeviceBuffer best_, done_;
   std::vector<DeviceBuffer> h_next_;
   std::vector<int> hpar_;
   // persistent path: second hidden-state buffer per layer, head partials, barrier
