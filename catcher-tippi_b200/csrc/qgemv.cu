@@ -76,6 +76,31 @@ __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
+// Kernel parameter blocks: one layer (every ordinary call), a group of
+// same-shape layers, or one layer with an RNNT epilogue.  Separate layouts
+// keep the common launch's parameters small (one map, one argument block).
+enum GemvKind : int { kKindPlain = 0, kKindGroup = 1, kKindEpilogue = 2 };
+template <int KIND>
+struct GemvParams {
+  CUtensorMap m[1];
+  GemvArgs a[1];
+  __device__ int count() const { return 1; }
+};
+template <>
+struct GemvParams<kKindGroup> {
+  CUtensorMap m[kGemvMaxGroup];
+  GemvArgs a[kGemvMaxGroup];
+  int n;
+  __device__ int count() const { return n; }
+};
+template <>
+struct GemvParams<kKindEpilogue> {
+  CUtensorMap m[1];
+  GemvArgs a[1];
+  RnntEpilogue epi;
+  __device__ int count() const { return 1; }
+};
+
 // Greedy epilogue, after this CTA folded token tile mt's maxima into
 // epi.best: the last of the tile's `ctas` CTAs records the choices of its 16
 // streams (one atomic round trip) and gathers their next embedding rows.
@@ -124,10 +149,8 @@ __device__ void greedy_finish(const RnntEpilogue& epi, int M, int mt, unsigned c
   __syncthreads();
 }
 
-template <int DT, int G, int RT>
-__global__ void __launch_bounds__(kThreads, 2)
-    qgemv_kernel(const __grid_constant__ GemvMaps maps, const __grid_constant__ GemvGroup grp,
-                 const __grid_constant__ RnntEpilogue epi) {
+template <int DT, int G, int RT, int KIND>
+__global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constant__ GemvParams<KIND> P) {
   constexpr int RB = 16 * RT;
   constexpr int SUBG = (G == 32) ? 2 : 1;  // groups per 64-wide sub-block
   extern __shared__ __align__(128) uint8_t smem[];
@@ -135,10 +158,10 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int S = gridDim.x;  // K-split factor == cluster size along x
   const int rank = blockIdx.x;
   // member of the group and band within it
-  const int bands = (grp.a[0].N + RB - 1) / RB;
-  const int member = blockIdx.y / bands;
-  const GemvArgs& a = grp.a[member];
-  const CUtensorMap* wmap = &maps.m[member];
+  const int bands = (P.a[0].N + RB - 1) / RB;
+  const int member = KIND == kKindGroup ? static_cast<int>(blockIdx.y) / bands : 0;
+  const GemvArgs& a = P.a[member];
+  const CUtensorMap* wmap = &P.m[member];
   const int n0 = (blockIdx.y - member * bands) * RB;
   const int nsb = (a.K + 63) >> 6;
   const int sb0 = rank * a.sb_per_cta;
@@ -283,8 +306,10 @@ __global__ void __launch_bounds__(kThreads, 2)
     // element e = tok * RB + row: consecutive threads write consecutive n
     if (S == 1) {
       unsigned long long* best_s = reinterpret_cast<unsigned long long*>(fin);  // [16], greedy mode
-      if (a.mode == kGemvGreedy && tid < 16) best_s[tid] = 0ull;
-      if (a.mode == kGemvGreedy) __syncthreads();
+      if (KIND == kKindEpilogue && a.mode == kGemvGreedy) {
+        if (tid < 16) best_s[tid] = 0ull;
+        __syncthreads();
+      }
       for (int e = tid; e < RB * 16; e += kThreads) {
         const int row = e % RB, tok = e / RB;
         float v = 0.f;
@@ -295,12 +320,13 @@ __global__ void __launch_bounds__(kThreads, 2)
           const float o = epilogue_value<DT>(v, has_bias, biasm[row], a.act);
           const size_t off = static_cast<size_t>(m) * a.ldy + n;
           st_t<DT>(a.y, off, o);
-          if (a.mode == kGemvJointInput) {
+          if constexpr (KIND != kKindEpilogue) {
+          } else if (a.mode == kGemvJointInput) {
             float d = o;
-            if (epi.active[m]) st_t<DT>(epi.dec, off, o);
-            else d = ld_t<DT>(epi.dec, off);
-            const float en = ld_t<DT>(epi.enc, static_cast<size_t>(m) * epi.ld_enc + n);
-            st_t<DT>(epi.fused, off, fmaxf(en + d, 0.0f));
+            if (P.epi.active[m]) st_t<DT>(P.epi.dec, off, o);
+            else d = ld_t<DT>(P.epi.dec, off);
+            const float en = ld_t<DT>(P.epi.enc, static_cast<size_t>(m) * P.epi.ld_enc + n);
+            st_t<DT>(P.epi.fused, off, fmaxf(en + d, 0.0f));
           } else if (a.mode == kGemvGreedy && !isnan(o)) {
             // larger logit -> larger key; equal logits -> the smaller index
             const uint32_t u = __float_as_uint(o);
@@ -311,10 +337,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       __syncthreads();
-      if (a.mode == kGemvGreedy) {
-        if (tid < 16 && mt * 16 + tid < a.M && best_s[tid] != 0ull)
-          atomicMax(&epi.best[mt * 16 + tid], best_s[tid]);
-        greedy_finish(epi, a.M, mt, gridDim.x * gridDim.y, reinterpret_cast<int*>(red), tid);
+      if constexpr (KIND == kKindEpilogue) {
+        if (a.mode == kGemvGreedy) {
+          if (tid < 16 && mt * 16 + tid < a.M && best_s[tid] != 0ull)
+            atomicMax(&P.epi.best[mt * 16 + tid], best_s[tid]);
+          greedy_finish(P.epi, a.M, mt, gridDim.x * gridDim.y, reinterpret_cast<int*>(red), tid);
+        }
       }
     } else {
       // ... then every CTA of the cluster pushes its partial into the
@@ -351,13 +379,13 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 }
 
-template <int DT, int G, int RT>
-cudaError_t launch_typed(const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
-                         const RnntEpilogue& epi, cudaStream_t stream, bool pdl) {
+template <int DT, int G, int RT, int KIND>
+cudaError_t launch_typed(const GemvPlan& plan, const GemvParams<KIND>& P, int count,
+                         cudaStream_t stream, bool pdl) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
-  const GemvArgs& args = grp.a[0];
+  const GemvArgs& args = P.a[0];
   const GemvSmem L = gemv_smem_layout(RT, plan.sb_per_cta, SUBG, plan.ksplit);
-  auto kern = qgemv_kernel<DT, G, RT>;
+  auto kern = qgemv_kernel<DT, G, RT, KIND>;
   static int configured_smem = 0;
   if (static_cast<int>(L.total) > configured_smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -367,7 +395,7 @@ cudaError_t launch_typed(const GemvPlan& plan, const GemvMaps& maps, const GemvG
   }
   cudaLaunchConfig_t cfg = {};
   // token tiles beyond the first spread over grid.z, within one wave
-  const int bands = (args.N + 16 * RT - 1) / (16 * RT) * grp.count;
+  const int bands = (args.N + 16 * RT - 1) / (16 * RT) * count;
   const int mtiles = (args.M + 15) / 16;
   const int zmax = std::max(1, (2 * plan.num_sms) / std::max(1, bands * plan.ksplit));
   cfg.gridDim = dim3(plan.ksplit, bands, std::min(mtiles, zmax));
@@ -390,27 +418,34 @@ cudaError_t launch_typed(const GemvPlan& plan, const GemvMaps& maps, const GemvG
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, maps, grp, epi);
+  return cudaLaunchKernelEx(&cfg, kern, P);
 }
 
-template <int DT, int G>
-cudaError_t launch_rt(const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
-                      const RnntEpilogue& epi, cudaStream_t stream, bool pdl) {
+template <int DT, int G, int KIND>
+cudaError_t launch_rt(const GemvPlan& plan, const GemvParams<KIND>& P, int count,
+                      cudaStream_t stream, bool pdl) {
   switch (plan.rt) {
-    case 1: return launch_typed<DT, G, 1>(plan, maps, grp, epi, stream, pdl);
-    case 2: return launch_typed<DT, G, 2>(plan, maps, grp, epi, stream, pdl);
-    case 4: return launch_typed<DT, G, 4>(plan, maps, grp, epi, stream, pdl);
+    case 1: return launch_typed<DT, G, 1, KIND>(plan, P, count, stream, pdl);
+    case 2: return launch_typed<DT, G, 2, KIND>(plan, P, count, stream, pdl);
+    case 4: return launch_typed<DT, G, 4, KIND>(plan, P, count, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <int DT>
-cudaError_t launch_g(int group, const GemvPlan& plan, const GemvMaps& maps, const GemvGroup& grp,
-                     const RnntEpilogue& epi, cudaStream_t stream, bool pdl) {
+template <int KIND>
+cudaError_t launch_kind(int dtype, int group, const GemvPlan& plan, const GemvParams<KIND>& P,
+                        int count, cudaStream_t stream, bool pdl) {
+  if (dtype != kF16 && dtype != kBF16) return cudaErrorInvalidValue;
   switch (group) {
-    case 32: return launch_rt<DT, 32>(plan, maps, grp, epi, stream, pdl);
-    case 64: return launch_rt<DT, 64>(plan, maps, grp, epi, stream, pdl);
-    case 128: return launch_rt<DT, 128>(plan, maps, grp, epi, stream, pdl);
+    case 32:
+      return dtype == kF16 ? launch_rt<kF16, 32, KIND>(plan, P, count, stream, pdl)
+                           : launch_rt<kBF16, 32, KIND>(plan, P, count, stream, pdl);
+    case 64:
+      return dtype == kF16 ? launch_rt<kF16, 64, KIND>(plan, P, count, stream, pdl)
+                           : launch_rt<kBF16, 64, KIND>(plan, P, count, stream, pdl);
+    case 128:
+      return dtype == kF16 ? launch_rt<kF16, 128, KIND>(plan, P, count, stream, pdl)
+                           : launch_rt<kBF16, 128, KIND>(plan, P, count, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -480,21 +515,34 @@ cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const 
     if (g.a[i].mode != kGemvPlain && (epi == nullptr || plan.ksplit != 1 || g.count != 1))
       return cudaErrorInvalidValue;
   }
-  const RnntEpilogue none{};
-  const RnntEpilogue& e = epi != nullptr ? *epi : none;
-  if (dtype == kF16) return launch_g<kF16>(group, plan, maps, g, e, stream, pdl);
-  if (dtype == kBF16) return launch_g<kBF16>(group, plan, maps, g, e, stream, pdl);
-  return cudaErrorInvalidValue;
+  if (epi != nullptr && g.a[0].mode != kGemvPlain) {
+    GemvParams<kKindEpilogue> P;
+    P.m[0] = maps.m[0];
+    P.a[0] = g.a[0];
+    P.epi = *epi;
+    return launch_kind(dtype, group, plan, P, 1, stream, pdl);
+  }
+  if (g.count == 1) {
+    GemvParams<kKindPlain> P;
+    P.m[0] = maps.m[0];
+    P.a[0] = g.a[0];
+    return launch_kind(dtype, group, plan, P, 1, stream, pdl);
+  }
+  GemvParams<kKindGroup> P;
+  for (int i = 0; i < g.count; ++i) {
+    P.m[i] = maps.m[i];
+    P.a[i] = g.a[i];
+  }
+  P.n = g.count;
+  return launch_kind(dtype, group, plan, P, g.count, stream, pdl);
 }
 
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
                         const GemvArgs& args, cudaStream_t stream, bool pdl) {
-  GemvMaps maps;
-  maps.m[0] = wmap;
-  GemvGroup g{};
-  g.a[0] = args;
-  g.count = 1;
-  return launch_gemv_group(dtype, group, plan, maps, g, stream, pdl);
+  GemvParams<kKindPlain> P;
+  P.m[0] = wmap;
+  P.a[0] = args;
+  return launch_kind(dtype, group, plan, P, 1, stream, pdl);
 }
 
 }  // namespace cq
