@@ -12,7 +12,10 @@
 // interleaved at load time (row 4j + q holds gate q of hidden unit j) so one
 // band holds all four gates of 16 hidden units.  The new hidden state goes to
 // a second buffer (other CTAs still read the old one); streams that are not
-// active keep their state (h copied across, c untouched).
+// active keep their state (h copied across, c untouched).  Token tiles
+// spread over grid.z; when all clusters fit one wave the kernel runs one CTA
+// per SM with the registers that allows, else two per SM (a cluster walks
+// several token tiles only past the grid limit, at one CTA per SM).
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "rnnt_ops.hpp"
@@ -43,8 +46,8 @@ __host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg) {
   off += static_cast<size_t>(sbn) * subg * kRB * sizeof(float2);
   L.red = off;  // [8][64][16] per-warp partials
   off += static_cast<size_t>(kNW) * kRB * 16 * sizeof(float);
-  L.fin = off;  // [2][64][16]: the two products of rank 0's band
-  off += 2ull * kRB * 16 * sizeof(float);
+  L.fin = off;  // [2 tiles in flight][2 products][64][16] of rank 0's band
+  off += 4ull * kRB * 16 * sizeof(float);
   L.total = off;
   return L;
 }
@@ -58,14 +61,13 @@ __device__ __forceinline__ float sigmoid_t(float x) {
   return round_t<DT>(1.0f / (1.0f + expf(-x)));
 }
 
-template <int DT, int G>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int DT, int G, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
     lstm_step_kernel(const __grid_constant__ LstmMaps maps, const LstmStepArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   const int rank = blockIdx.x;  // 0: W_ih x, 1: W_hh h
   const int n0 = blockIdx.y * kRB;
-  const int mt = blockIdx.z;
   const int H = a.H, K = a.H, N = 4 * a.H;
   const int sbn = (K + 63) >> 6;
   const int groups_per_row = K / G;
@@ -111,115 +113,156 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   pdl_wait();
 
-  // ---- activations of this token tile, all loads in flight at once
-  uint4 xr[kSbPerWarp][2][2];
-#pragma unroll
-  for (int u = 0; u < kSbPerWarp; ++u) {
-    const int j = warp + u * kNW;
-    if (j < sbn) {
-      load_x_raw<G>(x, H, a.S, K, mt * 16 + r4, j * 64, c, xr[u][0][0], xr[u][0][1]);
-      load_x_raw<G>(x, H, a.S, K, mt * 16 + 8 + r4, j * 64, c, xr[u][1][0], xr[u][1][1]);
-    }
-  }
-  float acc[kRT][2][4];
-#pragma unroll
-  for (int i = 0; i < kRT; ++i)
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
   bool ok = true;
-#pragma unroll
-  for (int u = 0; u < kSbPerWarp; ++u) {
-    const int j = warp + u * kNW;
-    if (j >= sbn) break;
-    const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
-    ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
-    subblock_mma<DT, G, kRT>(wt + static_cast<size_t>(j) * kRB * 64,
-                             sbsm + static_cast<size_t>(j) * SUBG * kRB, xo, lane, acc);
-  }
-#pragma unroll
-  for (int i = 0; i < kRT; ++i) {
-    const int ra = 16 * i + r4, rb = ra + 8;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      *reinterpret_cast<float2*>(&red[(warp * kRB + ra) * 16 + 8 * nt + 2 * c]) =
-          make_float2(acc[i][nt][0], acc[i][nt][1]);
-      *reinterpret_cast<float2*>(&red[(warp * kRB + rb) * 16 + 8 * nt + 2 * c]) =
-          make_float2(acc[i][nt][2], acc[i][nt][3]);
-    }
-  }
-  __syncthreads();
-  // this CTA's product into rank 0's slot `rank` ([row][token], warp order)
-  const uint32_t slot = mapa_shared(smem_u32(fin), 0) +
-                        static_cast<uint32_t>(rank * kRB * 16 * sizeof(float));
-  for (int e = tid; e < kRB * 16; e += kThreads) {
-    float v = 0.f;
-#pragma unroll
-    for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
-    st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
-  }
-  cluster_sync_all();
-
-  if (rank == 0) {
-    // one (hidden unit, token) per thread: 16 units x 16 tokens
-    const int u = tid >> 4, t = tid & 15;
-    const int s = mt * 16 + t;
-    const int j = n0 / 4 + u;
-    if (s < a.S && j < H) {
-      const size_t hj = static_cast<size_t>(s) * H + j;
-      if (a.all || a.active[s]) {
-        float gate[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int row = 4 * u + q;
-          const float gi = round_t<DT>(fin[row * 16 + t]);
-          const float gh = round_t<DT>(fin[kRB * 16 + row * 16 + t]);
-          gate[q] = round_t<DT>(round_t<DT>(gi + gh) + ld_t<DT>(a.gate_bias, n0 + row));
-        }
-        const float ig = sigmoid_t<DT>(gate[0]);
-        const float fg = sigmoid_t<DT>(gate[1]);
-        const float gg = round_t<DT>(tanhf(gate[2]));
-        const float og = sigmoid_t<DT>(gate[3]);
-        const float c_prev = ld_t<DT>(a.c, hj);
-        const float c_new = round_t<DT>(round_t<DT>(fg * c_prev) + round_t<DT>(ig * gg));
-        const float h_new = round_t<DT>(og * round_t<DT>(tanhf(c_new)));
-        st_t<DT>(a.c, hj, c_new);
-        st_t<DT>(a.h_out, hj, h_new);
-      } else {
-        st_t<DT>(a.h_out, hj, ld_t<DT>(a.h_prev, hj));  // state kept
+  auto tile = [&](const int mt, const int round) {
+    // ---- activations of this token tile, all loads in flight at once
+    uint4 xr[kSbPerWarp][2][2];
+    #pragma unroll
+    for (int u = 0; u < kSbPerWarp; ++u) {
+      const int j = warp + u * kNW;
+      if (j < sbn) {
+        load_x_raw<G>(x, H, a.S, K, mt * 16 + r4, j * 64, c, xr[u][0][0], xr[u][0][1]);
+        load_x_raw<G>(x, H, a.S, K, mt * 16 + 8 + r4, j * 64, c, xr[u][1][0], xr[u][1][1]);
       }
     }
+    float acc[kRT][2][4];
+    #pragma unroll
+    for (int i = 0; i < kRT; ++i)
+      #pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+        #pragma unroll
+        for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
+    #pragma unroll
+    for (int u = 0; u < kSbPerWarp; ++u) {
+      const int j = warp + u * kNW;
+      if (j >= sbn) break;
+      const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
+      ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
+      subblock_mma<DT, G, kRT>(wt + static_cast<size_t>(j) * kRB * 64,
+                               sbsm + static_cast<size_t>(j) * SUBG * kRB, xo, lane, acc);
+    }
+    #pragma unroll
+    for (int i = 0; i < kRT; ++i) {
+      const int ra = 16 * i + r4, rb = ra + 8;
+      #pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        *reinterpret_cast<float2*>(&red[(warp * kRB + ra) * 16 + 8 * nt + 2 * c]) =
+            make_float2(acc[i][nt][0], acc[i][nt][1]);
+        *reinterpret_cast<float2*>(&red[(warp * kRB + rb) * 16 + 8 * nt + 2 * c]) =
+            make_float2(acc[i][nt][2], acc[i][nt][3]);
+      }
+    }
+    __syncthreads();
+    // this CTA's product into rank 0's slot `rank` ([row][token], warp order)
+    // fin alternates between two buffers: a CTA's push for the next tile is
+    // preceded by this tile's cluster barrier, which rank 0 passes only
+    // after it read the buffer before -- one barrier per tile suffices
+    float* fbuf = fin + (round & 1) * 2 * kRB * 16;
+    const uint32_t slot = mapa_shared(smem_u32(fbuf), 0) +
+                          static_cast<uint32_t>(rank * kRB * 16 * sizeof(float));
+    for (int e = tid; e < kRB * 16; e += kThreads) {
+      float v = 0.f;
+      #pragma unroll
+      for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
+      st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
+    }
+    cluster_sync_all();
+
+    if (rank == 0) {
+      // one (hidden unit, token) per thread: 16 units x 16 tokens
+      const int u = tid >> 4, t = tid & 15;
+      const int s = mt * 16 + t;
+      const int j = n0 / 4 + u;
+      if (s < a.S && j < H) {
+        const size_t hj = static_cast<size_t>(s) * H + j;
+        if (a.all || a.active[s]) {
+          float gate[4];
+          #pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int row = 4 * u + q;
+            const float gi = round_t<DT>(fbuf[row * 16 + t]);
+            const float gh = round_t<DT>(fbuf[kRB * 16 + row * 16 + t]);
+            gate[q] = round_t<DT>(round_t<DT>(gi + gh) + ld_t<DT>(a.gate_bias, n0 + row));
+          }
+          const float ig = sigmoid_t<DT>(gate[0]);
+          const float fg = sigmoid_t<DT>(gate[1]);
+          const float gg = round_t<DT>(tanhf(gate[2]));
+          const float og = sigmoid_t<DT>(gate[3]);
+          const float c_prev = ld_t<DT>(a.c, hj);
+          const float c_new = round_t<DT>(round_t<DT>(fg * c_prev) + round_t<DT>(ig * gg));
+          const float h_new = round_t<DT>(og * round_t<DT>(tanhf(c_new)));
+          st_t<DT>(a.c, hj, c_new);
+          st_t<DT>(a.h_out, hj, h_new);
+        } else {
+          st_t<DT>(a.h_out, hj, ld_t<DT>(a.h_prev, hj));  // state kept
+        }
+      }
+    }
+  };
+  if constexpr (MINB == 1) {
+    for (int mt = blockIdx.z, round = 0; mt < (a.S + 15) / 16; mt += gridDim.z, ++round)
+      tile(mt, round);
+  } else {
+    tile(blockIdx.z, 0);  // launches at two CTAs per SM carry every token tile on grid.z
   }
   if (!ok && tid == 0)
     for (int j = 0; j < sbn; ++j) mbar_wait_bounded(&bars[j], 0, a.status);
 }
 
-template <int DT>
-cudaError_t launch_t(int group, const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream,
-                     bool pdl) {
-  void (*kern)(const LstmMaps, const LstmStepArgs) = nullptr;
-  int subg = 1;
-  switch (group) {
-    case 32: kern = lstm_step_kernel<DT, 32>; subg = 2; break;
-    case 64: kern = lstm_step_kernel<DT, 64>; break;
-    case 128: kern = lstm_step_kernel<DT, 128>; break;
-    default: return cudaErrorInvalidValue;
+// Clusters of a launch configuration resident at once (cached per kernel).
+int resident_clusters(const void* kern, cudaLaunchConfig_t cfg, int* cache) {
+  if (*cache > 0) return *cache;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = 2;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+    (void)cudaGetLastError();
+    n = 1;
   }
-  const LstmSmem L = lstm_smem_layout((a.H + 63) / 64, subg);
-  static int configured[3] = {0, 0, 0};  // per group size
-  int& conf = configured[group == 32 ? 0 : group == 64 ? 1 : 2];
-  if (static_cast<int>(L.total) > conf) {
+  *cache = n;
+  return n;
+}
+
+template <int DT, int G, int MINB>
+cudaError_t launch_cfg(const LstmMaps& maps, const LstmStepArgs& a, cudaLaunchConfig_t cfg) {
+  auto kern = lstm_step_kernel<DT, G, MINB>;
+  static int configured = 0;
+  if (static_cast<int>(cfg.dynamicSmemBytes) > configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(L.total));
+                                         static_cast<int>(cfg.dynamicSmemBytes));
     if (e != cudaSuccess) return e;
-    conf = static_cast<int>(L.total);
+    configured = static_cast<int>(cfg.dynamicSmemBytes);
   }
+  return cudaLaunchKernelEx(&cfg, kern, maps, a);
+}
+
+template <int DT, int G>
+cudaError_t launch_g(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream, bool pdl) {
+  constexpr int SUBG = (G == 32) ? 2 : 1;
+  const LstmSmem L = lstm_smem_layout((a.H + 63) / 64, SUBG);
+  const int bands = (4 * a.H + kRB - 1) / kRB;
+  const int mtiles = (a.S + 15) / 16;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2, (4 * a.H + kRB - 1) / kRB, (a.S + 15) / 16);
+  cfg.gridDim = dim3(2, bands, std::min(mtiles, 65535));
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
+  // one wave at one CTA per SM?  (needs the smem attribute set first)
+  static int res1 = 0;
+  if (res1 == 0) {
+    cudaError_t e = cudaFuncSetAttribute(lstm_step_kernel<DT, G, 1>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(L.total));
+    if (e != cudaSuccess) return e;
+  }
+  const bool one_wave =
+      bands * mtiles <= resident_clusters(reinterpret_cast<const void*>(lstm_step_kernel<DT, G, 1>),
+                                          cfg, &res1);
   cudaLaunchAttribute attrs[2];
   int na = 0;
   attrs[na].id = cudaLaunchAttributeClusterDimension;
@@ -234,7 +277,19 @@ cudaError_t launch_t(int group, const LstmMaps& maps, const LstmStepArgs& a, cud
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, maps, a);
+  return one_wave || mtiles > 65535 ? launch_cfg<DT, G, 1>(maps, a, cfg)
+                                    : launch_cfg<DT, G, 2>(maps, a, cfg);
+}
+
+template <int DT>
+cudaError_t launch_t(int group, const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream,
+                     bool pdl) {
+  switch (group) {
+    case 32: return launch_g<DT, 32>(maps, a, stream, pdl);
+    case 64: return launch_g<DT, 64>(maps, a, stream, pdl);
+    case 128: return launch_g<DT, 128>(maps, a, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace
