@@ -422,6 +422,83 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
     return res
 
 
+def bench_rnnt(torch, cq, args, world: int, local_rank: int, dist, streams: int) -> dict:
+    """Batched RNNT greedy decode alone (cq_rnnt_decode_chunk): one step = one
+    chunk of 14 encoder frames for every stream, the encoder output a fixed
+    random bf16 tensor (random weights emit the maximum of 10 symbols per
+    frame); e2e adds the pinned-host copy of the encoder output and the token
+    read-back to every step."""
+    from nemotron_cuda.rnnt import Rnnt
+    frames = 14
+    rn = Rnnt.random(None, seed=13, dtype="bf16", device=local_rank)
+    st = rn.state(streams, frames)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(17 + local_rank)
+    enc = (torch.randn((streams * frames, 1024), generator=gen, device="cuda") * 0.5) \
+        .to(torch.bfloat16)
+    host_enc = torch.empty((streams * frames, 1024), dtype=torch.bfloat16).pin_memory()
+    host_enc.copy_(enc.cpu())
+    tok = torch.empty((streams, st.capacity), dtype=torch.int32, device="cuda")
+    tfr, cnt = torch.empty_like(tok), torch.empty((streams,), dtype=torch.int32, device="cuda")
+    host_tok = torch.empty((streams, st.capacity), dtype=torch.int32).pin_memory()
+    host_cnt = torch.empty((streams,), dtype=torch.int32).pin_memory()
+    s = torch.cuda.Stream()
+
+    def run(n: int, e2e: bool) -> None:
+        with torch.cuda.stream(s):
+            for _ in range(n):
+                if e2e:
+                    enc.copy_(host_enc, non_blocking=True)
+                st.decode_chunk_raw(enc, frames, tok, tfr, cnt, stream=s)
+                if e2e:
+                    host_cnt.copy_(cnt, non_blocking=True)
+                    host_tok.copy_(tok, non_blocking=True)
+
+    def timed(e2e: bool) -> float:
+        run(args.warmup, e2e)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        run(args.steps, e2e)
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    ms = timed(False)
+    clock_info = clocks.stop()
+    ms_e2e = timed(True)
+    status = cq.device_status(local_rank)
+    if status != 0:
+        raise RuntimeError(f"device watchdog reported status {status}")
+    audio = world * streams * CHUNK_AUDIO_S * args.steps
+    res = {
+        "metric": "RNNT decode audio-sec/sec", "value": round(audio / (ms * 1e-3), 1),
+        "unit": "audio-s/s", "ms_per_chunk": round(ms / args.steps, 4),
+        "symbols_per_stream_per_chunk": round(float(cnt.float().mean().item()), 1),
+        "workload": (f"batched RNNT greedy decode (2-layer LSTM 640, joint 640 -> vocab 1025, at "
+                     f"most 10 symbols per frame), {streams} lock-step streams per GPU, 14 encoder "
+                     f"frames (1.12 s) per chunk, random-init INT8 group 64 bf16"),
+        "clocks": clock_info, "gpu_launches": st.kernels_per_chunk * args.steps,
+        "e2e": {"value": round(audio / (ms_e2e * 1e-3), 1), "unit": "audio-s/s",
+                "h2d_bytes_per_step": host_enc.numel() * 2,
+                "d2h_bytes_per_step": (host_tok.numel() + host_cnt.numel()) * 4,
+                "path": "pinned host encoder output -> device, cq_rnnt_decode_chunk, token ids "
+                        "and counts -> pinned host, every chunk inside the timed region"},
+    }
+    del st, rn
+    return res
+
+
 def cpu_encoder_baseline(target_s: float = 8.0, with_rnnt: bool = True) -> dict:
     """The CPU restatement of the encoder (oracle/encoder_oracle.py, numpy +
     the OpenMP C linear) and, with `with_rnnt`, of the RNNT greedy decoder
@@ -493,6 +570,23 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds, not args.no_rnnt)
         return line
+    if args.workload == "rnnt":
+        res = bench_rnnt(torch, cq, args, world, local_rank, dist, args.streams)
+        if dist:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        return {"metric": res["metric"], "value": res["value"], "unit": res["unit"],
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": res["ms_per_chunk"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init INT8 weights; encoder output ~ N(0, 0.25))",
+                "config": {"workload": res["workload"], "group_size": GROUP,
+                           "streams_per_gpu": args.streams,
+                           "symbols_per_stream_per_chunk": res["symbols_per_stream_per_chunk"],
+                           "parallelism": f"dp{world} (replicated weights, independent streams)",
+                           "l2": "weights (7.6 MB) L2-resident; every step reads them again"},
+                "e2e": res["e2e"], "clocks": res["clocks"], "gpu_launches": res["gpu_launches"]}
     step_flops = None
     if args.workload == "linear":
         enc = SingleLinear(torch, cq, local_rank)
@@ -733,16 +827,16 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "linear", "batched", "encoder"],
+    ap.add_argument("--workload", choices=["block", "linear", "batched", "encoder", "rnnt"],
                     default="block",
                     help="block: the 24-block M=14 linear chain (default, plus the full "
                          "encoder at 64 streams and at 1 stream as the line's 'encoder' "
                          "object); linear: one 4096x1024 linear, independent back-to-back "
                          "launches; batched: the 24-block chain at M=896 (64 streams), "
                          "tensor-core path; encoder: the full streaming encoder alone "
-                         "(value in audio-s/s)")
+                         "(value in audio-s/s); rnnt: the batched RNNT greedy decoder alone")
     ap.add_argument("--streams", type=int, default=ENC_STREAMS,
-                    help="streams per GPU of the encoder workload")
+                    help="streams per GPU of the encoder and rnnt workloads")
     ap.add_argument("--encoder-chunks", type=int, default=20,
                     help="timed chunks of the encoder measurement in the default run")
     ap.add_argument("--no-encoder", action="store_true")

@@ -135,9 +135,10 @@ __device__ void greedy_finish(const RnntEpilogue& epi, int M, int mt, unsigned c
       }
     }
     scratch[tid] = out;
+    if (epi.last_token != nullptr && out >= 0) epi.last_token[s] = out;
   }
   __syncthreads();
-  const int per_row = epi.H / 8;
+  const int per_row = epi.last_token != nullptr ? 0 : epi.H / 8;
   for (int i = tid; i < 16 * per_row; i += kThreads) {
     const int t = i / per_row, c8 = (i - t * per_row) * 8;
     if (scratch[t] < 0) continue;

@@ -44,6 +44,9 @@ struct RnntEpilogue {
   const void* emb;  // T [V, H] dequantised embedding
   int H;
   void* x;  // T [S, H]: the prediction network's next input
+  // When set, the emitted token id goes here instead of its embedding row
+  // into x (layer 0 then reads its ih product from a per-token table).
+  int* last_token;  // [S] or nullptr
   int* tokens;
   int* token_frames;
   int* counts;

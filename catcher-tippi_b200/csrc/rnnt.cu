@@ -257,6 +257,28 @@ void RnntDecoder::finalize() {
       check_cuda(cudaMemcpy(t.get(), bi.data(), bi.size() * 2, cudaMemcpyHostToDevice), "gate bias");
       gate_bias_il_.push_back(std::move(t));
     }
+    // layer 0's ih product of every embedding row, by the step kernel's own
+    // arithmetic (the W_hh half of the launch multiplies the same rows and is
+    // discarded)
+    ih0_table_ = DeviceBuffer(static_cast<size_t>(V) * 4 * H * 2);
+    cq::LstmMaps maps;
+    maps.m[0] = ih_il_[0]->gemv_map(4);
+    maps.m[1] = hh_il_[0]->gemv_map(4);
+    cq::LstmStepArgs a{};
+    a.x = embedding_.get();
+    a.h_prev = embedding_.get();
+    a.scales_ih = ih_il_[0]->scales();
+    a.biases_ih = ih_il_[0]->biases();
+    a.scales_hh = hh_il_[0]->scales();
+    a.biases_hh = hh_il_[0]->biases();
+    a.gate_bias = gate_bias_il_[0].get();
+    a.all = 1;
+    a.status = device_context(device_).status;
+    a.S = V;
+    a.H = H;
+    a.gi_out = ih0_table_.get();
+    const int dt = dtype_ == CQ_BF16 ? cq::kBF16 : cq::kF16;
+    check_cuda(cq::launch_lstm_step(dt, g, maps, a, nullptr, false), "layer-0 ih table");
   }
   check_cuda(cudaDeviceSynchronize(), "finalize RNNT");
   finalized_ = true;
@@ -295,6 +317,8 @@ RnntState::RnntState(RnntDecoder& dec, int streams, int max_frames)
     done_ = DeviceBuffer(static_cast<size_t>((S_ + 15) / 16) * sizeof(unsigned));
     check_cuda(cudaMemset(best_.get(), 0, best_.bytes()), "greedy keys");
     check_cuda(cudaMemset(done_.get(), 0, done_.bytes()), "greedy counter");
+    ih0_from_table_ = dec_.ih0_table() != nullptr;
+    if (ih0_from_table_) last_token_ = DeviceBuffer(S * sizeof(int));
   }
   size_t need = dec_.enc_proj()->scratch_bytes_for(S_ * max_frames);
   for (const QuantizedLinear* L : {dec_.head(), dec_.dec_proj()}) need = std::max(need, L->scratch_bytes_for(S_));
@@ -364,6 +388,10 @@ void RnntState::prediction_step(bool all, cudaStream_t st, const cq::RnntEpilogu
       a.status = device_context(dec_.device()).status;
       a.S = S_;
       a.H = H;
+      if (l == 0 && ih0_from_table_) {
+        a.gi_table = dec_.ih0_table();
+        a.gi_token = last_token_.as<int>();
+      }
       check_cuda(cq::launch_lstm_step(dt, g, maps, a, st, pdl), "lstm step");
       hpar_[l] ^= 1;
       in = h_cur(l);
@@ -416,6 +444,11 @@ void RnntState::reset() {
   // the first PredictionNetwork::step(blank) of every stream
   check_cuda(cq::launch_broadcast_row(dec_.embedding(), c.blank, c.pred_hidden, x_.get(), S_, nullptr),
              "blank embedding");
+  if (ih0_from_table_) {
+    const std::vector<int> blank(S_, c.blank);
+    check_cuda(cudaMemcpy(last_token_.get(), blank.data(), blank.size() * sizeof(int), cudaMemcpyHostToDevice),
+               "blank token");
+  }
   std::fill(hpar_.begin(), hpar_.end(), 0);
   prediction_step(true, nullptr);
   normalize_h(nullptr);
@@ -505,6 +538,7 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
       e.emb = dec_.embedding();
       e.H = H;
       e.x = x_.get();
+      e.last_token = ih0_from_table_ ? last_token_.as<int>() : nullptr;
       e.tokens = tokens;
       e.token_frames = token_frames;
       e.counts = counts;

@@ -59,6 +59,9 @@ class RnntDecoder {
   const QuantizedLinear* ih_interleaved(int l) const { return ih_il_[l].get(); }
   const QuantizedLinear* hh_interleaved(int l) const { return hh_il_[l].get(); }
   const void* gate_bias_interleaved(int l) const { return gate_bias_il_[l].get(); }
+  // T(W_ih emb[v]) of layer 0 for every token v, gate-interleaved: T [vocab, 4 H]
+  // (nullptr when the one-launch LSTM step is off)
+  const void* ih0_table() const { return ih0_table_.get(); }
 
  private:
   const Spec& spec(const std::string& name, bool linear) const;
@@ -71,7 +74,7 @@ class RnntDecoder {
   std::map<std::string, size_t> index_;
   std::map<std::string, std::unique_ptr<QuantizedLinear>> linears_;
   std::map<std::string, DeviceBuffer> dense_;  // f32 copies of the LSTM biases
-  DeviceBuffer embedding_;
+  DeviceBuffer embedding_, ih0_table_;
   std::vector<DeviceBuffer> lstm_bias_;
   std::vector<std::unique_ptr<QuantizedLinear>> ih_il_, hh_il_;
   std::vector<DeviceBuffer> gate_bias_il_;
@@ -121,6 +124,10 @@ class RnntState {
   // epilogues (per-stream argmax keys and a CTA counter, zero between calls)
   bool fused_epi_ = false;
   DeviceBuffer best_, done_;
+  // layer 0 reads T(W_ih emb[token]) from the decoder's table: the token each
+  // stream feeds its prediction network next (the greedy epilogue writes it)
+  bool ih0_from_table_ = false;
+  DeviceBuffer last_token_;
   std::vector<DeviceBuffer> h_next_;
   std::vector<int> hpar_;
   // persistent path: second hidden-state buffer per layer, head partials, barrier

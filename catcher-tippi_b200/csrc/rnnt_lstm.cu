@@ -12,7 +12,10 @@
 // interleaved at load time (row 4j + q holds gate q of hidden unit j) so one
 // band holds all four gates of 16 hidden units.  The new hidden state goes to
 // a second buffer (other CTAs still read the old one); streams that are not
-// active keep their state (h copied across, c untouched).  Token tiles
+// active keep their state (h copied across, c untouched).  Layer 0 can take
+// its ih product from a per-token table instead (FORM 1: one CTA per band
+// multiplies W_hh h, the cell reads T(W_ih emb[token]) from the table made
+// once by this kernel's FORM 0 with gi_out set).  Token tiles
 // spread over grid.z; when all clusters fit one wave the kernel runs one CTA
 // per SM with the registers that allows, else two per SM (a cluster walks
 // several token tiles only past the grid limit, at one CTA per SM).
@@ -61,12 +64,32 @@ __device__ __forceinline__ float sigmoid_t(float x) {
   return round_t<DT>(1.0f / (1.0f + expf(-x)));
 }
 
-template <int DT, int G, int MINB>
+// Loads issued where they stand (asm volatile keeps the compiler from
+// sinking them to their use).
+__device__ __forceinline__ int ld_volatile_s32(const int* p) {
+  int v;
+  asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint2 ld_volatile_v2u32(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+template <int DT>
+__device__ __forceinline__ float widen_t(uint32_t bits16) {
+  if constexpr (DT == kBF16) return __uint_as_float(bits16 << 16);
+  else return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+
+template <int DT, int G, int MINB, int FORM>
 __global__ void __launch_bounds__(kThreads, MINB)
     lstm_step_kernel(const __grid_constant__ LstmMaps maps, const LstmStepArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int rank = blockIdx.x;  // 0: W_ih x, 1: W_hh h
+  // the product this CTA computes -- 0: W_ih x, 1: W_hh h (FORM 1: only that)
+  const int rank = FORM == 1 ? 1 : static_cast<int>(blockIdx.x);
   const int n0 = blockIdx.y * kRB;
   const int H = a.H, K = a.H, N = 4 * a.H;
   const int sbn = (K + 63) >> 6;
@@ -115,9 +138,21 @@ __global__ void __launch_bounds__(kThreads, MINB)
 
   bool ok = true;
   auto tile = [&](const int mt, const int round) {
+    // FORM 1: this thread's four table gates (unit n0/4 + tid/16, stream
+    // mt*16 + tid%16), fetched before the product so the lookup (token id,
+    // then row) overlaps the MMAs
+    uint2 gi_bits = make_uint2(0u, 0u);
+    if constexpr (FORM == 1) {
+      const int s = mt * 16 + (tid & 15);
+      if (s < a.S && n0 / 4 + (tid >> 4) < H) {
+        const int tok = ld_volatile_s32(a.gi_token + s);
+        gi_bits = ld_volatile_v2u32(static_cast<const uint16_t*>(a.gi_table) + static_cast<size_t>(tok) * N +
+                                    n0 + 4 * (tid >> 4));
+      }
+    }
     // ---- activations of this token tile, all loads in flight at once
     uint4 xr[kSbPerWarp][2][2];
-    #pragma unroll
+#pragma unroll
     for (int u = 0; u < kSbPerWarp; ++u) {
       const int j = warp + u * kNW;
       if (j < sbn) {
@@ -126,13 +161,13 @@ __global__ void __launch_bounds__(kThreads, MINB)
       }
     }
     float acc[kRT][2][4];
-    #pragma unroll
+#pragma unroll
     for (int i = 0; i < kRT; ++i)
-      #pragma unroll
+#pragma unroll
       for (int nt = 0; nt < 2; ++nt)
-        #pragma unroll
+#pragma unroll
         for (int e = 0; e < 4; ++e) acc[i][nt][e] = 0.f;
-    #pragma unroll
+#pragma unroll
     for (int u = 0; u < kSbPerWarp; ++u) {
       const int j = warp + u * kNW;
       if (j >= sbn) break;
@@ -141,10 +176,10 @@ __global__ void __launch_bounds__(kThreads, MINB)
       subblock_mma<DT, G, kRT>(wt + static_cast<size_t>(j) * kRB * 64,
                                sbsm + static_cast<size_t>(j) * SUBG * kRB, xo, lane, acc);
     }
-    #pragma unroll
+#pragma unroll
     for (int i = 0; i < kRT; ++i) {
       const int ra = 16 * i + r4, rb = ra + 8;
-      #pragma unroll
+#pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         *reinterpret_cast<float2*>(&red[(warp * kRB + ra) * 16 + 8 * nt + 2 * c]) =
             make_float2(acc[i][nt][0], acc[i][nt][1]);
@@ -158,31 +193,58 @@ __global__ void __launch_bounds__(kThreads, MINB)
     // preceded by this tile's cluster barrier, which rank 0 passes only
     // after it read the buffer before -- one barrier per tile suffices
     float* fbuf = fin + (round & 1) * 2 * kRB * 16;
-    const uint32_t slot = mapa_shared(smem_u32(fbuf), 0) +
-                          static_cast<uint32_t>(rank * kRB * 16 * sizeof(float));
-    for (int e = tid; e < kRB * 16; e += kThreads) {
-      float v = 0.f;
-      #pragma unroll
-      for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
-      st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
+    if constexpr (FORM == 1) {
+      for (int e = tid; e < kRB * 16; e += kThreads) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
+        fbuf[kRB * 16 + e] = v;
+      }
+      __syncthreads();
+    } else {
+      const uint32_t slot = mapa_shared(smem_u32(fbuf), 0) +
+                            static_cast<uint32_t>(rank * kRB * 16 * sizeof(float));
+      for (int e = tid; e < kRB * 16; e += kThreads) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
+        st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
+      }
+      cluster_sync_all();
     }
-    cluster_sync_all();
 
-    if (rank == 0) {
+    if (rank == 0 || FORM == 1) {
       // one (hidden unit, token) per thread: 16 units x 16 tokens
       const int u = tid >> 4, t = tid & 15;
       const int s = mt * 16 + t;
       const int j = n0 / 4 + u;
-      if (s < a.S && j < H) {
+      if (FORM == 0 && a.gi_out != nullptr) {
+        // table row: the rounded ih product of the band's 4 gates x 16 units
+        if (s < a.S && j < H)
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            st_t<DT>(a.gi_out, static_cast<size_t>(s) * N + n0 + 4 * u + q,
+                     round_t<DT>(fbuf[(4 * u + q) * 16 + t]));
+      } else if (s < a.S && j < H) {
         const size_t hj = static_cast<size_t>(s) * H + j;
         if (a.all || a.active[s]) {
+          float gi[4];
+          if constexpr (FORM == 1) {
+            // the four gates of unit j are adjacent in the interleaved row
+            gi[0] = widen_t<DT>(gi_bits.x & 0xFFFFu);
+            gi[1] = widen_t<DT>(gi_bits.x >> 16);
+            gi[2] = widen_t<DT>(gi_bits.y & 0xFFFFu);
+            gi[3] = widen_t<DT>(gi_bits.y >> 16);
+          } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) gi[q] = round_t<DT>(fbuf[(4 * u + q) * 16 + t]);
+          }
           float gate[4];
-          #pragma unroll
+#pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int row = 4 * u + q;
-            const float gi = round_t<DT>(fbuf[row * 16 + t]);
             const float gh = round_t<DT>(fbuf[kRB * 16 + row * 16 + t]);
-            gate[q] = round_t<DT>(round_t<DT>(gi + gh) + ld_t<DT>(a.gate_bias, n0 + row));
+            gate[q] = round_t<DT>(round_t<DT>(gi[q] + gh) + ld_t<DT>(a.gate_bias, n0 + row));
           }
           const float ig = sigmoid_t<DT>(gate[0]);
           const float fg = sigmoid_t<DT>(gate[1]);
@@ -209,18 +271,29 @@ __global__ void __launch_bounds__(kThreads, MINB)
     for (int j = 0; j < sbn; ++j) mbar_wait_bounded(&bars[j], 0, a.status);
 }
 
-// Clusters of a launch configuration resident at once (cached per kernel).
-int resident_clusters(const void* kern, cudaLaunchConfig_t cfg, int* cache) {
+// Launch units (clusters of `cluster` CTAs) of a configuration resident at
+// once, cached per kernel; the kernel's smem attribute must be set already.
+int resident_units(const void* kern, cudaLaunchConfig_t cfg, int cluster, int* cache) {
   if (*cache > 0) return *cache;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeClusterDimension;
-  attr.val.clusterDim.x = 2;
-  attr.val.clusterDim.y = 1;
-  attr.val.clusterDim.z = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+  if (cluster > 1) {
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = cluster;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) n = 0;
+  } else {
+    int per_sm = 0, dev = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, static_cast<int>(cfg.blockDim.x),
+                                                      cfg.dynamicSmemBytes) == cudaSuccess &&
+        cudaGetDevice(&dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+      n = per_sm * sms;
+  }
+  if (n < 1) {
     (void)cudaGetLastError();
     n = 1;
   }
@@ -228,48 +301,44 @@ int resident_clusters(const void* kern, cudaLaunchConfig_t cfg, int* cache) {
   return n;
 }
 
-template <int DT, int G, int MINB>
-cudaError_t launch_cfg(const LstmMaps& maps, const LstmStepArgs& a, cudaLaunchConfig_t cfg) {
-  auto kern = lstm_step_kernel<DT, G, MINB>;
+template <int DT, int G, int MINB, int FORM>
+cudaError_t set_smem(size_t bytes) {
   static int configured = 0;
-  if (static_cast<int>(cfg.dynamicSmemBytes) > configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(cfg.dynamicSmemBytes));
-    if (e != cudaSuccess) return e;
-    configured = static_cast<int>(cfg.dynamicSmemBytes);
-  }
-  return cudaLaunchKernelEx(&cfg, kern, maps, a);
+  if (static_cast<int>(bytes) <= configured) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(lstm_step_kernel<DT, G, MINB, FORM>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) configured = static_cast<int>(bytes);
+  return e;
 }
 
-template <int DT, int G>
-cudaError_t launch_g(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream, bool pdl) {
+template <int DT, int G, int FORM>
+cudaError_t launch_form(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream, bool pdl) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
+  constexpr int kCluster = FORM == 1 ? 1 : 2;
   const LstmSmem L = lstm_smem_layout((a.H + 63) / 64, SUBG);
   const int bands = (4 * a.H + kRB - 1) / kRB;
   const int mtiles = (a.S + 15) / 16;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2, bands, std::min(mtiles, 65535));
+  cfg.gridDim = dim3(kCluster, bands, std::min(mtiles, 65535));
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
-  // one wave at one CTA per SM?  (needs the smem attribute set first)
+  // one wave at one CTA per SM?
+  cudaError_t e = set_smem<DT, G, 1, FORM>(L.total);
+  if (e != cudaSuccess) return e;
   static int res1 = 0;
-  if (res1 == 0) {
-    cudaError_t e = cudaFuncSetAttribute(lstm_step_kernel<DT, G, 1>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(L.total));
-    if (e != cudaSuccess) return e;
-  }
   const bool one_wave =
-      bands * mtiles <= resident_clusters(reinterpret_cast<const void*>(lstm_step_kernel<DT, G, 1>),
-                                          cfg, &res1);
+      bands * mtiles <=
+      resident_units(reinterpret_cast<const void*>(lstm_step_kernel<DT, G, 1, FORM>), cfg, kCluster, &res1);
   cudaLaunchAttribute attrs[2];
   int na = 0;
-  attrs[na].id = cudaLaunchAttributeClusterDimension;
-  attrs[na].val.clusterDim.x = 2;
-  attrs[na].val.clusterDim.y = 1;
-  attrs[na].val.clusterDim.z = 1;
-  ++na;
+  if (kCluster > 1) {
+    attrs[na].id = cudaLaunchAttributeClusterDimension;
+    attrs[na].val.clusterDim.x = kCluster;
+    attrs[na].val.clusterDim.y = 1;
+    attrs[na].val.clusterDim.z = 1;
+    ++na;
+  }
   if (pdl) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
@@ -277,8 +346,19 @@ cudaError_t launch_g(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t s
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  return one_wave || mtiles > 65535 ? launch_cfg<DT, G, 1>(maps, a, cfg)
-                                    : launch_cfg<DT, G, 2>(maps, a, cfg);
+  if (one_wave || mtiles > 65535) return cudaLaunchKernelEx(&cfg, lstm_step_kernel<DT, G, 1, FORM>, maps, a);
+  e = set_smem<DT, G, 2, FORM>(L.total);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, lstm_step_kernel<DT, G, 2, FORM>, maps, a);
+}
+
+template <int DT, int G>
+cudaError_t launch_g(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream, bool pdl) {
+  if (a.gi_table != nullptr) {
+    if (a.gi_token == nullptr || a.gi_out != nullptr) return cudaErrorInvalidValue;
+    return launch_form<DT, G, 1>(maps, a, stream, pdl);
+  }
+  return launch_form<DT, G, 0>(maps, a, stream, pdl);
 }
 
 template <int DT>

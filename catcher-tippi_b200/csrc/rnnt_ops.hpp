@@ -92,6 +92,15 @@ struct LstmStepArgs {
   int all;                // update every stream
   int* status;
   int S, H;
+  // Layer 0's input is always an embedding row, so its ih product is a
+  // function of the token: with gi_table set, a launch reads
+  // gi_table[gi_token[s]] (T [V, 4H], interleaved) instead of multiplying,
+  // one CTA per band and no cluster.  With gi_out set, a launch only writes
+  // T(W_ih x) (T [S, 4H], interleaved) -- how the table is made, by the same
+  // arithmetic -- and leaves the state alone.
+  const void* gi_table;
+  const int* gi_token;  // [S]
+  void* gi_out;
 };
 bool lstm_step_fits(int H, int group);
 cudaError_t launch_lstm_step(int dtype, int group, const LstmMaps& maps, const LstmStepArgs& a,
