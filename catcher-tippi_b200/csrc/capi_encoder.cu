@@ -166,6 +166,13 @@ int32_t cq_encoder_state_kernels_per_chunk(const cq_encoder_state* st) {
   return st ? st->impl->launches_per_chunk() : -1;
 }
 
+cq_status cq_encoder_state_set_pdl(cq_encoder_state* st, int32_t enable) {
+  return guarded([&] {
+    need_handle(st, "state");
+    st->impl->set_pdl(enable != 0);
+  });
+}
+
 cq_status cq_encoder_state_reset(cq_encoder_state* st) {
   return guarded([&] {
     need_handle(st, "state");

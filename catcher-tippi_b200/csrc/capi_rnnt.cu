@@ -152,6 +152,13 @@ cq_status cq_rnnt_state_set_persistent(cq_rnnt_state* st, int32_t enable) {
   });
 }
 
+cq_status cq_rnnt_state_set_pdl(cq_rnnt_state* st, int32_t enable) {
+  return guarded([&] {
+    need_handle(st, "state");
+    st->impl->set_pdl(enable != 0);
+  });
+}
+
 int32_t cq_rnnt_state_kernels_per_chunk(const cq_rnnt_state* st) {
   return st ? st->impl->launches_per_chunk() : -1;
 }

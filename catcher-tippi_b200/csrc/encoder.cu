@@ -17,14 +17,6 @@ namespace nemotron_cuda {
 
 namespace {
 
-bool pdl_on() {
-  static const bool on = [] {
-    const char* e = std::getenv("CQ_PDL");
-    return e == nullptr || std::strcmp(e, "0") != 0;
-  }();
-  return on;
-}
-
 bool graphs_on() {
   static const bool on = [] {
     const char* e = std::getenv("CQ_ENCODER_GRAPH");
@@ -452,6 +444,15 @@ EncoderState::~EncoderState() {
   if (capture_stream_ != nullptr) cudaStreamDestroy(capture_stream_);
 }
 
+void EncoderState::set_pdl(bool on) {
+  if (on == pdl_) return;
+  DeviceGuard guard(enc_.device());
+  check_cuda(cudaDeviceSynchronize(), "switch PDL");
+  for (auto& g : graphs_) cudaGraphExecDestroy(g.exec);
+  graphs_.clear();
+  pdl_ = on;
+}
+
 void EncoderState::reset() {
   DeviceGuard guard(enc_.device());
   check_cuda(cudaDeviceSynchronize(), "reset");
@@ -488,7 +489,8 @@ void EncoderState::linear(QuantizedLinear* L, const void* x, int ldx, int rows, 
 void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, cudaStream_t st) {
   const auto& c = enc_.config();
   const int dt = enc_.dtype() == CQ_BF16 ? cq::kBF16 : cq::kF16;
-  const bool pdl = pdl_on();
+  const bool pdl = pdl_;
+  PdlScope pdl_scope(pdl_);  // the linears follow the state's setting
   const int S = S_, D = c.hidden, C = c.sub_channels, Q = g.T3, rows = S * Q;
   const int P = c.num_prompts;
   int* ctr = counters_.as<int>();

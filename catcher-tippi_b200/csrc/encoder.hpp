@@ -89,6 +89,10 @@ class EncoderState {
   int output_frames(int mel_frames) const;
   void encode_chunk(const float* mel, int mel_frames, void* out, cudaStream_t stream);
   void reset();
+  // Programmatic dependent launch between this state's kernels (default: on
+  // unless CQ_PDL=0).  Changing it drops the captured chunk graphs.
+  void set_pdl(bool on);
+  bool pdl() const { return pdl_; }
   int chunks() const { return chunks_; }
   // Kernel launches of one chunk (the node count of the last captured chunk
   // graph, or the launches of the last eager chunk).
@@ -113,6 +117,7 @@ class EncoderState {
   int S_, max_mel_, qmax_, ring_, vmax_, pmax_;
   int chunks_ = 0;
   int launches_ = 0;
+  bool pdl_ = pdl_default();
   DeviceBuffer counters_, prompts_;
   DeviceBuffer res_, xn_, hid_, y_, att_, qkv_, pin_, relk_, pos_table_;
   // f16 copy + per-row scales of the LayerNorm / conv outputs that feed a

@@ -28,13 +28,24 @@ bool gemm_allowed() {
   return on;
 }
 
-bool pdl_enabled() {
+thread_local int t_pdl = -1;  // -1: the default
+
+}  // namespace
+
+bool pdl_default() {
   static const bool on = [] {
     const char* e = std::getenv("CQ_PDL");
     return e == nullptr || std::strcmp(e, "0") != 0;
   }();
   return on;
 }
+
+bool pdl_enabled() { return t_pdl >= 0 ? t_pdl != 0 : pdl_default(); }
+
+PdlScope::PdlScope(bool on) : prev_(t_pdl) { t_pdl = on ? 1 : 0; }
+PdlScope::~PdlScope() { t_pdl = prev_; }
+
+namespace {
 
 void validate_group(int group) {
   if (group != 32 && group != 64 && group != 128) {

@@ -59,6 +59,23 @@ class DeviceGuard {
 CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
                         int box_rows, int box_cols, CUtensorMapSwizzle swizzle);
 
+// Programmatic dependent launch (PDL) on this thread's kernel launches: on
+// unless CQ_PDL=0, or as the innermost live PdlScope says.  Encoder and RNNT
+// states set it per chunk (streams that overlap on one GPU can run faster
+// without it: CTAs launched early wait on the GPU holding their SM's room).
+bool pdl_default();
+bool pdl_enabled();
+class PdlScope {
+ public:
+  explicit PdlScope(bool on);
+  ~PdlScope();
+  PdlScope(const PdlScope&) = delete;
+  PdlScope& operator=(const PdlScope&) = delete;
+
+ private:
+  int prev_;
+};
+
 class QuantizedLinear {
  public:
   // Packed arrays in host memory -> owned device copy (from_artifact).

@@ -17,14 +17,6 @@ namespace nemotron_cuda {
 
 namespace {
 
-bool pdl_on() {
-  static const bool on = [] {
-    const char* e = std::getenv("CQ_PDL");
-    return e == nullptr || std::strcmp(e, "0") != 0;
-  }();
-  return on;
-}
-
 bool graphs_on() {
   static const bool on = [] {
     const char* e = std::getenv("CQ_RNNT_GRAPH");
@@ -362,7 +354,8 @@ void RnntState::linear(QuantizedLinear* L, const void* x, int ldx, int rows, voi
 void RnntState::prediction_step(bool all, cudaStream_t st, const cq::RnntEpilogue* proj_epi) {
   const auto& c = dec_.config();
   const int dt = dec_.dtype() == CQ_BF16 ? cq::kBF16 : cq::kF16;
-  const bool pdl = pdl_on();
+  const bool pdl = pdl_;
+  PdlScope pdl_scope(pdl_);  // the linears follow the state's setting
   const int H = c.pred_hidden;
   if (lstm_fused_) {
     const void* in = x_.get();
@@ -461,7 +454,8 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
                              int* counts, cudaStream_t st) {
   const auto& c = dec_.config();
   const int dt = dec_.dtype() == CQ_BF16 ? cq::kBF16 : cq::kF16;
-  const bool pdl = pdl_on();
+  const bool pdl = pdl_;
+  PdlScope pdl_scope(pdl_);  // the linears follow the state's setting
   const int J = c.joint_hidden, V = c.vocab, H = c.pred_hidden;
   const int cap = capacity();
   if (use_persistent_) {
@@ -560,6 +554,15 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
     }
   }
   normalize_h(st);  // the chunk ends with the state in h_, whatever its step count
+}
+
+void RnntState::set_pdl(bool on) {
+  if (on == pdl_) return;
+  DeviceGuard guard(dec_.device());
+  check_cuda(cudaDeviceSynchronize(), "switch PDL");
+  for (auto& g : graphs_) cudaGraphExecDestroy(g.exec);
+  graphs_.clear();
+  pdl_ = on;
 }
 
 void RnntState::set_persistent(bool on) {

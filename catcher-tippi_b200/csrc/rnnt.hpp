@@ -97,6 +97,10 @@ class RnntState {
   // launch per op (false, the default).  Throws if the persistent kernel does
   // not fit this state's shapes.
   void set_persistent(bool on);
+  // Programmatic dependent launch between this state's kernels (default: on
+  // unless CQ_PDL=0).  Changing it drops the captured chunk graphs.
+  void set_pdl(bool on);
+  bool pdl() const { return pdl_; }
   bool persistent() const { return use_persistent_; }
 
  private:
@@ -117,6 +121,7 @@ class RnntState {
   RnntDecoder& dec_;
   int S_, max_frames_;
   int launches_ = 0;
+  bool pdl_ = pdl_default();
   DeviceBuffer ep_, dec_out_, dec_new_, fused_, logits_, x_, gi_, gh_, active_;
   std::vector<DeviceBuffer> h_, c_;
   bool lstm_fused_ = false;

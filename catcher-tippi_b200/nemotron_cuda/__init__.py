@@ -82,6 +82,7 @@ def lib() -> ctypes.CDLL:
         "cq_encoder_state_chunks": ([vp], i32),
         "cq_encoder_state_kernels_per_chunk": ([vp], i32),
         "cq_encoder_state_reset": ([vp], i32),
+        "cq_encoder_state_set_pdl": ([vp, i32], i32),
         "cq_encoder_state_destroy": ([vp], None),
         # batched RNNT decoder (include/cqrnnt.h)
         "cq_rnnt_default_config": ([vp], None),
@@ -99,6 +100,7 @@ def lib() -> ctypes.CDLL:
         "cq_rnnt_decode_chunk": ([vp, vp, i32, i32, vp, vp, vp, vp], i32),
         "cq_rnnt_state_kernels_per_chunk": ([vp], i32),
         "cq_rnnt_state_set_persistent": ([vp, i32], i32),
+        "cq_rnnt_state_set_pdl": ([vp, i32], i32),
         "cq_rnnt_state_reset": ([vp], i32),
         "cq_rnnt_state_destroy": ([vp], None),
         # persistent linear chains (include/cqchain.h)

@@ -160,6 +160,10 @@ class EncoderState:
     def reset(self) -> None:
         _check(lib().cq_encoder_state_reset(self._h))
 
+    def set_pdl(self, enable: bool = True) -> None:
+        """Programmatic dependent launch between this state's kernels."""
+        _check(lib().cq_encoder_state_set_pdl(self._h, int(enable)))
+
     def encode_chunk(self, mel, out=None, stream=None):
         """mel torch f32 [streams, frames, mel_bins] on the device -> out torch T
         [streams * encoder_frames, hidden]."""

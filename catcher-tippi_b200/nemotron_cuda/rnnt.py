@@ -139,6 +139,10 @@ class RnntState:
     def reset(self) -> None:
         _check(lib().cq_rnnt_state_reset(self._h))
 
+    def set_pdl(self, enable: bool = True) -> None:
+        """Programmatic dependent launch between this state's kernels."""
+        _check(lib().cq_rnnt_state_set_pdl(self._h, int(enable)))
+
     def decode_chunk_raw(self, encoded, frames: int, tokens, token_frames, counts, stream=None):
         """Device tensors in and out (no synchronisation)."""
         _check(lib().cq_rnnt_decode_chunk(self._h, _ptr(encoded), encoded.stride(0), frames,

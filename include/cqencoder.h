@@ -137,6 +137,13 @@ int32_t cq_encoder_state_kernels_per_chunk(const cq_encoder_state *st);
 /* Zeroes every cache (a new utterance on every stream). Synchronous. */
 cq_status cq_encoder_state_reset(cq_encoder_state *st);
 
+/* Programmatic dependent launch between the state's kernels: 1 (the default
+ * unless the environment sets CQ_PDL=0) or 0.  With another stream's work
+ * overlapping the encoder on the same GPU (an RNNT decoder pipelined beside
+ * it), 0 can be faster: kernels launched early hold SM room while they wait.
+ * Synchronous; drops the captured chunk graphs. */
+cq_status cq_encoder_state_set_pdl(cq_encoder_state *st, int32_t enable);
+
 void cq_encoder_state_destroy(cq_encoder_state *st);
 
 #ifdef __cplusplus

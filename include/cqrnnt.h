@@ -105,6 +105,11 @@ cq_status cq_rnnt_decode_chunk(cq_rnnt_state *st, const void *encoded, int32_t l
  */
 cq_status cq_rnnt_state_set_persistent(cq_rnnt_state *st, int32_t enable);
 
+/* Programmatic dependent launch between the state's kernels: 1 (the default
+ * unless the environment sets CQ_PDL=0) or 0 (see cq_encoder_state_set_pdl).
+ * Synchronous; drops the captured chunk graphs. */
+cq_status cq_rnnt_state_set_pdl(cq_rnnt_state *st, int32_t enable);
+
 /* Kernels one chunk launches (nodes of the captured graph; 0 before capture). */
 int32_t cq_rnnt_state_kernels_per_chunk(const cq_rnnt_state *st);
 
