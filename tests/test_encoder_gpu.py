@@ -131,6 +131,13 @@ def test_streams_are_independent_and_reset_restarts(cq, oracle_mod):
     torch.cuda.synchronize()
     for a, b in zip(again, outs1):
         assert torch.equal(a, b)
+    # without programmatic dependent launch: the same bits
+    st1.set_pdl(False)
+    st1.reset()
+    no_pdl = [st1.encode_chunk(m[1:2].contiguous()).clone() for m in mels]
+    torch.cuda.synchronize()
+    for a, b in zip(no_pdl, outs1):
+        assert torch.equal(a, b)
 
 
 def test_prompt_changes_only_through_the_projector(cq, oracle_mod):

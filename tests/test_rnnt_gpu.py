@@ -156,6 +156,9 @@ def test_reset_replays_the_same_tokens(cq):
     state.reset()
     again = [state.decode_chunk(enc, 6) for _ in range(2)]
     assert first == again
+    state.set_pdl(False)  # without programmatic dependent launch
+    state.reset()
+    assert [state.decode_chunk(enc, 6) for _ in range(2)] == first
 
 
 def test_rnnt_binding_errors(cq):
