@@ -249,6 +249,11 @@ void RnntDecoder::finalize() {
       check_cuda(cudaMemcpy(t.get(), bi.data(), bi.size() * 2, cudaMemcpyHostToDevice), "gate bias");
       gate_bias_il_.push_back(std::move(t));
     }
+    lstm_m5_.clear();
+    if ((4 * H) % 80 == 0)
+      for (int l = 0; l < cfg_.lstm_layers; ++l)
+        for (const auto* w : {ih_il_[l].get(), hh_il_[l].get()})
+          lstm_m5_.push_back(make_map_2d(w->qweight(), 1, 4 * H, H, H, 80, 64, CU_TENSOR_MAP_SWIZZLE_NONE));
     // layer 0's ih product of every embedding row, by the step kernel's own
     // arithmetic (the W_hh half of the launch multiplies the same rows and is
     // discarded)
@@ -256,6 +261,7 @@ void RnntDecoder::finalize() {
     cq::LstmMaps maps;
     maps.m[0] = ih_il_[0]->gemv_map(4);
     maps.m[1] = hh_il_[0]->gemv_map(4);
+    maps.has_m5 = 0;
     cq::LstmStepArgs a{};
     a.x = embedding_.get();
     a.h_prev = embedding_.get();
@@ -366,6 +372,11 @@ void RnntState::prediction_step(bool all, cudaStream_t st, const cq::RnntEpilogu
       cq::LstmMaps maps;
       maps.m[0] = wi->gemv_map(4);
       maps.m[1] = wh->gemv_map(4);
+      maps.has_m5 = dec_.has_lstm_m5() ? 1 : 0;
+      if (maps.has_m5) {
+        maps.m5[0] = dec_.lstm_m5(l, 0);
+        maps.m5[1] = dec_.lstm_m5(l, 1);
+      }
       cq::LstmStepArgs a{};
       a.x = in;
       a.h_prev = h_cur(l);

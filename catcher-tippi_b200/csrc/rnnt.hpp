@@ -62,6 +62,9 @@ class RnntDecoder {
   // T(W_ih emb[v]) of layer 0 for every token v, gate-interleaved: T [vocab, 4 H]
   // (nullptr when the one-launch LSTM step is off)
   const void* ih0_table() const { return ih0_table_.get(); }
+  // interleaved W_ih / W_hh of layer l with 80-row TMA boxes (has_lstm_m5())
+  bool has_lstm_m5() const { return !lstm_m5_.empty(); }
+  const CUtensorMap& lstm_m5(int l, int which) const { return lstm_m5_[2 * l + which]; }
 
  private:
   const Spec& spec(const std::string& name, bool linear) const;
@@ -75,6 +78,7 @@ class RnntDecoder {
   std::map<std::string, std::unique_ptr<QuantizedLinear>> linears_;
   std::map<std::string, DeviceBuffer> dense_;  // f32 copies of the LSTM biases
   DeviceBuffer embedding_, ih0_table_;
+  std::vector<CUtensorMap> lstm_m5_;
   std::vector<DeviceBuffer> lstm_bias_;
   std::vector<std::unique_ptr<QuantizedLinear>> ih_il_, hh_il_;
   std::vector<DeviceBuffer> gate_bias_il_;

@@ -27,8 +27,8 @@ namespace cq {
 
 namespace {
 
-constexpr int kRT = 4;
-constexpr int kRB = 16 * kRT;  // 64 interleaved gate rows = 16 hidden units
+// A band is 16 * RT interleaved gate rows = 4 * RT hidden units: RT 4 (64
+// rows), or 5 (80 rows) where that keeps a launch within one wave.
 constexpr int kNW = 8;
 constexpr int kThreads = kNW * 32;
 constexpr int kMaxSb = 16;  // K = hidden <= 1024
@@ -38,19 +38,20 @@ struct LstmSmem {
   size_t wt, bars, sbsm, red, fin, total;
 };
 
-__host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg) {
+// rb rows per band; fin_bufs 2 where a CTA walks several token tiles.
+__host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg, int rb, int fin_bufs) {
   LstmSmem L{};
   size_t off = 0;
-  L.wt = off;  // [sbn][64][64] u8, TMA destination
-  off += static_cast<size_t>(sbn) * kRB * 64;
+  L.wt = off;  // [sbn][rb][64] u8, TMA destination
+  off += static_cast<size_t>(sbn) * rb * 64;
   L.bars = off;
   off += kMaxSb * 8;
-  L.sbsm = off;  // [sbn * subg][64] (s, b - 1024 s)
-  off += static_cast<size_t>(sbn) * subg * kRB * sizeof(float2);
-  L.red = off;  // [8][64][16] per-warp partials
-  off += static_cast<size_t>(kNW) * kRB * 16 * sizeof(float);
-  L.fin = off;  // [2 tiles in flight][2 products][64][16] of rank 0's band
-  off += 4ull * kRB * 16 * sizeof(float);
+  L.sbsm = off;  // [sbn * subg][rb] (s, b - 1024 s)
+  off += static_cast<size_t>(sbn) * subg * rb * sizeof(float2);
+  L.red = off;  // [8][rb][16] per-warp partials
+  off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
+  L.fin = off;  // [fin_bufs tiles in flight][2 products][rb][16] of rank 0's band
+  off += static_cast<size_t>(fin_bufs) * 2 * rb * 16 * sizeof(float);
   L.total = off;
   return L;
 }
@@ -83,10 +84,14 @@ __device__ __forceinline__ float widen_t(uint32_t bits16) {
   else return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
 }
 
-template <int DT, int G, int MINB, int FORM>
+template <int DT, int G, int RT, int MINB, int FORM>
 __global__ void __launch_bounds__(kThreads, MINB)
     lstm_step_kernel(const __grid_constant__ LstmMaps maps, const LstmStepArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
+  constexpr int kRB = 16 * RT;
+  constexpr int kUnits = kRB / 4;                                // hidden units per band
+  constexpr int kCellIters = (kUnits * 16 + kThreads - 1) / kThreads;  // (unit, token) pairs
+  constexpr int kFinBufs = MINB == 1 ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   // the product this CTA computes -- 0: W_ih x, 1: W_hh h (FORM 1: only that)
   const int rank = FORM == 1 ? 1 : static_cast<int>(blockIdx.x);
@@ -94,13 +99,13 @@ __global__ void __launch_bounds__(kThreads, MINB)
   const int H = a.H, K = a.H, N = 4 * a.H;
   const int sbn = (K + 63) >> 6;
   const int groups_per_row = K / G;
-  const LstmSmem L = lstm_smem_layout(sbn, SUBG);
+  const LstmSmem L = lstm_smem_layout(sbn, SUBG, kRB, kFinBufs);
   uint8_t* wt = smem + L.wt;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
   float2* sbsm = reinterpret_cast<float2*>(smem + L.sbsm);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* fin = reinterpret_cast<float*>(smem + L.fin);
-  const CUtensorMap* wmap = &maps.m[rank];
+  const CUtensorMap* wmap = RT == 4 ? &maps.m[rank] : &maps.m5[rank];
   const void* scales = rank == 0 ? a.scales_ih : a.scales_hh;
   const void* biases = rank == 0 ? a.biases_ih : a.biases_hh;
   const void* x = rank == 0 ? a.x : a.h_prev;
@@ -138,16 +143,21 @@ __global__ void __launch_bounds__(kThreads, MINB)
 
   bool ok = true;
   auto tile = [&](const int mt, const int round) {
-    // FORM 1: this thread's four table gates (unit n0/4 + tid/16, stream
-    // mt*16 + tid%16), fetched before the product so the lookup (token id,
+    // FORM 1: this thread's table gates (pair p = unit p/16, stream
+    // mt*16 + p%16), fetched before the product so the lookup (token id,
     // then row) overlaps the MMAs
-    uint2 gi_bits = make_uint2(0u, 0u);
-    if constexpr (FORM == 1) {
-      const int s = mt * 16 + (tid & 15);
-      if (s < a.S && n0 / 4 + (tid >> 4) < H) {
-        const int tok = ld_volatile_s32(a.gi_token + s);
-        gi_bits = ld_volatile_v2u32(static_cast<const uint16_t*>(a.gi_table) + static_cast<size_t>(tok) * N +
-                                    n0 + 4 * (tid >> 4));
+    uint2 gi_bits[kCellIters];
+#pragma unroll
+    for (int it = 0; it < kCellIters; ++it) {
+      gi_bits[it] = make_uint2(0u, 0u);
+      const int p = tid + it * kThreads;
+      if constexpr (FORM == 1) {
+        const int s = mt * 16 + (p & 15);
+        if (p < kUnits * 16 && s < a.S && n0 / 4 + (p >> 4) < H) {
+          const int tok = ld_volatile_s32(a.gi_token + s);
+          gi_bits[it] = ld_volatile_v2u32(static_cast<const uint16_t*>(a.gi_table) +
+                                          static_cast<size_t>(tok) * N + n0 + 4 * (p >> 4));
+        }
       }
     }
     // ---- activations of this token tile, all loads in flight at once
@@ -160,9 +170,9 @@ __global__ void __launch_bounds__(kThreads, MINB)
         load_x_raw<G>(x, H, a.S, K, mt * 16 + 8 + r4, j * 64, c, xr[u][1][0], xr[u][1][1]);
       }
     }
-    float acc[kRT][2][4];
+    float acc[RT][2][4];
 #pragma unroll
-    for (int i = 0; i < kRT; ++i)
+    for (int i = 0; i < RT; ++i)
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -173,11 +183,11 @@ __global__ void __launch_bounds__(kThreads, MINB)
       if (j >= sbn) break;
       const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
       ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
-      subblock_mma<DT, G, kRT>(wt + static_cast<size_t>(j) * kRB * 64,
+      subblock_mma<DT, G, RT>(wt + static_cast<size_t>(j) * kRB * 64,
                                sbsm + static_cast<size_t>(j) * SUBG * kRB, xo, lane, acc);
     }
 #pragma unroll
-    for (int i = 0; i < kRT; ++i) {
+    for (int i = 0; i < RT; ++i) {
       const int ra = 16 * i + r4, rb = ra + 8;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
     // fin alternates between two buffers: a CTA's push for the next tile is
     // preceded by this tile's cluster barrier, which rank 0 passes only
     // after it read the buffer before -- one barrier per tile suffices
-    float* fbuf = fin + (round & 1) * 2 * kRB * 16;
+    float* fbuf = fin + (kFinBufs == 2 ? (round & 1) : 0) * 2 * kRB * 16;
     if constexpr (FORM == 1) {
       for (int e = tid; e < kRB * 16; e += kThreads) {
         float v = 0.f;
@@ -214,27 +224,31 @@ __global__ void __launch_bounds__(kThreads, MINB)
     }
 
     if (rank == 0 || FORM == 1) {
-      // one (hidden unit, token) per thread: 16 units x 16 tokens
-      const int u = tid >> 4, t = tid & 15;
-      const int s = mt * 16 + t;
-      const int j = n0 / 4 + u;
-      if (FORM == 0 && a.gi_out != nullptr) {
-        // table row: the rounded ih product of the band's 4 gates x 16 units
-        if (s < a.S && j < H)
+#pragma unroll
+      for (int it = 0; it < kCellIters; ++it) {
+        // one (hidden unit, token) pair per thread and pass
+        const int p = tid + it * kThreads;
+        const int u = p >> 4, t = p & 15;
+        const int s = mt * 16 + t;
+        const int j = n0 / 4 + u;
+        if (p >= kUnits * 16 || s >= a.S || j >= H) continue;
+        if (FORM == 0 && a.gi_out != nullptr) {
+          // table row: the rounded ih product of the unit's 4 gates
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             st_t<DT>(a.gi_out, static_cast<size_t>(s) * N + n0 + 4 * u + q,
                      round_t<DT>(fbuf[(4 * u + q) * 16 + t]));
-      } else if (s < a.S && j < H) {
+          continue;
+        }
         const size_t hj = static_cast<size_t>(s) * H + j;
         if (a.all || a.active[s]) {
           float gi[4];
           if constexpr (FORM == 1) {
             // the four gates of unit j are adjacent in the interleaved row
-            gi[0] = widen_t<DT>(gi_bits.x & 0xFFFFu);
-            gi[1] = widen_t<DT>(gi_bits.x >> 16);
-            gi[2] = widen_t<DT>(gi_bits.y & 0xFFFFu);
-            gi[3] = widen_t<DT>(gi_bits.y >> 16);
+            gi[0] = widen_t<DT>(gi_bits[it].x & 0xFFFFu);
+            gi[1] = widen_t<DT>(gi_bits[it].x >> 16);
+            gi[2] = widen_t<DT>(gi_bits[it].y & 0xFFFFu);
+            gi[3] = widen_t<DT>(gi_bits[it].y >> 16);
           } else {
 #pragma unroll
             for (int q = 0; q < 4; ++q) gi[q] = round_t<DT>(fbuf[(4 * u + q) * 16 + t]);
@@ -272,9 +286,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
 }
 
 // Launch units (clusters of `cluster` CTAs) of a configuration resident at
-// once, cached per kernel; the kernel's smem attribute must be set already.
-int resident_units(const void* kern, cudaLaunchConfig_t cfg, int cluster, int* cache) {
-  if (*cache > 0) return *cache;
+// once; the kernel's smem attribute must be set already.
+int resident_units(const void* kern, cudaLaunchConfig_t cfg, int cluster) {
   int n = 0;
   if (cluster > 1) {
     cudaLaunchAttribute attr;
@@ -297,39 +310,57 @@ int resident_units(const void* kern, cudaLaunchConfig_t cfg, int cluster, int* c
     (void)cudaGetLastError();
     n = 1;
   }
-  *cache = n;
   return n;
 }
 
-template <int DT, int G, int MINB, int FORM>
-cudaError_t set_smem(size_t bytes) {
-  static int configured = 0;
-  if (static_cast<int>(bytes) <= configured) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(lstm_step_kernel<DT, G, MINB, FORM>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
-  if (e == cudaSuccess) configured = static_cast<int>(bytes);
-  return e;
-}
+template <int DT, int G, int RT, int MINB, int FORM>
+struct Variant {
+  static constexpr int kCluster = FORM == 1 ? 1 : 2;
+  static size_t smem(int H) {
+    return lstm_smem_layout((H + 63) / 64, G == 32 ? 2 : 1, 16 * RT, MINB == 1 ? 2 : 1).total;
+  }
+  static cudaError_t prepare(size_t bytes) {
+    static int configured = 0;
+    if (static_cast<int>(bytes) <= configured) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(lstm_step_kernel<DT, G, RT, MINB, FORM>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+    if (e == cudaSuccess) configured = static_cast<int>(bytes);
+    return e;
+  }
+  // launch units (clusters or CTAs) resident at once; 0 if it cannot launch
+  static int resident(const cudaLaunchConfig_t& base, int H) {
+    static int cache = 0;
+    if (cache != 0) return std::max(cache, 0);
+    cudaLaunchConfig_t cfg = base;
+    cfg.dynamicSmemBytes = smem(H);
+    if (prepare(cfg.dynamicSmemBytes) != cudaSuccess) {
+      (void)cudaGetLastError();
+      cache = -1;
+      return 0;
+    }
+    cache = resident_units(reinterpret_cast<const void*>(lstm_step_kernel<DT, G, RT, MINB, FORM>), cfg,
+                           kCluster);
+    return cache;
+  }
+  static cudaError_t launch(cudaLaunchConfig_t cfg, const LstmMaps& maps, const LstmStepArgs& a) {
+    cfg.dynamicSmemBytes = smem(a.H);
+    cfg.gridDim.y = (4 * a.H) / (16 * RT);
+    cudaError_t e = prepare(cfg.dynamicSmemBytes);
+    if (e != cudaSuccess) return e;
+    return cudaLaunchKernelEx(&cfg, lstm_step_kernel<DT, G, RT, MINB, FORM>, maps, a);
+  }
+};
 
 template <int DT, int G, int FORM>
 cudaError_t launch_form(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_t stream, bool pdl) {
-  constexpr int SUBG = (G == 32) ? 2 : 1;
   constexpr int kCluster = FORM == 1 ? 1 : 2;
-  const LstmSmem L = lstm_smem_layout((a.H + 63) / 64, SUBG);
-  const int bands = (4 * a.H + kRB - 1) / kRB;
+  const int bands4 = (4 * a.H) / 64;
+  const int bands5 = maps.has_m5 && (4 * a.H) % 80 == 0 ? (4 * a.H) / 80 : 0;
   const int mtiles = (a.S + 15) / 16;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(kCluster, bands, std::min(mtiles, 65535));
+  cfg.gridDim = dim3(kCluster, bands4, std::min(mtiles, 65535));
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = L.total;
   cfg.stream = stream;
-  // one wave at one CTA per SM?
-  cudaError_t e = set_smem<DT, G, 1, FORM>(L.total);
-  if (e != cudaSuccess) return e;
-  static int res1 = 0;
-  const bool one_wave =
-      bands * mtiles <=
-      resident_units(reinterpret_cast<const void*>(lstm_step_kernel<DT, G, 1, FORM>), cfg, kCluster, &res1);
   cudaLaunchAttribute attrs[2];
   int na = 0;
   if (kCluster > 1) {
@@ -339,6 +370,7 @@ cudaError_t launch_form(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_
     attrs[na].val.clusterDim.z = 1;
     ++na;
   }
+  const int n_cluster_attrs = na;
   if (pdl) {
     attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attrs[na].val.programmaticStreamSerializationAllowed = 1;
@@ -346,10 +378,19 @@ cudaError_t launch_form(const LstmMaps& maps, const LstmStepArgs& a, cudaStream_
   }
   cfg.attrs = attrs;
   cfg.numAttrs = na;
-  if (one_wave || mtiles > 65535) return cudaLaunchKernelEx(&cfg, lstm_step_kernel<DT, G, 1, FORM>, maps, a);
-  e = set_smem<DT, G, 2, FORM>(L.total);
-  if (e != cudaSuccess) return e;
-  return cudaLaunchKernelEx(&cfg, lstm_step_kernel<DT, G, 2, FORM>, maps, a);
+  cudaLaunchConfig_t probe = cfg;  // occupancy queries see the cluster shape only
+  probe.numAttrs = n_cluster_attrs;
+  // One wave if possible: 64-row bands at one CTA per SM (most registers),
+  // then two per SM, then 80-row bands at two per SM.  Past that, two per SM
+  // in several waves (one CTA per SM walking tiles beyond the grid limit).
+  using V41 = Variant<DT, G, 4, 1, FORM>;
+  using V42 = Variant<DT, G, 4, 2, FORM>;
+  using V52 = Variant<DT, G, 5, 2, FORM>;
+  if (mtiles > 65535) return V41::launch(cfg, maps, a);
+  if (bands4 * mtiles <= V41::resident(probe, a.H)) return V41::launch(cfg, maps, a);
+  if (bands4 * mtiles <= V42::resident(probe, a.H)) return V42::launch(cfg, maps, a);
+  if (bands5 > 0 && bands5 * mtiles <= V52::resident(probe, a.H)) return V52::launch(cfg, maps, a);
+  return V42::launch(cfg, maps, a);
 }
 
 template <int DT, int G>

@@ -76,7 +76,9 @@ cudaError_t launch_rnnt_chunk(int dtype, const RnntChunkArgs& a, int grid, cudaS
 // hh products of a 64-row band of gate-interleaved weights (row 4j + q = gate
 // q of hidden unit j) on a two-CTA cluster, then the cell.
 struct LstmMaps {
-  CUtensorMap m[2];  // interleaved W_ih, W_hh: box 64 k x 64 rows
+  CUtensorMap m[2];   // interleaved W_ih, W_hh: box 64 k x 64 rows
+  CUtensorMap m5[2];  // the same with box 64 k x 80 rows (valid if has_m5)
+  int has_m5;
 };
 struct LstmStepArgs {
   const void* x;       // T [S, H]: the layer input
