@@ -320,7 +320,8 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
         if (n < a.N && m < a.M) {
           const float o = epilogue_value<DT>(v, has_bias, biasm[row], a.act);
           const size_t off = static_cast<size_t>(m) * a.ldy + n;
-          st_t<DT>(a.y, off, o);
+          // the greedy head keeps only the per-stream maximum
+          if (KIND != kKindEpilogue || a.mode != kGemvGreedy) st_t<DT>(a.y, off, o);
           if constexpr (KIND != kKindEpilogue) {
           } else if (a.mode == kGemvJointInput) {
             float d = o;
@@ -342,7 +343,8 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
         if (a.mode == kGemvGreedy) {
           if (tid < 16 && mt * 16 + tid < a.M && best_s[tid] != 0ull)
             atomicMax(&P.epi.best[mt * 16 + tid], best_s[tid]);
-          greedy_finish(P.epi, a.M, mt, gridDim.x * gridDim.y, reinterpret_cast<int*>(red), tid);
+          if (!P.epi.defer)
+            greedy_finish(P.epi, a.M, mt, gridDim.x * gridDim.y, reinterpret_cast<int*>(red), tid);
         }
       }
     } else {

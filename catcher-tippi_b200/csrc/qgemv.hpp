@@ -47,6 +47,9 @@ struct RnntEpilogue {
   // When set, the emitted token id goes here instead of its embedding row
   // into x (layer 0 then reads its ih product from a per-token table).
   int* last_token;  // [S] or nullptr
+  // Deferred: the head only folds its logits into `best`; the next LSTM step
+  // decodes the tokens and updates the flags (no arrival counter, no finish).
+  int defer;
   int* tokens;
   int* token_frames;
   int* counts;

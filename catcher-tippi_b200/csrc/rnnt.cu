@@ -317,6 +317,7 @@ RnntState::RnntState(RnntDecoder& dec, int streams, int max_frames)
     check_cuda(cudaMemset(done_.get(), 0, done_.bytes()), "greedy counter");
     ih0_from_table_ = dec_.ih0_table() != nullptr;
     if (ih0_from_table_) last_token_ = DeviceBuffer(S * sizeof(int));
+    defer_greedy_ = ih0_from_table_ && c.lstm_layers >= 2;
   }
   size_t need = dec_.enc_proj()->scratch_bytes_for(S_ * max_frames);
   for (const QuantizedLinear* L : {dec_.head(), dec_.dec_proj()}) need = std::max(need, L->scratch_bytes_for(S_));
@@ -395,6 +396,21 @@ void RnntState::prediction_step(bool all, cudaStream_t st, const cq::RnntEpilogu
       if (l == 0 && ih0_from_table_) {
         a.gi_table = dec_.ih0_table();
         a.gi_token = last_token_.as<int>();
+      }
+      if (proj_epi != nullptr && proj_epi->defer) {
+        // the greedy choice the head deferred (launch_chunk)
+        if (l == 0) {
+          a.greedy_best = proj_epi->best;
+          a.greedy_active = proj_epi->active;
+          a.greedy_blank = proj_epi->blank;
+          a.tokens = proj_epi->tokens;
+          a.token_frames = proj_epi->token_frames;
+          a.counts = proj_epi->counts;
+          a.cap = proj_epi->cap;
+          a.frame = proj_epi->frame;
+        } else if (l == 1) {
+          a.clear_best = proj_epi->best;
+        }
       }
       check_cuda(cq::launch_lstm_step(dt, g, maps, a, st, pdl), "lstm step");
       hpar_[l] ^= 1;
@@ -544,6 +560,7 @@ void RnntState::launch_chunk(const void* encoded, int ld, int frames, int* token
       e.H = H;
       e.x = x_.get();
       e.last_token = ih0_from_table_ ? last_token_.as<int>() : nullptr;
+      e.defer = defer_greedy_ ? 1 : 0;
       e.tokens = tokens;
       e.token_frames = token_frames;
       e.counts = counts;

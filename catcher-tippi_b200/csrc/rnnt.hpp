@@ -137,6 +137,9 @@ class RnntState {
   // stream feeds its prediction network next (the greedy epilogue writes it)
   bool ih0_from_table_ = false;
   DeviceBuffer last_token_;
+  // the head only folds logits into best_; layer 0's step decodes the tokens
+  // and records them, layer 1's clears best_ (two or more layers)
+  bool defer_greedy_ = false;
   std::vector<DeviceBuffer> h_next_;
   std::vector<int> hpar_;
   // persistent path: second hidden-state buffer per layer, head partials, barrier

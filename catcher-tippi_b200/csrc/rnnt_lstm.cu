@@ -72,6 +72,11 @@ __device__ __forceinline__ int ld_volatile_s32(const int* p) {
   asm volatile("ld.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ uint2 ld_volatile_v2u32(const void* p) {
   uint2 v;
   asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
@@ -147,19 +152,53 @@ __global__ void __launch_bounds__(kThreads, MINB)
     // mt*16 + p%16), fetched before the product so the lookup (token id,
     // then row) overlaps the MMAs
     uint2 gi_bits[kCellIters];
+    bool steps[kCellIters];  // deferred greedy choice: the stream steps
 #pragma unroll
     for (int it = 0; it < kCellIters; ++it) {
       gi_bits[it] = make_uint2(0u, 0u);
+      steps[it] = false;
       const int p = tid + it * kThreads;
       if constexpr (FORM == 1) {
         const int s = mt * 16 + (p & 15);
         if (p < kUnits * 16 && s < a.S && n0 / 4 + (p >> 4) < H) {
-          const int tok = ld_volatile_s32(a.gi_token + s);
+          int tok;
+          if (a.greedy_best != nullptr) {
+            const unsigned long long key = ld_volatile_u64(a.greedy_best + s);
+            tok = key == 0ull ? 0 : static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key));
+            steps[it] = ld_volatile_s32(a.greedy_active + s) != 0 && tok != a.greedy_blank;
+          } else {
+            tok = ld_volatile_s32(a.gi_token + s);
+          }
           gi_bits[it] = ld_volatile_v2u32(static_cast<const uint16_t*>(a.gi_table) +
                                           static_cast<size_t>(tok) * N + n0 + 4 * (p >> 4));
         }
       }
     }
+    // band 0 records the deferred choice of its 16 streams (other CTAs that
+    // read `active` after this write decide the same: a stream that emitted
+    // blank reads 0 either way, one that emitted a token reads 1)
+    if (FORM == 1 && a.greedy_best != nullptr && blockIdx.y == 0 && tid < 16) {
+      const int s = mt * 16 + tid;
+      if (s < a.S) {
+        const unsigned long long key = ld_volatile_u64(a.greedy_best + s);
+        const int tok = key == 0ull ? 0 : static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key));
+        if (ld_volatile_s32(a.greedy_active + s) != 0) {
+          if (tok == a.greedy_blank) {
+            a.greedy_active[s] = 0;
+          } else {
+            const int n = a.counts[s];
+            if (n < a.cap) {
+              a.tokens[static_cast<size_t>(s) * a.cap + n] = tok;
+              a.token_frames[static_cast<size_t>(s) * a.cap + n] = a.frame;
+            }
+            a.counts[s] = n + 1;
+          }
+        }
+      }
+    }
+    if (FORM == 0 && a.clear_best != nullptr && blockIdx.y == 0 && rank == 0 && tid < 16 &&
+        mt * 16 + tid < a.S)
+      a.clear_best[mt * 16 + tid] = 0ull;
     // ---- activations of this token tile, all loads in flight at once
     uint4 xr[kSbPerWarp][2][2];
 #pragma unroll
@@ -241,7 +280,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
           continue;
         }
         const size_t hj = static_cast<size_t>(s) * H + j;
-        if (a.all || a.active[s]) {
+        const bool step = FORM == 1 && a.greedy_best != nullptr ? steps[it] : (a.all || a.active[s]);
+        if (step) {
           float gi[4];
           if constexpr (FORM == 1) {
             // the four gates of unit j are adjacent in the interleaved row

@@ -103,6 +103,19 @@ struct LstmStepArgs {
   const void* gi_table;
   const int* gi_token;  // [S]
   void* gi_out;
+  // Greedy choice deferred from the head (layer 0 with gi_table): the token
+  // of stream s decodes from greedy_best[s] (ordered logit << 32 | ~index,
+  // 0: index 0); a stream steps if it was active and the token is not blank.
+  // The CTAs of band 0 record it: active, tokens, token_frames, counts.
+  const unsigned long long* greedy_best;  // [S] or nullptr
+  int* greedy_active;                     // [S]
+  int greedy_blank;
+  int* tokens;        // [S, cap]
+  int* token_frames;  // [S, cap]
+  int* counts;        // [S]
+  int cap, frame;
+  // A later layer's band 0 zeroes the keys for the next head (or nullptr).
+  unsigned long long* clear_best;
 };
 bool lstm_step_fits(int H, int group);
 cudaError_t launch_lstm_step(int dtype, int group, const LstmMaps& maps, const LstmStepArgs& a,
