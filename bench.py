@@ -99,6 +99,24 @@ def measured_tensor_peak() -> tuple[float, str]:
         return 1400.0, "fallback"
 
 
+def max_over_ranks(dist, ms: float, device: str = "cuda") -> float:
+    """The slowest rank's device time: every rank passes its own, all get the
+    maximum (one all-reduce, taken by every rank in the same order)."""
+    if dist is None:
+        return ms
+    import torch
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def weak_scaling_value(world: int, units_per_rank: float, ms: float) -> float:
+    """Whole-job throughput of a weak-scaling run: every rank processed the
+    same units (bytes, audio seconds) and the job took the slowest rank's
+    time, so value = world * units / max time."""
+    return world * units_per_rank / (ms * 1e-3)
+
+
 def measured_peak() -> tuple[float, str]:
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -380,11 +398,7 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
         e.record(s_enc)
         torch.cuda.synchronize()
         ms = s.elapsed_time(e)
-        if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(dist, ms)
 
     clocks = ClockSampler(local_rank)
     clocks.start()
@@ -396,7 +410,7 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
     if status != 0:
         raise RuntimeError(f"device watchdog reported status {status}")
     per_chunk = ms / chunks
-    audio = world * streams * CHUNK_AUDIO_S * chunks
+    audio = streams * CHUNK_AUDIO_S * chunks  # per rank
     flops = encoder_flops_per_chunk(streams)
     tpeak, tkind = measured_tensor_peak()
     tflops = flops / (per_chunk * 1e-3) / 1e12
@@ -407,7 +421,7 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
                  "10 symbols per frame; random weights emit the maximum), RNNT of chunk c pipelined "
                  "with the encoder of chunk c+1 on a second CUDA stream")
     res = {
-        "metric": "encoder audio-sec/sec", "value": round(audio / (ms * 1e-3), 1),
+        "metric": "encoder audio-sec/sec", "value": round(weak_scaling_value(world, audio, ms), 1),
         "unit": "audio-s/s", "streams_per_gpu": streams, "chunks": chunks,
         "ms_per_chunk": round(per_chunk, 4), "chunk_audio_s": CHUNK_AUDIO_S,
         "workload": (f"{what}; {streams} lock-step streams per GPU, 112 log-mel frames x 128 bins "
@@ -421,7 +435,7 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
         "gpu_launches": kernels * chunks, "kernels_per_chunk": kernels,
     }
     if ms_e2e is not None:
-        res["e2e"] = {"value": round(audio / (ms_e2e * 1e-3), 1), "unit": "audio-s/s",
+        res["e2e"] = {"value": round(weak_scaling_value(world, audio, ms_e2e), 1), "unit": "audio-s/s",
                       "h2d_bytes_per_step": host_mel.numel() * 4,
                       "d2h_bytes_per_step": (host_tok.numel() + host_cnt.numel()) * 4
                       if with_rnnt else host_out.numel() * 2,
@@ -477,11 +491,7 @@ def bench_rnnt(torch, cq, args, world: int, local_rank: int, dist, streams: int)
         e1.record(s)
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1)
-        if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        return ms
+        return max_over_ranks(dist, ms)
 
     clocks = ClockSampler(local_rank)
     clocks.start()
@@ -491,16 +501,16 @@ def bench_rnnt(torch, cq, args, world: int, local_rank: int, dist, streams: int)
     status = cq.device_status(local_rank)
     if status != 0:
         raise RuntimeError(f"device watchdog reported status {status}")
-    audio = world * streams * CHUNK_AUDIO_S * args.steps
+    audio = streams * CHUNK_AUDIO_S * args.steps  # per rank
     res = {
-        "metric": "RNNT decode audio-sec/sec", "value": round(audio / (ms * 1e-3), 1),
+        "metric": "RNNT decode audio-sec/sec", "value": round(weak_scaling_value(world, audio, ms), 1),
         "unit": "audio-s/s", "ms_per_chunk": round(ms / args.steps, 4),
         "symbols_per_stream_per_chunk": round(float(cnt.float().mean().item()), 1),
         "workload": (f"batched RNNT greedy decode (2-layer LSTM 640, joint 640 -> vocab 1025, at "
                      f"most 10 symbols per frame), {streams} lock-step streams per GPU, 14 encoder "
                      f"frames (1.12 s) per chunk, random-init INT8 group 64 bf16"),
         "clocks": clock_info, "gpu_launches": st.kernels_per_chunk * args.steps,
-        "e2e": {"value": round(audio / (ms_e2e * 1e-3), 1), "unit": "audio-s/s",
+        "e2e": {"value": round(weak_scaling_value(world, audio, ms_e2e), 1), "unit": "audio-s/s",
                 "h2d_bytes_per_step": host_enc.numel() * 2,
                 "d2h_bytes_per_step": (host_tok.numel() + host_cnt.numel()) * 4,
                 "path": "pinned host encoder output -> device, cq_rnnt_decode_chunk, token ids "
@@ -652,10 +662,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         e.record(cur)
         torch.cuda.synchronize()
         ms = s.elapsed_time(e)
+        ms = max_over_ranks(dist, ms)
         if dist:
-            t = torch.tensor([ms], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
             dist.barrier()
         return ms
 
@@ -683,8 +691,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     if status != 0:
         raise RuntimeError(f"device watchdog reported status {status}")
     ms_step = ms / args.steps
-    value = world * step_bytes / (ms_step * 1e-3) / 1e9
-    value_e2e = world * step_bytes / (ms_e2e / args.steps * 1e-3) / 1e9
+    value = weak_scaling_value(world, step_bytes, ms_step) / 1e9
+    value_e2e = weak_scaling_value(world, step_bytes, ms_e2e / args.steps) / 1e9
     peak, peak_kind = measured_peak()
     per_launch_us = ms_step * 1e3 / launches
     achieved = (step_bytes / launches) / (per_launch_us * 1e-6) / 1e9
