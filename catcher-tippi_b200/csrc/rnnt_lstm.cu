@@ -368,14 +368,16 @@ struct Variant {
     return e;
   }
   // launch units (clusters or CTAs) resident at once; 0 if it cannot launch
+  // (cached for the last hidden size asked about: the shared memory follows it)
   static int resident(const cudaLaunchConfig_t& base, int H) {
-    static int cache = 0;
-    if (cache != 0) return std::max(cache, 0);
+    static int cache_h = -1, cache = 0;
+    if (cache_h == H) return cache;
     cudaLaunchConfig_t cfg = base;
     cfg.dynamicSmemBytes = smem(H);
+    cache_h = H;
     if (prepare(cfg.dynamicSmemBytes) != cudaSuccess) {
       (void)cudaGetLastError();
-      cache = -1;
+      cache = 0;
       return 0;
     }
     cache = resident_units(reinterpret_cast<const void*>(lstm_step_kernel<DT, G, RT, MINB, FORM>), cfg,
