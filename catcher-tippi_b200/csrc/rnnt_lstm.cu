@@ -3,22 +3,27 @@
 // (LstmCell::forward, crates/nemotron-mlx/src/model/rnnt.rs:86-150) -- the
 // work of two K1 launches and the cell kernel.
 //
-// The two products run as the two CTAs of a (2, 1, 1) cluster over the same
-// 64-row band: rank 0 multiplies the layer input by W_ih, rank 1 the previous
-// hidden state by W_hh, each exactly as K1 does for one band (same sub-block
-// order, same warp reduction: bit-identical partial sums).  Rank 1 pushes its
-// partial tile into rank 0's shared memory, and rank 0 rounds each product to
-// T, adds them and the gate bias in T and runs the cell.  The weight rows are
-// interleaved at load time (row 4j + q holds gate q of hidden unit j) so one
-// band holds all four gates of 16 hidden units.  The new hidden state goes to
-// a second buffer (other CTAs still read the old one); streams that are not
-// active keep their state (h copied across, c untouched).  Layer 0 can take
-// its ih product from a per-token table instead (FORM 1: one CTA per band
-// multiplies W_hh h, the cell reads T(W_ih emb[token]) from the table made
-// once by this kernel's FORM 0 with gi_out set).  Token tiles
-// spread over grid.z; when all clusters fit one wave the kernel runs one CTA
-// per SM with the registers that allows, else two per SM (a cluster walks
-// several token tiles only past the grid limit, at one CTA per SM).
+// The weight rows are interleaved at load time (row 4j + q holds gate q of
+// hidden unit j), so one band of 16 * RT rows holds all four gates of 4 * RT
+// hidden units.  FORM 0: the two products run as the two CTAs of a (2, 1, 1)
+// cluster over the same band -- rank 0 multiplies the layer input by W_ih,
+// rank 1 the previous hidden state by W_hh, each exactly as K1 does for one
+// band (same sub-block order, same warp reduction: bit-identical partial
+// sums); rank 1 pushes its partial tile into rank 0's shared memory, and rank
+// 0 rounds each product to T, adds them and the gate bias in T and runs the
+// cell.  FORM 1 (layer 0, whose input is always an embedding row): one CTA
+// per band multiplies W_hh h and reads T(W_ih emb[token]) from a per-token
+// table that FORM 0 made once with gi_out set; it can also finish the greedy
+// choice the head deferred (token from the per-stream argmax key, band 0
+// records it).  The new hidden state goes to a second buffer (other CTAs
+// still read the old one); streams that are not stepping keep their state
+// (h copied across, c untouched).
+//
+// Launch shape, per launch: token tiles spread over grid.z; the first of
+// {64-row bands at one CTA per SM, 64-row bands at two per SM, 80-row bands
+// at two per SM} whose grid fits one wave of resident CTAs, else 64-row
+// bands at two per SM (a CTA walks several token tiles only past the grid
+// limit, at one per SM).
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "rnnt_ops.hpp"
