@@ -103,7 +103,8 @@ struct GemvParams<kKindEpilogue> {
 
 // Greedy epilogue, after this CTA folded token tile mt's maxima into
 // epi.best: the last of the tile's `ctas` CTAs records the choices of its 16
-// streams (one atomic round trip) and gathers their next embedding rows.
+// streams (one atomic round trip) and passes each emitted token on, as its id
+// (last_token) or its embedding row (x).
 __device__ void greedy_finish(const RnntEpilogue& epi, int M, int mt, unsigned ctas, int* scratch,
                               int tid) {
   if (tid == 0) {

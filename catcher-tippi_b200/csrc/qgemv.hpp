@@ -25,10 +25,12 @@ struct GemvArgs {
 // input and the greedy choice need no launches of their own:
 //  * kGemvJointInput (decoder projector, y = dec_new): active streams take
 //    dec = y, then fused = T(relu(enc + dec)) for every stream;
-//  * kGemvGreedy (vocabulary head, y = logits): each CTA folds its logits into
-//    a per-stream 64-bit maximum of (ordered value, ~index) -- the first index
-//    of the largest logit, MLX argmax -- and the last CTA to finish records the
-//    token (or retires the stream on blank) and gathers the next embedding row.
+//  * kGemvGreedy (vocabulary head; no logits are stored): each CTA folds its
+//    logits into a per-stream 64-bit maximum of (ordered value, ~index) --
+//    the first index of the largest logit, MLX argmax.  Unless `defer` hands
+//    the choice to the next launch, the last CTA to finish records the token
+//    (or retires the stream on blank) and either writes its id to last_token
+//    or gathers the next embedding row into x.
 enum GemvMode : int { kGemvPlain = 0, kGemvJointInput = 1, kGemvGreedy = 2 };
 struct RnntEpilogue {
   int* active;  // [S] stream still emitting on this frame
