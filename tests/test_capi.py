@@ -137,3 +137,6 @@ def test_encoder_abi_rejects_null_arguments_without_a_device(cq):
     assert L.cq_encoder_state_output_frames(None, 112) == 0
     assert L.cq_encoder_tensor_count(None) == -1
     assert L.cq_encoder_linear(None, b"x") is None
+    assert L.cq_encoder_state_set_pdl(None, 0) == cq.CQ_INVALID_ARGUMENT
+    assert L.cq_rnnt_state_set_pdl(None, 0) == cq.CQ_INVALID_ARGUMENT
+    assert L.cq_rnnt_state_set_persistent(None, 1) == cq.CQ_INVALID_ARGUMENT
