@@ -520,6 +520,76 @@ def bench_rnnt(torch, cq, args, world: int, local_rank: int, dist, streams: int)
     return res
 
 
+def bench_logmel(torch, cq, args, world: int, local_rank: int, dist, streams: int) -> dict:
+    """GPU log-mel frontend alone (cq_logmel_extract): one step = the uncentered
+    18320-sample window of every stream (112 frames x 128 mel bins, one 1.12 s
+    chunk of the streaming scheduler); e2e adds the pinned-host PCM copy and
+    the feature read-back to every step."""
+    from nemotron_cuda.logmel import LogMelFrontend
+    fe = LogMelFrontend.nemotron(device=local_rank)
+    samples = 112 * 160 + 400
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(23 + local_rank)
+    audio = torch.randn((streams, samples), generator=gen, device="cuda") * 0.1
+    frames = fe.frames(samples, False)
+    out = torch.empty((streams, frames, 128), device="cuda")
+    host_audio = torch.empty((streams, samples), dtype=torch.float32).pin_memory()
+    host_audio.copy_(audio.cpu())
+    host_out = torch.empty((streams, frames, 128), dtype=torch.float32).pin_memory()
+    s = torch.cuda.Stream()
+
+    def run(n: int, e2e: bool) -> None:
+        with torch.cuda.stream(s):
+            for _ in range(n):
+                if e2e:
+                    audio.copy_(host_audio, non_blocking=True)
+                fe.extract_raw(audio, samples, False, out, stream=s)
+                if e2e:
+                    host_out.copy_(out, non_blocking=True)
+
+    def timed(e2e: bool) -> float:
+        run(args.warmup, e2e)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        run(args.steps, e2e)
+        e1.record(s)
+        torch.cuda.synchronize()
+        return max_over_ranks(dist, e0.elapsed_time(e1))
+
+    clocks = ClockSampler(local_rank)
+    clocks.start()
+    ms = timed(False)
+    clock_info = clocks.stop()
+    ms_e2e = timed(True)
+    status = cq.device_status(local_rank)
+    if status != 0:
+        raise RuntimeError(f"device watchdog reported status {status}")
+    audio_s = streams * CHUNK_AUDIO_S * args.steps  # per rank
+    step_bytes = streams * samples * 4 + streams * frames * 128 * 4
+    peak, peak_kind = measured_peak()
+    achieved = step_bytes / (ms / args.steps * 1e-3) / 1e9
+    res = {
+        "metric": "log-mel frontend audio-sec/sec", "value": round(weak_scaling_value(world, audio_s, ms), 1),
+        "unit": "audio-s/s", "ms_per_chunk": round(ms / args.steps, 4),
+        "workload": (f"log-mel frontend (preemphasis 0.97, Hann 400 in n_fft 512, f64 FFT, 128 Slaney "
+                     f"mel bins, ln) of {streams} uncentered 18320-sample windows per step"),
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
+                     "note": "PCM in + features out per step / step time", "traffic": None},
+        "clocks": clock_info, "gpu_launches": args.steps,
+        "e2e": {"value": round(weak_scaling_value(world, audio_s, ms_e2e), 1), "unit": "audio-s/s",
+                "h2d_bytes_per_step": host_audio.numel() * 4, "d2h_bytes_per_step": host_out.numel() * 4,
+                "path": "pinned host PCM -> device, cq_logmel_extract, features -> pinned host, every "
+                        "step inside the timed region"},
+    }
+    del fe
+    return res
+
+
 def cpu_encoder_baseline(target_s: float = 8.0, with_rnnt: bool = True) -> dict:
     """The CPU restatement of the encoder (oracle/encoder_oracle.py, numpy +
     the OpenMP C linear) and, with `with_rnnt`, of the RNNT greedy decoder
@@ -591,6 +661,21 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds, not args.no_rnnt)
         return line
+    if args.workload == "logmel":
+        res = bench_logmel(torch, cq, args, world, local_rank, dist, args.streams)
+        if dist:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        return {"metric": res["metric"], "value": res["value"], "unit": res["unit"],
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": res["ms_per_chunk"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (PCM ~ N(0, 0.01))",
+                "config": {"workload": res["workload"], "streams_per_gpu": args.streams,
+                           "parallelism": f"dp{world} (independent streams)",
+                           "l2": "inputs smaller than L2 (8.4 MB per step at 64 streams)"},
+                "e2e": res["e2e"], "roofline": res["roofline"], "clocks": res["clocks"],
+                "gpu_launches": res["gpu_launches"]}
     if args.workload == "rnnt":
         res = bench_rnnt(torch, cq, args, world, local_rank, dist, args.streams)
         if dist:
@@ -846,16 +931,17 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["block", "linear", "batched", "encoder", "rnnt"],
+    ap.add_argument("--workload", choices=["block", "linear", "batched", "encoder", "rnnt", "logmel"],
                     default="block",
                     help="block: the 24-block M=14 linear chain (default, plus the full "
                          "encoder at 64 streams and at 1 stream as the line's 'encoder' "
                          "object); linear: one 4096x1024 linear, independent back-to-back "
                          "launches; batched: the 24-block chain at M=896 (64 streams), "
                          "tensor-core path; encoder: the full streaming encoder alone "
-                         "(value in audio-s/s); rnnt: the batched RNNT greedy decoder alone")
+                         "(value in audio-s/s); rnnt: the batched RNNT greedy decoder alone; "
+                         "logmel: the GPU log-mel frontend alone")
     ap.add_argument("--streams", type=int, default=ENC_STREAMS,
-                    help="streams per GPU of the encoder and rnnt workloads")
+                    help="streams per GPU of the encoder, rnnt and logmel workloads")
     ap.add_argument("--encoder-chunks", type=int, default=20,
                     help="timed chunks of the encoder measurement in the default run")
     ap.add_argument("--no-encoder", action="store_true")

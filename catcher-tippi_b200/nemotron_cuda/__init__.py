@@ -127,6 +127,15 @@ def lib() -> ctypes.CDLL:
         "cq_linear_from_artifact": ([vp, ctypes.c_char_p, ctypes.c_char_p, i32, i32, pp], i32),
         "cq_encoder_bind_artifact": ([vp, vp], i32),
         "cq_rnnt_bind_artifact": ([vp, vp], i32),
+        # log-mel frontend (include/cqlogmel.h)
+        "cq_logmel_create": ([i32, i32, i32, i32, i32, ctypes.c_float, i32, pp], i32),
+        "cq_logmel_create_nemotron": ([i32, pp], i32),
+        "cq_logmel_frames": ([vp, ctypes.c_int64, i32], ctypes.c_int64),
+        "cq_logmel_mel_bins": ([vp], i32),
+        "cq_logmel_window": ([vp, vp, sz], i32),
+        "cq_logmel_filters": ([vp, vp, sz], i32),
+        "cq_logmel_extract": ([vp, vp, i32, ctypes.c_int64, ctypes.c_int64, i32, vp, vp], i32),
+        "cq_logmel_destroy": ([vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
