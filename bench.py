@@ -336,8 +336,16 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
     outs = [st.encode_chunk(mel)]  # first chunk (eager; later chunks replay a graph)
     frames = outs[0].shape[0] // streams
     s_enc = torch.cuda.Stream()
-    host_mel = torch.empty(tuple(mel.shape), dtype=torch.float32).pin_memory()
-    host_mel.copy_(mel.cpu())
+    # e2e input: each stream's 1.12 s window of 16 kHz PCM as the chunk
+    # scheduler cuts it (18320 samples, uncentered -> 112 frames), through the
+    # GPU log-mel frontend (cq_logmel_extract) into the encoder's input
+    from nemotron_cuda.logmel import LogMelFrontend
+    fe = LogMelFrontend.nemotron(device=local_rank)
+    pcm_samples = CHUNK_MEL * 160 + 400
+    assert fe.frames(pcm_samples, False) == CHUNK_MEL
+    pcm = torch.randn((streams, pcm_samples), generator=gen, device="cuda") * 0.1
+    host_pcm = torch.empty((streams, pcm_samples), dtype=torch.float32).pin_memory()
+    host_pcm.copy_(pcm.cpu())
     rn = rst = None
     if with_rnnt:
         from nemotron_cuda.rnnt import Rnnt
@@ -365,7 +373,8 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
             b = i % 2 if with_rnnt else 0
             with torch.cuda.stream(s_enc):
                 if e2e:
-                    mel.copy_(host_mel, non_blocking=True)
+                    pcm.copy_(host_pcm, non_blocking=True)
+                    fe.extract_raw(pcm, pcm_samples, False, mel, stream=s_enc)
                 if with_rnnt:
                     s_enc.wait_event(dec_done[b])  # the decoder has read this buffer
                 st.encode_chunk(mel, outs[b], stream=s_enc)
@@ -436,14 +445,15 @@ def bench_encoder(torch, cq, args, world: int, local_rank: int, dist, streams: i
     }
     if ms_e2e is not None:
         res["e2e"] = {"value": round(weak_scaling_value(world, audio, ms_e2e), 1), "unit": "audio-s/s",
-                      "h2d_bytes_per_step": host_mel.numel() * 4,
+                      "h2d_bytes_per_step": host_pcm.numel() * 4,
                       "d2h_bytes_per_step": (host_tok.numel() + host_cnt.numel()) * 4
                       if with_rnnt else host_out.numel() * 2,
-                      "path": "pinned host log-mel -> device, cq_encoder_encode_chunk"
+                      "path": "pinned host PCM (18320 samples per stream) -> device, "
+                              "cq_logmel_extract, cq_encoder_encode_chunk"
                               + (", cq_rnnt_decode_chunk, token ids and counts" if with_rnnt
                                  else ", encoder output") +
                               " -> pinned host, every chunk inside the timed region"}
-    del st, enc, rst, rn
+    del st, enc, rst, rn, fe
     return res
 
 
