@@ -288,3 +288,37 @@ def test_from_f32_matches_oracle_quantiser(cq, torch_dev, oracle_mod):
 
 def test_device_status_clean(cq, torch_dev):
     assert cq.device_status(0) == 0
+
+
+# The diarizer's Fast-Conformer (crates/sortformer-mlx/src/model/encoder.rs)
+# binds the same QuantizedLinear, with output biases everywhere: d_model 512,
+# ff 2048, 8 heads, 256 subsampling channels over 16 frequency bins
+# (tests/fixtures/sortformer_config.json); a 188-frame chunk with context
+# runs about 190 rows per call.
+SORTFORMER_SITES = [
+    (2048, 512),  # FFN linear1 (encoder.rs:413-431)
+    (512, 2048),  # FFN linear2
+    (512, 512),   # q/k/v/out/pos (encoder.rs:446-480), conv pointwise2
+    (1024, 512),  # conv pointwise1 (encoder.rs:570-612)
+    (256, 256),   # subsampling pointwise convs (encoder.rs:283-335)
+    (512, 4096),  # subsampling output linear
+]
+
+
+@pytest.mark.parametrize("n,k", SORTFORMER_SITES)
+@pytest.mark.parametrize("m", [1, 190])
+def test_sortformer_call_sites_f16(cq, torch_dev, oracle_mod, n, k, m):
+    q, s, b, x, bias = make_case(oracle_mod, n, k, m, 64, "f16", seed=5 * n + k + m, with_bias=True)
+    y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, "f16")
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "f16", bias), "f16", min_exact=0.97,
+                  bias_bits=bias)
+
+
+@pytest.mark.parametrize("n,k", [(2048, 512), (512, 2048), (512, 4096)])
+def test_sortformer_call_sites_batched(cq, torch_dev, oracle_mod, n, k):
+    """Two streams' chunks stacked (400 rows): the tensor-core GEMM."""
+    from conftest import GEMM_FLOOR
+    q, s, b, x, bias = make_case(oracle_mod, n, k, 400, 128, "f16", seed=n + 3 * k, with_bias=True)
+    y = run_gpu(cq, torch_dev, q, s, b, bias, x, 128, "f16")
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 128, "f16", bias), "f16", min_exact=0.6,
+                  floor_frac=GEMM_FLOOR, bias_bits=bias)
