@@ -13,9 +13,15 @@
 namespace cq {
 namespace {
 
-// One warp per (row, group).  scale = (max - min) / 255, bias = min,
-// q = round-half-even((w - min) / scale) clamped to [0, 255]; a constant group
-// gets scale 0 and q = 0 so that it dequantises to its value exactly.
+// One warp per (row, group), MLX's edge/sign form of affine quantisation:
+// the group's extreme of larger magnitude (the edge) becomes the bias and is
+// represented exactly; step = max((max - min) / 255, 1e-7) takes the edge's
+// sign, q0 = round(edge / step), and when q0 != 0 the scale is edge / q0 (else
+// the scale stays step and the bias is 0).  Codes are
+// clamp(round((w - bias) / scale), 0, 255) from the fp32 scale and bias, which
+// are rounded to T only when stored.  round = half to even; every operation is
+// an IEEE single-rounded fp32 operation, so the result is bit-identical to the
+// CPU restatement.
 template <int DT>
 __global__ void quantize_kernel(const float* __restrict__ w, int N, int K, int g, int round_input,
                                 uint8_t* __restrict__ q, void* __restrict__ scales,
@@ -41,16 +47,25 @@ __global__ void quantize_kernel(const float* __restrict__ w, int N, int K, int g
     lo = fminf(lo, __shfl_xor_sync(0xFFFFFFFFu, lo, o));
     hi = fmaxf(hi, __shfl_xor_sync(0xFFFFFFFFu, hi, o));
   }
-  const float scale = (hi - lo) / 255.0f;
+  const bool low_edge = fabsf(lo) > fabsf(hi);
+  const float step = fmaxf(__fdiv_rn(__fsub_rn(hi, lo), 255.0f), 1e-7f);
+  float scale = low_edge ? step : -step;
+  const float edge = low_edge ? lo : hi;
+  const float q0 = rintf(__fdiv_rn(edge, scale));
+  float bias = 0.0f;
+  if (q0 != 0.0f) {
+    scale = __fdiv_rn(edge, q0);
+    bias = edge;
+  }
   uint8_t* dst = q + static_cast<size_t>(n) * K + static_cast<size_t>(j) * g;
   for (int i = 0; i < per; ++i) {
-    float cdx = scale > 0.0f ? rintf((v[i] - lo) / scale) : 0.0f;
+    float cdx = rintf(__fdiv_rn(__fsub_rn(v[i], bias), scale));
     cdx = fminf(fmaxf(cdx, 0.0f), 255.0f);
     dst[lane * per + i] = static_cast<uint8_t>(cdx);
   }
   if (lane == 0) {
     st_t<DT>(scales, item, scale);
-    st_t<DT>(biases, item, lo);
+    st_t<DT>(biases, item, bias);
   }
 }
 

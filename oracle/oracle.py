@@ -15,11 +15,15 @@ Two independent restatements of the same algorithm live here:
 Both follow crates/nemotron-mlx/src/model/layers.rs:298-310
 (``QuantizedLinear::forward_array``: cast x to T, ``quantized_matmul(transpose=true,
 bits=8)`` in T, add the T output bias) and MLX's published affine quantisation
-(scale = (max-min)/255, bias = min, q = round((w-min)/scale), 4 codes per u32,
-least significant byte first).  Bit-level agreement with MLX's Metal kernels is
-unpinned (MLX cannot run here); the oracle is pinned to the reference's own
-tolerance tests (crates/nemotron-mlx/tests/quantized_matmul.rs:24-47,
-model_layers.rs:35-78, weight_roundtrip.rs:50-115).
+in its fp32 (CPU-stream) form: the group's extreme of larger magnitude is the
+edge and the bias, step = max((max-min)/255, 1e-7) with the edge's sign,
+q0 = round(edge/step), scale = edge/q0 when q0 != 0, codes
+clamp(round((w-bias)/scale), 0, 255) from the fp32 scale and bias, which are
+then stored in T; round half to even; 4 codes per u32, least significant byte
+first.  Bit-level agreement with MLX itself is unpinned (MLX cannot run here);
+the oracle is pinned to the reference's own tolerance tests
+(crates/nemotron-mlx/tests/quantized_matmul.rs:24-47, model_layers.rs:35-78,
+weight_roundtrip.rs:50-115) and to hand-derived cases of the edge/sign rule.
 """
 from __future__ import annotations
 
@@ -110,6 +114,8 @@ def quantize(w: np.ndarray, group: int, dtype: str, round_input: bool = True):
     n, k = w.shape
     if group <= 0 or k % group:
         raise ValueError(f"input dimension {k} is not divisible by group size {group}")
+    if group > 128:
+        raise ValueError(f"group size {group} is above MLX's largest (128)")
     q = np.empty((n, k), dtype=np.uint8)
     s = np.empty((n, k // group), dtype=_tbits(dtype))
     b = np.empty_like(s)
@@ -194,19 +200,26 @@ def np_from_t(x: np.ndarray, dtype: str) -> np.ndarray:
 
 
 def np_quantize(w: np.ndarray, group: int, dtype: str, round_input: bool = True):
+    """numpy mirror of MLX's edge/sign affine quantisation (oracle_quantize_group)."""
     w = np.asarray(w, dtype=np.float32)
     if round_input:
         w = np_from_t(np_to_t(w, dtype), dtype)
     n, k = w.shape
+    f = np.float32
     wg = w.reshape(n, k // group, group)
     lo = wg.min(axis=2)
     hi = wg.max(axis=2)
-    scale = ((hi - lo) / np.float32(255.0)).astype(np.float32)
-    safe = np.where(scale > 0, scale, np.float32(1.0))
-    c = np.rint((wg - lo[..., None]) / safe[..., None])
-    c = np.where(scale[..., None] > 0, c, 0.0)
+    low_edge = np.abs(lo) > np.abs(hi)
+    step = np.maximum((hi - lo) / f(255.0), f(1e-7)).astype(f)
+    scale = np.where(low_edge, step, -step).astype(f)
+    edge = np.where(low_edge, lo, hi).astype(f)
+    q0 = np.rint(edge / scale).astype(f)
+    nz = q0 != 0
+    scale = np.where(nz, edge / np.where(nz, q0, f(1.0)), scale).astype(f)
+    bias = np.where(nz, edge, f(0.0)).astype(f)
+    c = np.rint((wg - bias[..., None]) / scale[..., None])
     q = np.clip(c, 0, 255).astype(np.uint8).reshape(n, k)
-    return q.view(np.uint32), np_to_t(scale, dtype), np_to_t(lo, dtype)
+    return q.view(np.uint32), np_to_t(scale, dtype), np_to_t(bias, dtype)
 
 
 def np_dequantize(q, s, b, group, dtype) -> np.ndarray:

@@ -15,14 +15,21 @@
  *       `__qweight` (u32 [N, K/4]), `__scales` / `__biases` (T [N, K/g]).
  *   - mlx-rs 0.25.3 / mlx-sys 0.2.0 (MLX C++), `quantize` / `dequantize` /
  *     `quantized_matmul` with bits=8 (absent from the reference tree; restated
- *     from MLX's published documentation of affine quantization):
- *       per row and per group of g consecutive elements along K:
- *         scale = (max - min) / (2^8 - 1),  bias = min,
- *         q     = round((w - min) / scale)  in [0, 255],
- *         w_hat = scale * q + bias,
- *       codes packed 4 per uint32 from the least significant byte up, so on a
- *       little-endian host the u32 [N, K/4] array is byte-identical to a
- *       uint8 [N, K] row-major array.
+ *     from MLX's published affine_quantize, the fp32 form of its CPU stream):
+ *       per row and per group of g consecutive elements along K, with the
+ *       group's min and max taken in fp32:
+ *         the edge is the extreme of larger magnitude (min when |min| > |max|,
+ *         else max), step = max((max - min) / 255, 1e-7) carrying the edge's
+ *         sign, q0 = round(edge / step); when q0 != 0 the scale is edge / q0
+ *         and the bias is the edge (so the edge is represented exactly and the
+ *         scale is negative when the edge is the max), otherwise the scale
+ *         stays step and the bias is 0;
+ *         q = clamp(round((w - bias) / scale), 0, 255) from the fp32 scale and
+ *         bias, which are then rounded to T for storage;
+ *         w_hat = scale * q + bias from the stored T values;
+ *       round = round half to even; codes packed 4 per uint32 from the least
+ *       significant byte up, so on a little-endian host the u32 [N, K/4] array
+ *       is byte-identical to a uint8 [N, K] row-major array.
  *
  * Accumulation is fp32 (oracle_qmatmul) or fp64 (oracle_qmatmul_f64, unrounded)
  * over the dequantised fp32 weight; the output is rounded to T once (the
@@ -156,33 +163,51 @@ void oracle_set_threads(int n) {
 }
 
 /*
- * Affine 8-bit quantisation of a row-major [N, K] matrix, groups of g along K.
- * `round_input` != 0 first rounds w to T, as QuantizedLinear::from_f32 does
- * (layers.rs:266-269: the f32 weight is cast to the layer dtype before quantize).
+ * Affine 8-bit quantisation of a row-major [N, K] matrix, groups of g along K,
+ * in MLX's edge/sign form (file header).  `round_input` != 0 first rounds w to
+ * T, as the reference's call sites do (layers.rs:266-269 and artifact.rs:295-297
+ * cast the weight to f16 before `quantize`).
  * q: N*K bytes (the u32 [N, K/4] packing); scales/biases: T [N, K/g].
  */
+void oracle_quantize_group(const float* v, int g, uint8_t* q, float* scale_out, float* bias_out) {
+    float lo = INFINITY, hi = -INFINITY;
+    for (int k = 0; k < g; ++k) {
+        lo = v[k] < lo ? v[k] : lo;
+        hi = v[k] > hi ? v[k] : hi;
+    }
+    const int low_edge = fabsf(lo) > fabsf(hi);
+    float step = (hi - lo) / 255.0f;
+    step = step > 1e-7f ? step : 1e-7f;
+    float scale = low_edge ? step : -step;
+    const float edge = low_edge ? lo : hi;
+    const float q0 = rintf(edge / scale);
+    float bias = 0.0f;
+    if (q0 != 0.0f) {
+        scale = edge / q0;
+        bias = edge;
+    }
+    for (int k = 0; k < g; ++k) {
+        float c = rintf((v[k] - bias) / scale);
+        c = c < 0.0f ? 0.0f : (c > 255.0f ? 255.0f : c);
+        q[k] = (uint8_t)c;
+    }
+    *scale_out = scale;
+    *bias_out = bias;
+}
+
 void oracle_quantize(const float* w, int N, int K, int g, int dtype, int round_input,
                      uint8_t* q, void* scales, void* biases) {
     const int groups = K / g;
 #pragma omp parallel for schedule(static)
     for (int n = 0; n < N; ++n) {
+        float v[128];
         for (int j = 0; j < groups; ++j) {
             const float* src = w + (size_t)n * K + (size_t)j * g;
-            float lo = INFINITY, hi = -INFINITY;
-            for (int k = 0; k < g; ++k) {
-                float v = round_input ? round_t(src[k], dtype) : src[k];
-                lo = v < lo ? v : lo;
-                hi = v > hi ? v : hi;
-            }
-            float scale = (hi - lo) / 255.0f;
-            for (int k = 0; k < g; ++k) {
-                float v = round_input ? round_t(src[k], dtype) : src[k];
-                float c = scale > 0.0f ? rintf((v - lo) / scale) : 0.0f;
-                c = c < 0.0f ? 0.0f : (c > 255.0f ? 255.0f : c);
-                q[(size_t)n * K + (size_t)j * g + k] = (uint8_t)c;
-            }
+            for (int k = 0; k < g; ++k) v[k] = round_input ? round_t(src[k], dtype) : src[k];
+            float scale, bias;
+            oracle_quantize_group(v, g, q + (size_t)n * K + (size_t)j * g, &scale, &bias);
             store_t(scales, (size_t)n * groups + j, scale, dtype);
-            store_t(biases, (size_t)n * groups + j, lo, dtype);
+            store_t(biases, (size_t)n * groups + j, bias, dtype);
         }
     }
 }

@@ -64,9 +64,12 @@ def test_identity_matrices_survive_quantization(fixture_dir, oracle_mod):
     assert g == 128 and list(shape) == [128, 128]
     w = oracle_mod.dequantize(q, s, b, g, "f16")
     off = ~np.eye(128, dtype=bool)
-    assert np.all(w[off] == 0.0)  # zero is exact (bias 0, q 0)
-    # the diagonal is 255 * f16(1/255): within an f16 ulp of 1
-    np.testing.assert_allclose(np.diag(w), 1.0, atol=2.0 ** -10)
+    # each group's edge is its 1.0 (the bias, code 0): the diagonal is exact
+    assert np.all(np.diag(w) == 1.0)
+    # zeros take code 255 at scale f16(-1/255): 1 + 255 * scale, 2^-16 from 0
+    s16 = np.float32(np.float16(np.float32(-1.0) / np.float32(255.0)))
+    assert np.all(w[off] == np.float32(255.0) * s16 + np.float32(1.0))
+    assert np.abs(w[off]).max() <= 2.0 ** -16
 
 
 def test_oracle_encoder_binds_the_fixture(fixture_dir, oracle_mod):

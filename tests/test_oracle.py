@@ -10,7 +10,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from conftest import golden, parity_stats
+from conftest import DEFAULT_FLOOR, golden, parity_stats
 
 
 def test_rounding_matches_numpy_f16(oracle_mod):
@@ -92,7 +92,10 @@ def test_quantize_c_matches_numpy(oracle_mod):
     for dtype in ("f16", "bf16", "f32"):
         for g in (32, 64, 128):
             w = (rng.standard_normal((37, 256)) * 0.05).astype(np.float32)
-            w[3, :g] = 0.25  # constant group: scale 0, q 0
+            w[3, :g] = 0.25  # constant group: bias 0.25, codes 0
+            w[4, :g] = 0.0  # zero group: bias 0, codes 0
+            w[5, :g] = np.abs(w[5, :g]) + 0.01  # one-signed groups
+            w[6, :g] = -np.abs(w[6, :g]) - 0.01
             a = oracle_mod.quantize(w, g, dtype, round_input=dtype != "f32")
             b = oracle_mod.np_quantize(w, g, dtype, round_input=dtype != "f32")
             for x, y in zip(a, b):
@@ -103,10 +106,63 @@ def test_quantize_c_matches_numpy(oracle_mod):
 
 def test_packing_is_lsb_first(oracle_mod):
     """4 codes per u32, first element in the least significant byte (MLX layout)."""
-    w = np.tile(np.array([0.0, 1.0, 2.0, 3.0], np.float32), (1, 16)) * (255.0 / 3.0)
+    # min edge -255 with step 1: codes 0, 85, 170, 255
+    w = np.tile(np.array([-3.0, -2.0, -1.0, 0.0], np.float32), (1, 16)) * (255.0 / 3.0)
     q, s, b = oracle_mod.quantize(w, 64, "f32", round_input=False)
     word = int(q[0, 0])
     assert [(word >> (8 * i)) & 0xFF for i in range(4)] == [0, 85, 170, 255]
+
+
+F = np.float32
+# (group values, codes, scale, bias), derived by hand from the edge/sign rule:
+# edge = the extreme of larger magnitude (the max on a tie), step =
+# (max - min) / 255 with the edge's sign, q0 = round(edge / step),
+# scale = edge / q0, bias = edge, codes round((w - bias) / scale).
+EDGE_SIGN_CASES = [
+    # max edge: q0 = round(1 / (-1.5/255)) = -170, the scale is negative
+    ([1.0, -0.5, 0.0], [0, 255, 170], F(1.0) / F(-170.0), 1.0),
+    # min edge: the mirror image, positive scale
+    ([-1.0, 0.5, 0.0], [0, 255, 170], F(-1.0) / F(-170.0), -1.0),
+    # all positive: q0 = round(1 / (-0.5/255)) = -510
+    ([0.5, 1.0, 0.7], [255, 0, 153], F(1.0) / F(-510.0), 1.0),
+    # all negative: q0 = round(-1 / (0.5/255)) = -510
+    ([-1.0, -0.5, -0.7], [0, 255, 153], F(-1.0) / F(-510.0), -1.0),
+    # |min| == |max| takes the max; 1 / (-2/255) rounds to -127.49999 -> -127,
+    # so -1 lands on code 254
+    ([-1.0, 1.0, 0.3], [254, 0, 89], F(1.0) / F(-127.0), 1.0),
+    # all zero: step is the 1e-7 floor, q0 = 0, bias 0
+    ([0.0], [0], -F(1e-7), 0.0),
+]
+
+
+@pytest.mark.parametrize("vals,codes,scale,bias", EDGE_SIGN_CASES)
+def test_quantize_edge_sign_rule(oracle_mod, vals, codes, scale, bias):
+    """MLX's affine_quantize rule (fp32 form), checked on hand-derived groups."""
+    vals = np.array(vals, np.float32)
+    w = np.full((1, 32), vals[-1], np.float32)
+    w[0, :len(vals)] = vals
+    for impl in (oracle_mod.quantize, oracle_mod.np_quantize):
+        q, s, b = impl(w, 32, "f32", round_input=False)
+        assert list(q.view(np.uint8)[0, :len(vals)]) == codes
+        assert s.view(np.float32)[0, 0] == F(scale)
+        assert b.view(np.float32)[0, 0] == F(bias)
+    # stored in T, the scale and bias are the fp32 values rounded once; the
+    # codes still come from the fp32 values
+    for dtype in ("f16", "bf16"):
+        q, s, b = oracle_mod.quantize(w, 32, dtype)
+        assert list(q.view(np.uint8)[0, :len(vals)]) == codes
+        assert np.array_equal(s, oracle_mod.to_t(np.array([[scale]], np.float32), dtype))
+        assert np.array_equal(b, oracle_mod.to_t(np.array([[bias]], np.float32), dtype))
+
+
+def test_quantize_constant_group_is_exact(oracle_mod):
+    """A constant group keeps its value as the bias with all codes 0."""
+    w = np.full((2, 64), 0.25, np.float32)
+    w[1] = -3.5
+    q, s, b = oracle_mod.quantize(w, 64, "f16")
+    assert not q.any()
+    assert np.array_equal(oracle_mod.from_t(b, "f16").ravel(), [0.25, -3.5])
+    assert np.array_equal(oracle_mod.dequantize(q, s, b, 64, "f16"), w)
 
 
 @pytest.mark.parametrize("dtype", ["f16", "bf16"])
@@ -119,8 +175,11 @@ def test_c_oracle_matches_golden(oracle_mod, dtype, group):
         bias = z.get(f"{name}_bias")
         y = oracle_mod.qmatmul(z[f"{name}_x"], z[f"{name}_q"], z[f"{name}_s"], z[f"{name}_b"],
                                group, dtype, bias, ["none", "silu", "relu"][act])
-        st = parity_stats(y, z[f"{name}_y"], dtype)
+        st = parity_stats(y, z[f"{name}_y"], dtype, bias, DEFAULT_FLOOR)
         # fp32 (C) vs fp64 (numpy) contraction: equal up to one rounding flip
+        # per T rounding, counted as the GPU parity tests count (at |y| + |bias|
+        # + 2^-6 rms(y): fp32 sums of outputs that cancel to near zero carry an
+        # absolute error)
         assert st["exact"] >= 0.98 and st["max_ulp"] <= 2, (name, st)
 
 

@@ -257,7 +257,17 @@ def test_device_quantize_is_bit_exact(cq, torch_dev, oracle_mod, dtype, group):
     torch = torch_dev
     rng = np.random.default_rng(group)
     w = (rng.standard_normal((300, 512)) * 0.03).astype(np.float32)
+    # groups that separate MLX's edge/sign rule from a plain min/max rule:
+    # constant, all zero, one-signed either way, max edge, min edge, |min| == |max|
     w[5, :group] = 0.75
+    w[6, :group] = 0.0
+    w[7] = np.abs(w[7]) + 0.01
+    w[8] = -np.abs(w[8]) - 0.01
+    w[9, :3] = [1.0, -0.5, 0.0]
+    w[10, :3] = [-1.0, 0.5, 0.0]
+    w[11, :2] = [-1.0, 1.0]
+    w[12] *= 1e4  # large values
+    w[13] *= 1e-4  # small values
     q, s, b = cq.quantize(torch.from_numpy(w).cuda(), group, dtype, round_input=dtype != "f32")
     torch.cuda.synchronize()
     q0, s0, b0 = oracle_mod.quantize(w, group, dtype, round_input=dtype != "f32")
