@@ -328,6 +328,18 @@ Artifact::Artifact(const std::string& dir) {
     map_ = nullptr;
     throw Error(CQ_RUNTIME_ERROR, "cannot map " + path);
   }
+  // a constructor that throws runs no destructor: unmap on every error below
+  try {
+    index_safetensors(path);
+  } catch (...) {
+    ::munmap(map_, map_bytes_);
+    map_ = nullptr;
+    arrays_.clear();
+    throw;
+  }
+}
+
+void Artifact::index_safetensors(const std::string& path) {
   const uint8_t* base = static_cast<const uint8_t*>(map_);
   uint64_t hlen = 0;
   for (int i = 7; i >= 0; --i) hlen = (hlen << 8) | base[i];
@@ -345,6 +357,12 @@ Artifact::Artifact(const std::string& dir) {
       throw_invalid("invalid safetensors entry " + kv.first);
     a.dtype = dt->str;
     a.shape = shape_of(kv.second.get("shape"), "safetensors entry " + kv.first);
+    // offsets are JSON numbers (doubles): accept only non-negative integers
+    // that a double represents exactly, before any conversion
+    for (const Json& o : off->arr)
+      if (o.kind != Json::kNum || !(o.num >= 0.0) || o.num > 9007199254740992.0 ||
+          o.num != std::floor(o.num))
+        throw_invalid("invalid safetensors entry " + kv.first + ": bad data_offsets");
     const size_t b0 = static_cast<size_t>(off->arr[0].num), b1 = static_cast<size_t>(off->arr[1].num);
     if (b1 < b0 || b1 > data_bytes) throw_invalid("safetensors entry " + kv.first + " lies outside the file");
     a.data = data + b0;

@@ -59,6 +59,8 @@ class Artifact {
   std::vector<float> f16_to_f32(const std::string& name) const;
 
  private:
+  void index_safetensors(const std::string& path);  // parses the mapped header
+
   std::string model_id_;
   int format_version_ = 0;
   std::map<std::string, ArtifactTensorInfo> tensors_;

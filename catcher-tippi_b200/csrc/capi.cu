@@ -122,7 +122,8 @@ cq_status cq_linear_forward_noalloc(cq_linear* layer, const void* x, int32_t ldx
           "rows x input_dims = " + std::to_string(rows) + "x" + std::to_string(L.input_dims()) +
           " exceeds the no-allocation scratch of " + std::to_string(cap) + " bytes");
     void* scratch = rows > 0 && L.scratch_bytes_for(rows) > 0
-                        ? nemotron_cuda::noalloc_scratch_address(L.device())
+                        ? nemotron_cuda::noalloc_scratch_address(L.device(),
+                                                                static_cast<cudaStream_t>(stream))
                         : nullptr;
     L.forward_array_in_scratch(x, ldx, rows, y, ldy, act, static_cast<cudaStream_t>(stream),
                                scratch, cap);

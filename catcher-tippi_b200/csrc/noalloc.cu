@@ -41,14 +41,25 @@ namespace nemotron_cuda {
 size_t noalloc_scratch_capacity() { return kNoAllocScratchBytes; }
 
 // Device address of the scratch array on `device`.  Looked up once per device,
-// with that device current, on the first no-allocation call there (which
-// therefore must come before any stream capture).
-void* noalloc_scratch_address(int device) {
+// with that device current, on the first no-allocation call there, which
+// therefore must come before any stream capture: a first call on a capturing
+// stream is rejected with a message that says so.  The cached address lives as
+// long as the process's device context; like every handle of this library it
+// does not survive a cudaDeviceReset.
+void* noalloc_scratch_address(int device, cudaStream_t stream) {
   std::lock_guard<std::mutex> lock(g_mu);
   if (device < 0) throw_invalid("invalid device " + std::to_string(device));
   if (g_addr.size() <= static_cast<size_t>(device)) g_addr.resize(device + 1, nullptr);
   if (g_addr[device] == nullptr) {
     DeviceGuard guard(device);
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    const cudaError_t qs = cudaStreamIsCapturing(stream, &capture);
+    if (qs != cudaSuccess || capture != cudaStreamCaptureStatusNone) {
+      if (qs != cudaSuccess) (void)cudaGetLastError();
+      throw_invalid("the first no-allocation call on device " + std::to_string(device) +
+                    " looks up its scratch address and must not run during stream capture;"
+                    " make one call before capturing");
+    }
     void* p = nullptr;
     check_cuda(cudaGetSymbolAddress(&p, g_noalloc_scratch),
                "cudaGetSymbolAddress(no-allocation scratch)");

@@ -205,7 +205,7 @@ size_t dtype_size(cq_dtype dtype);
 
 // Device scratch of the no-allocation entry point (noalloc.cu).
 size_t noalloc_scratch_capacity();
-void* noalloc_scratch_address(int device);
+void* noalloc_scratch_address(int device, cudaStream_t stream);
 
 // backend::quantized_matmul: quantise the f32 weight (f32 scales) on the
 // device and return input . dequant(weight)^T as f32.

@@ -144,9 +144,11 @@ cq_status cq_linear_reserve(cq_linear *layer, int32_t max_rows);
  * 896 rows at input_dims 4096; larger calls fail with CQ_INVALID_ARGUMENT and
  * a message naming the limit.  The first such call on a device looks the
  * array's device address up (once per device), so make it before any stream
- * capture.  All calls share the array and it keeps the last call's contents
- * (every call overwrites what it reads); calls that overlap on the GPU race,
- * so serialise them (one stream, or events).
+ * capture; a first call on a capturing stream fails with CQ_INVALID_ARGUMENT
+ * and says so.  The looked-up address, like every handle of this library,
+ * does not survive a cudaDeviceReset.  All calls share the array and it keeps
+ * the last call's contents (every call overwrites what it reads); calls that
+ * overlap on the GPU race, so serialise them (one stream, or events).
  * No counterpart in the reference: MLX allocates inside its own graph.
  */
 cq_status cq_linear_forward_noalloc(cq_linear *layer, const void *x, int32_t ldx, int32_t rows,

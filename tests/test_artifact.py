@@ -173,6 +173,22 @@ def test_missing_arrays_and_malformed_files_are_rejected(cq, fixture_dir, tmp_pa
         Artifact(_copy_artifact(fixture_dir, str(tmp_path / "hdr"), None,
                                 lambda w: struct.pack("<Q", 1 << 40) + w[8:]))
 
+    def offsets(first):
+        def edit(w):
+            (n,) = struct.unpack("<Q", w[:8])
+            h = json.loads(w[8:8 + n])
+            name = next(k for k in h if k != "__metadata__")
+            h[name]["data_offsets"][0] = first
+            text = json.dumps(h, separators=(",", ":")).encode()
+            text += b" " * (-len(text) % 8)
+            return struct.pack("<Q", len(text)) + text + w[8 + n:]
+        return edit
+    # negative, fractional and beyond-2^53 offsets are rejected before use;
+    # the file mapping is released on every one of these errors
+    for i, first in enumerate((-8, 0.5, 2.0 ** 60)):
+        with pytest.raises(CQError, match="bad data_offsets"):
+            Artifact(_copy_artifact(fixture_dir, str(tmp_path / f"off{i}"), None, offsets(first)))
+
 
 def test_abi_rejects_null_arguments_without_a_device(cq):
     import ctypes
