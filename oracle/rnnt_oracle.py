@@ -156,6 +156,107 @@ def random_params(cfg: RnntConfig, seed: int, dtype: str) -> dict:
     return params
 
 
+# Wide-margin decoder ("trained-like").  Every structural weight is 255 * 2^-k,
+# so in its group of zeros the scale (w / 255 with the edge/sign rule) is
+# exact in f16 and bf16 and the zeros dequantise to exactly 0: nothing but the
+# intended paths carries signal, and every greedy decision stays several logit
+# units from the runner-up.
+_ONE = 255.0 / 256.0     # one-hot embedding and encoder pass-through weight
+_GATE_OPEN = 6.0         # input / output gate bias (sigmoid ~ 0.9975); forget gate -6
+_LSTM_GAIN = 255.0 / 64.0  # g-gate weight: a one-hot input -> ~0.757 one-hot output per layer
+_SUPPRESS_W = -255.0 / 32.0  # decoder projector: last token's unit -> its joint coordinate
+_LIFT_W = 255.0 / 512.0  # decoder projector: "a token was emitted" unit -> blank's coordinate
+_HEAD_GAIN = 255.0 / 64.0
+_BLANK_BIAS = 1.5
+_OTHER_BIAS = -8.0
+
+
+def structured_params(cfg: RnntConfig, seed: int, dtype: str, active: int = 48):
+    """Parameters of a decoder whose greedy decisions all have wide margins.
+
+    It behaves like a trained transducer on synthetic "phone" frames: the
+    encoder projector passes encoder channel c to joint coordinate c; active
+    token i (vocabulary id tokens[i]) is embedded as prediction unit i plus a
+    shared unit (the last one), which both LSTM layers carry through (input and
+    output gates open, forget gate closed, g-gate = gain * identity); the
+    decoder projector turns unit i into a push of about -6 on joint coordinate
+    i (the last token is not repeated) and the shared unit into about +0.38 on
+    blank's coordinate (the last joint unit); the head reads token i from
+    coordinate i and blank from its own, with a blank bias.  So a frame
+    carrying strength 2-4 on channel i emits token i once and then blank, a
+    strength above about 6.8 repeats the token up to max_symbols, and two
+    channels alternate up to the cap.  Head rows of the inactive tokens are
+    N(0, 0.02) noise under a -8 bias.  Returns (params, tokens)."""
+    rng = np.random.default_rng(seed)
+    H, J, E, V = cfg.pred_hidden, cfg.joint_hidden, cfg.enc_hidden, cfg.vocab
+    if not (active < min(H, J) - 1 and J <= E):
+        raise ValueError("structured decoder needs active < hidden sizes and joint <= encoder")
+    tokens = rng.choice(cfg.blank, size=active, replace=False).astype(np.int64)
+    idx = np.arange(active)
+    bc = J - 1  # blank's joint coordinate
+    shared = H - 1  # prediction unit set by every active token
+    f = np.float32
+    params = {}
+
+    def put(name, w, bias=None):
+        q, s, b = qo.quantize(w, cfg.group, dtype)
+        params[name] = (q, s, b, None if bias is None else qo.to_t(np.asarray(bias, f), dtype))
+
+    w = np.zeros((J, E), f)
+    w[np.arange(J), np.arange(J)] = _ONE
+    put("encoder_projector.weight", w, np.zeros(J, f))
+    w = np.zeros((V, H), f)
+    w[tokens, idx] = _ONE
+    w[tokens, shared] = _ONE
+    put("decoder.embedding.weight", w)
+    for l in range(cfg.layers):
+        w = np.zeros((4 * H, H), f)
+        w[2 * H + np.arange(H), np.arange(H)] = _LSTM_GAIN
+        put(f"decoder.lstm.weight_ih_l{l}", w)
+        put(f"decoder.lstm.weight_hh_l{l}", np.zeros((4 * H, H), f))
+        params[f"decoder.lstm.bias_ih_l{l}"] = np.concatenate(
+            [np.full(H, _GATE_OPEN), np.full(H, -_GATE_OPEN), np.zeros(H), np.full(H, _GATE_OPEN)]
+        ).astype(f)
+        params[f"decoder.lstm.bias_hh_l{l}"] = np.zeros(4 * H, f)
+    w = np.zeros((J, H), f)
+    w[idx, idx] = _SUPPRESS_W
+    w[bc, shared] = _LIFT_W
+    put("decoder.decoder_projector.weight", w, np.zeros(J, f))
+    w = (rng.standard_normal((V, J)) * 0.02).astype(f)
+    w[tokens] = 0.0
+    w[cfg.blank] = 0.0
+    w[tokens, idx] = _HEAD_GAIN
+    w[cfg.blank, bc] = _HEAD_GAIN
+    bias = np.full(V, _OTHER_BIAS, f)
+    bias[tokens] = 0.0
+    bias[cfg.blank] = _BLANK_BIAS
+    put("joint.head.weight", w, bias)
+    return params, tokens
+
+
+def structured_frames(rng, streams: int, frames: int, enc_hidden: int, active: int) -> np.ndarray:
+    """Encoder frames for structured_params: f32 [streams, frames, enc_hidden]
+    of N(0, 0.02) noise where each frame is silence (30 %), one token of
+    strength 2-4 (45 %: emits once, then blank), two tokens of strengths 3.5-4
+    and 2-3 (15 %: alternate up to the cap) or one strong token of 8.5-9.5
+    (10 %: repeats up to the cap)."""
+    x = (rng.standard_normal((streams, frames, enc_hidden)) * 0.02).astype(np.float32)
+    kind = rng.random((streams, frames))
+    for s in range(streams):
+        for t in range(frames):
+            a, b = rng.choice(active, size=2, replace=False)
+            if kind[s, t] < 0.30:
+                continue
+            if kind[s, t] < 0.75:
+                x[s, t, a] += rng.uniform(2.0, 4.0)
+            elif kind[s, t] < 0.90:
+                x[s, t, a] += rng.uniform(3.5, 4.0)
+                x[s, t, b] += rng.uniform(2.0, 3.0)
+            else:
+                x[s, t, a] += rng.uniform(8.5, 9.5)
+    return x
+
+
 class RnntDecoder:
     """rnnt.rs:336-388: encoder projector + prediction network + joint."""
 
@@ -182,7 +283,8 @@ class RnntDecoder:
 
     def decode_frames(self, encoded: np.ndarray, st: dict, margins: list | None = None):
         """encoded f32 [frames, enc_hidden] -> [(token, frame)] (frame local to the call).
-        `margins` collects the top-1 / top-2 logit gap of every decision."""
+        `margins` collects the top-1 / top-2 logit gap of every decision, in T
+        ulps of the top logit."""
         dec = self.prediction.step(self.cfg.blank, st)
         enc_all = self.enc_proj(encoded)
         out = []
@@ -192,7 +294,7 @@ class RnntDecoder:
                 token = int(np.argmax(logits))
                 if margins is not None:
                     top = np.sort(logits)[-2:]
-                    margins.append(float(top[1] - top[0]))
+                    margins.append(float(top[1] - top[0]) / t_ulp(top[1], self.dtype))
                 if token == self.cfg.blank:
                     break
                 out.append((token, frame))

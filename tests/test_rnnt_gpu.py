@@ -1,11 +1,15 @@
 """Batched RNNT greedy decoder on the GPU (include/cqrnnt.h) against the CPU
 restatement in oracle/rnnt_oracle.py.
 
-Greedy decisions are compared by teacher forcing: the oracle replays the GPU's
-tokens and checks every decision against its own argmax.  A differing choice
-must be a near tie (its logit within 8 T ulps of the oracle's maximum: the two
-sides sum in different orders, so logits can differ in their last bits) and
-such ties must stay rare; every other decision must be identical.
+Two kinds of checks.  Free running (test_free_running_tokens_equal_the_oracle):
+on a decoder built so that every greedy decision clears its runner-up by at
+least 8 T ulps (asserted from the oracle's logits), the GPU's token stream --
+tokens, frames and counts, chunk after chunk -- must equal the oracle's
+exactly.  Teacher forced (random weights, where the top two logits are often
+closer than the two sides' summation-order differences): the oracle replays
+the GPU's tokens and checks every decision against its own argmax; a differing
+choice must be a near tie (its logit within 8 T ulps of the oracle's maximum)
+and such ties must stay rare; every other decision must be identical.
 """
 from __future__ import annotations
 
@@ -40,6 +44,53 @@ def _check_streams(torch, state, ref, caches, enc_f32, streams, frames, dtype, t
         totals["decisions"] += stats["decisions"]
         totals["differ"] += stats["differ"]
     return paths
+
+
+def _bind(dec, params, cfg):
+    for name, (n, k, has_bias) in ro.linear_names(cfg).items():
+        q, s, b, bias = params[name]
+        dec.set_linear(name, q, s, b, bias if has_bias else None, cfg.group)
+    for name in ro.dense_names(cfg):
+        dec.set_tensor(name, params[name])
+
+
+@pytest.mark.parametrize("dtype,streams,chunks,persistent", [
+    ("bf16", 1, 4, False), ("bf16", 64, 3, False), ("f16", 1, 4, False), ("f16", 64, 3, False),
+    ("bf16", 1, 4, True)])
+def test_free_running_tokens_equal_the_oracle(cq, oracle_mod, dtype, streams, chunks, persistent):
+    """Full size (hidden 640, encoder 1024, vocab 1025, two LSTM layers, ten
+    symbols per frame).  Greedy decoding runs free on both sides -- each side
+    feeds its own tokens back -- over several chunks (the prediction state
+    crosses chunk boundaries); the token streams must be identical.  The
+    structured decoder (rnnt_oracle.structured_params) makes most frames end at
+    blank early, some alternate or repeat up to the cap; every decision's
+    top-1 / top-2 margin is at least 8 T ulps (asserted)."""
+    import torch
+    from nemotron_cuda.rnnt import Rnnt, RnntConfig
+    cfg = ro.RnntConfig()
+    params, tokens = ro.structured_params(cfg, 7, dtype)
+    dec = Rnnt(RnntConfig.default(), dtype)
+    _bind(dec, params, cfg)
+    ref = ro.RnntDecoder(cfg, params, dtype)
+    frames = 14
+    state = dec.state(streams, frames)
+    state.set_persistent(persistent)
+    caches = [ref.new_state() for _ in range(streams)]
+    rng = np.random.default_rng(100 + streams)
+    margins, emitted, capped, early = [], 0, 0, 0
+    for chunk in range(chunks):
+        enc = ro.structured_frames(rng, streams, frames, cfg.enc_hidden, len(tokens))
+        got = state.decode_chunk(_dev(torch, enc.reshape(streams * frames, -1), dtype), frames)
+        for s in range(streams):
+            want = ref.decode_frames(enc[s], caches[s], margins)
+            assert got[s] == want, (chunk, s, got[s], want)
+            per_frame = np.bincount([f for _, f in want], minlength=frames)
+            emitted += len(want)
+            capped += int((per_frame == cfg.max_symbols).sum())
+            early += int((per_frame < cfg.max_symbols).sum())
+    assert min(margins) >= 8.0, min(margins)
+    assert emitted > 0 and capped > 0 and early > capped
+    assert cq.device_status(0) == 0
 
 
 @pytest.mark.parametrize("persistent", [False, True])

@@ -72,4 +72,29 @@ def test_small_decoder_emits_bounded_symbols(oracle_mod, dtype):
     per_frame = np.bincount([f for _, f in toks], minlength=5)
     assert per_frame.max() <= cfg.max_symbols
     assert all(0 <= t < cfg.vocab and t != cfg.blank for t, _ in toks)
-    assert len(margins) >= len(toks)
+    assert len(margins) >= len(toks) and min(margins) >= 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_structured_decoder_has_wide_margins_and_early_ends(oracle_mod, dtype):
+    """The wide-margin decoder used by the exact-token GPU test: every greedy
+    decision clears the runner-up by at least 8 T ulps, most frames end at
+    blank before the symbol cap, some run to the cap, and only active tokens
+    are emitted."""
+    cfg = ro.RnntConfig()
+    params, tokens = ro.structured_params(cfg, 7, dtype)
+    dec = ro.RnntDecoder(cfg, params, dtype)
+    rng = np.random.default_rng(1)
+    states = [dec.new_state() for _ in range(3)]
+    margins, per_frame, emitted = [], [], set()
+    for _ in range(2):
+        x = ro.structured_frames(rng, 3, 14, cfg.enc_hidden, len(tokens))
+        for s, st in enumerate(states):
+            out = dec.decode_frames(x[s], st, margins)
+            per_frame += list(np.bincount([f for _, f in out], minlength=14))
+            emitted |= {t for t, _ in out}
+    per_frame = np.array(per_frame)
+    assert min(margins) >= 8.0, min(margins)
+    assert np.mean(per_frame < cfg.max_symbols) > 0.5
+    assert np.any(per_frame == cfg.max_symbols) and np.any(per_frame == 0)
+    assert emitted <= set(tokens.tolist()) and len(emitted) > 10
