@@ -1,33 +1,47 @@
 #!/usr/bin/env python
-"""Benchmark of the B200 affine INT8 quantized linear (batch-1 streaming chunk).
+"""Benchmark of the B200 affine INT8 quantized linear (batch-1 streaming chunks).
 
-Workload (one "step"): the quantized linears of all 24 FastConformer blocks
-for one 1120 ms chunk at batch 1 (M = 14 frames after 8x subsampling,
-d_model 1024, ff 4096), bf16 activations, INT8 weights with group 64 and bf16
-scale/bias, random init N(0, 0.02) quantised on the device, 24 distinct weight
-sets (~640 MB, far larger than the 126 MB L2).  Per block, in data-dependency
-order: FFN1 up (+SiLU) 1024->4096, FFN1 down 4096->1024, fused q|k|v
-1024->3072, pos-proj 1024->1024 over 2*70-1 = 139 rows, out 1024->1024,
-conv pointwise-1 1024->2048, pointwise-2 1024->1024, FFN2 up (+SiLU), FFN2
-down.  The non-linear ops between them (attention core, GLU, depthwise conv,
-LayerNorm) are not part of this workload; their inputs are stood in by the
-producing linear's output of the same shape, so every launch depends on the
-previous one as in the encoder.
+Workload (one "step"): one 60 s stream at batch 1 -- 54 chunks of 1120 ms --
+through the quantized linears of all 24 FastConformer blocks (M = 14 frames
+after 8x subsampling, d_model 1024, ff 4096), bf16 activations, INT8 weights
+with group 64 and bf16 scale/bias, random init N(0, 0.02) quantised on the
+device, 24 distinct weight sets (~640 MB, far larger than the 126 MB L2,
+re-read by every chunk).  Per block, in data-dependency order: FFN1 up
+(+SiLU) 1024->4096, FFN1 down 4096->1024, fused q|k|v 1024->3072, out
+1024->1024, conv pointwise-1 1024->2048, pointwise-2 1024->1024, FFN2 up
+(+SiLU), FFN2 down.  (The relative-position projection is not per chunk: its
+input table is constant, so the encoder projects it once when its weights are
+bound.)  The non-linear ops between the linears (attention core, GLU,
+depthwise conv, LayerNorm) are not part of this workload; their inputs are
+stood in by the producing linear's output of the same shape, so every launch
+depends on the previous one as in the encoder.
 
 metric: GB/s of algorithmic bytes (N*K weight bytes + 4*N*K/g scale/bias bytes
 + 2*M*K activation bytes + 2*M*N output bytes per linear) / device time.
 
+The line also carries:
+  linear   -- config 1: the single 4096x1024 linear at M = 14 over 40 distinct
+              weight copies, launched back to back on one stream and as four
+              independent streams, plus a sweep of N that separates K1's
+              streaming rate from its fixed cost per launch;
+  batched  -- the same 24 blocks at M = 896 (64 streams' chunks stacked: the
+              tensor-core GEMM) and the FFN-up GEMM alone;
+  encoder  -- the full streaming encoder + RNNT greedy decode at 64 streams
+              per GPU for a 60 s stream (54 chunks), the encoder alone, and
+              one stream.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 N > 1 runs under torchrun: every rank holds a full weight replica and runs its
-own stream's chunks (no data-path collective; a barrier and a max-reduction of
-the timings are the only communication).  --impl reference times the CPU
-restatement of the reference's quantized_matmul (the oracle, OpenMP C) on the
-host cores with the same metric.
+own streams (no data-path collective; a barrier and a max-reduction of the
+timings are the only communication).  --impl reference times the CPU
+restatement of the reference's quantized_matmul (the oracle, OpenMP C, all
+host cores) on the same 24-block workload with the same metric.
 """
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -45,14 +59,13 @@ GROUP = 64
 M_FRAMES = 14
 N_BLOCKS = 24
 ENCODER_LAYERS = 24
-POS_ROWS = 139
+CHUNKS_PER_STEP = 54  # a 60 s stream: ceil(60 / 1.12) chunks
 
-# name, N, K, rows, act, input (name of a producer or "x0" / "pe"), input columns used
+# name, N, K, rows, act, input (name of a producer or "x0")
 BLOCK = [
     ("ffn1_up", 4096, 1024, M_FRAMES, "silu", "x0"),
     ("ffn1_down", 1024, 4096, M_FRAMES, "none", "ffn1_up"),
     ("qkv", 3072, 1024, M_FRAMES, "none", "ffn1_down"),
-    ("pos", 1024, 1024, POS_ROWS, "none", "pe"),
     ("out", 1024, 1024, M_FRAMES, "none", "qkv"),
     ("pw1", 2048, 1024, M_FRAMES, "none", "out"),
     ("pw2", 1024, 1024, M_FRAMES, "none", "pw1"),
@@ -65,19 +78,22 @@ def linear_bytes(n: int, k: int, m: int, g: int = GROUP) -> int:
     return n * k + 4 * n * k // g + 2 * m * k + 2 * m * n
 
 
-BLOCK_BYTES = sum(linear_bytes(n, k, m) for _, n, k, m, _, _ in BLOCK)
-STEP_BYTES = N_BLOCKS * BLOCK_BYTES
-LAUNCHES_PER_STEP = N_BLOCKS * len(BLOCK)
-WORKLOAD = ("quantized linears of the 24-block FastConformer encoder for one 1120 ms chunk "
-            "at batch 1 (M=14; pos-proj M=139), bf16, INT8 group 64, 24 distinct weight sets")
+def block_bytes(rows: int = M_FRAMES) -> int:
+    return sum(linear_bytes(n, k, rows) for _, n, k, _, _, _ in BLOCK)
+
+
+CHUNK_BYTES = N_BLOCKS * block_bytes()
+LAUNCHES_PER_CHUNK = N_BLOCKS * len(BLOCK)
+WORKLOAD = ("quantized linears of the 24-block FastConformer encoder at batch 1 (M=14), one 60 s "
+            "stream = 54 chunks of 1120 ms per step, bf16, INT8 group 64, 24 distinct weight sets")
 
 
 def set_blocks(n: int) -> None:
     """Fewer blocks for small profiling captures (the workload line says so)."""
-    global N_BLOCKS, STEP_BYTES, LAUNCHES_PER_STEP, WORKLOAD
+    global N_BLOCKS, CHUNK_BYTES, LAUNCHES_PER_CHUNK, WORKLOAD
     N_BLOCKS = n
-    STEP_BYTES = N_BLOCKS * BLOCK_BYTES
-    LAUNCHES_PER_STEP = N_BLOCKS * len(BLOCK)
+    CHUNK_BYTES = N_BLOCKS * block_bytes()
+    LAUNCHES_PER_CHUNK = N_BLOCKS * len(BLOCK)
     WORKLOAD = WORKLOAD.replace("24-block", f"{n}-block").replace("24 distinct", f"{n} distinct")
 
 
@@ -85,18 +101,27 @@ def set_blocks(n: int) -> None:
 # the 4096x1024 linear at M = 14 (4.531 MB for 4.600 MB algorithmic); traffic
 # grows with the bytes a launch streams, so it is scaled to the average launch.
 K1_TRAFFIC_PER_ALGO_BYTE = 4.5312e6 / 4599808
-# The same ratio for the persistent chain kernel (qchain_kernel), from one ncu
-# capture of a 2-block chain; 1.0 until that capture is summarised.
-CHAIN_TRAFFIC_PER_ALGO_BYTE = 1.0
 
 
-def measured_tensor_peak() -> tuple[float, str]:
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+def _peaks() -> dict:
     try:
-        with open(p) as f:
-            return float(json.load(f)["bf16_tflops_sustained"]), "measured"
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
     except Exception:
-        return 1400.0, "fallback"
+        return {}
+
+
+def measured_peak() -> tuple[float, str]:
+    p = _peaks()
+    return (float(p["hbm_gbs"]), "measured") if "hbm_gbs" in p else (6650.0, "fallback")
+
+
+def measured_tensor_peak(sustained: bool = True) -> tuple[float, str]:
+    p = _peaks()
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    if key in p:
+        return float(p[key]), "measured"
+    return (1400.0 if sustained else 1590.0), "fallback"
 
 
 def max_over_ranks(dist, ms: float, device: str = "cuda") -> float:
@@ -117,13 +142,12 @@ def weak_scaling_value(world: int, units_per_rank: float, ms: float) -> float:
     return world * units_per_rank / (ms * 1e-3)
 
 
-def measured_peak() -> tuple[float, str]:
-    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+def host_threads() -> int:
+    """Host cores this process may run on (the cgroup / affinity set)."""
     try:
-        with open(p) as f:
-            return float(json.load(f)["hbm_gbs"]), "measured"
-    except Exception:
-        return 6650.0, "fallback"
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 # ----------------------------------------------------------------- clocks
@@ -188,8 +212,7 @@ class ClockSampler:
 
 class EncoderLinears:
     """Weights and activation buffers of the 24-block linear chain on one GPU.
-    rows = 14 is one stream's chunk; rows = 896 stacks 64 streams' chunks (the
-    pos-proj input is shared by all streams and keeps its 139 rows)."""
+    rows = 14 is one stream's chunk; rows = 896 stacks 64 streams' chunks."""
 
     def __init__(self, torch, cq, device: int, seed: int = 0, rows: int = M_FRAMES):
         self.torch, self.cq = torch, cq
@@ -210,85 +233,239 @@ class EncoderLinears:
         torch.cuda.synchronize()
         bf = torch.bfloat16
         self.rows = rows
-        self.spec = [(nm, n, k, rows if m == M_FRAMES else m, act, src)
-                     for nm, n, k, m, act, src in BLOCK]
+        self.spec = [(nm, n, k, rows, act, src) for nm, n, k, _, act, src in BLOCK]
         self.x0 = torch.randn((rows, 1024), generator=gen, device=dev).to(bf)
-        self.pe = torch.randn((POS_ROWS, 1024), generator=gen, device=dev).to(bf)
-        # the batch-1 chain keeps every block's outputs (no buffer reuse, so the
-        # persistent chain needs no completion waits); the batched workload
-        # reuses one set
-        sets = N_BLOCKS if rows == M_FRAMES else 1
-        self.outs = [{name: torch.empty((m, n), dtype=bf, device=dev)
-                      for name, n, _, m, _, _ in self.spec} for _ in range(sets)]
-        self.out = self.outs[-1]
+        self.out = {name: torch.empty((rows, n), dtype=bf, device=dev)
+                    for name, n, _, _, _, _ in self.spec}
+        self.final = self.out["ffn2_down"]
+        fn = cq.lib().cq_linear_forward_ex
+        self._fn = fn
+        self._calls = None
 
     def steps(self):
-        """(layer, x, y, act, rows) of every linear, in launch order."""
+        """(layer, x, y, act, rows) of every linear of one chunk, in launch order."""
         out = []
         for b, blk in enumerate(self.layers):
-            cur = self.outs[b % len(self.outs)]
-            prev = self.outs[(b - 1) % len(self.outs)]
             for layer, (name, n, k, m, act, src) in zip(blk, self.spec):
                 if src == "x0":
-                    x = self.x0 if b == 0 else prev["ffn2_down"]
-                elif src == "pe":
-                    x = self.pe
+                    x = self.x0 if b == 0 else self.out["ffn2_down"]
                 else:
-                    x = cur[src]
-                out.append((layer, x, cur[name], act, m))
+                    x = self.out[src]
+                out.append((layer, x, self.out[name], act, m))
         return out
 
-    def use_chain(self) -> None:
-        """Run every step as one persistent launch (include/cqchain.h)."""
-        self.chain = self.cq.LinearChain(self.steps())
+    def launch_chunk(self, stream_ptr: int) -> None:
+        """All 24 blocks' linears, each consuming its producer's output, as
+        C-ABI calls (cq_linear_forward_ex) with their argument tuples built
+        once."""
+        if self._calls is None or self._calls[0] != stream_ptr:
+            acts = self.cq.ACTS
+            self._calls = (stream_ptr, [
+                (layer._h, ctypes.c_void_p(x.data_ptr()), x.stride(0), m,
+                 ctypes.c_void_p(y.data_ptr()), y.stride(0), acts[act], ctypes.c_void_p(stream_ptr))
+                for layer, x, y, act, m in self.steps()])
+        fn = self._fn
+        bad = 0
+        for args in self._calls[1]:
+            bad |= fn(*args)
+        if bad:
+            raise RuntimeError("cq_linear_forward_ex failed: " + self.cq.last_error())
 
-    def launch_step(self, stream_ptr: int) -> None:
-        """All 24 blocks' linears, each consuming its producer's output."""
-        if getattr(self, "chain", None) is not None:
-            self.chain.run_raw(stream_ptr)
-            return
-        for layer, x, y, act, m in self.steps():
-            layer.forward_raw(x.data_ptr(), x.stride(0), m, y.data_ptr(), y.stride(0), act,
-                              stream_ptr)
+    def launch_step(self, stream_ptr: int, chunks: int = 1) -> None:
+        for _ in range(chunks):
+            self.launch_chunk(stream_ptr)
 
 
 class SingleLinear:
-    """Back-to-back independent launches of the single-linear workload:
-    x bf16 [14, 1024] . W[4096, 1024]^T, group 64, over 40 distinct weight
-    copies (~184 MB, larger than L2); every launch reads the same x."""
+    """Config 1: x bf16 [14, K] . W[N, K]^T, group 64, over `copies` distinct
+    weight copies (together larger than L2); every launch reads the same x and
+    writes its own output."""
 
-    COPIES = 40
-    N, K = 4096, 1024
-
-    def __init__(self, torch, cq, device: int, seed: int = 0):
+    def __init__(self, torch, cq, device: int, n: int = 4096, k: int = 1024, copies: int = 40,
+                 seed: int = 0):
         dev = torch.device("cuda", device)
         gen = torch.Generator(device=dev)
         gen.manual_seed(seed)
+        self.torch, self.cq, self.N, self.K, self.copies = torch, cq, n, k, copies
         self.layers = []
-        for _ in range(self.COPIES):
-            w = torch.randn((self.N, self.K), generator=gen, device=dev) * 0.02
+        for _ in range(copies):
+            w = torch.randn((n, k), generator=gen, device=dev) * 0.02
             q, s, b = cq.quantize(w, GROUP, "bf16")
             self.layers.append(cq.QuantizedLinear.from_device(q, s, b, None, GROUP, "bf16", device))
             del w, q, s, b
-        self.x0 = torch.randn((M_FRAMES, self.K), generator=gen, device=dev).to(torch.bfloat16)
-        self.ys = [torch.empty((M_FRAMES, self.N), dtype=torch.bfloat16, device=dev)
-                   for _ in range(2)]
-        self.final = self.ys[(self.COPIES - 1) % 2]
+        self.x0 = torch.randn((M_FRAMES, k), generator=gen, device=dev).to(torch.bfloat16)
+        self.ys = [torch.empty((M_FRAMES, n), dtype=torch.bfloat16, device=dev)
+                   for _ in range(copies)]
+        self.final = self.ys[-1]
+        self.bytes = linear_bytes(n, k, M_FRAMES)
 
-    def launch_step(self, stream_ptr: int) -> None:
+    def launch_step(self, stream_ptr: int, branches=None) -> None:
+        """One stream (branches None) or round-robin over the given streams."""
         for i, layer in enumerate(self.layers):
-            y = self.ys[i % 2]
-            layer.forward_raw(self.x0.data_ptr(), self.K, M_FRAMES, y.data_ptr(), self.N, "none",
-                              stream_ptr)
+            sp = stream_ptr if branches is None else branches[i % len(branches)]
+            layer.forward_raw(self.x0.data_ptr(), self.K, M_FRAMES, self.ys[i].data_ptr(), self.N,
+                              "none", sp)
 
 
-BATCH_ROWS = 64 * M_FRAMES  # 64 concurrent streams' chunks stacked per linear
-BATCHED_WORKLOAD = ("quantized linears of the 24-block FastConformer encoder for one 1120 ms chunk "
-                    "of 64 concurrent streams (M=896 rows per linear; pos-proj M=139), bf16, INT8 "
-                    "group 64, 24 distinct weight sets")
-LINEAR_BYTES = linear_bytes(SingleLinear.N, SingleLinear.K, M_FRAMES)
-LINEAR_WORKLOAD = ("single INT8 affine quantized linear x bf16 [14,1024] . W[4096,1024]^T, "
-                   "group 64, 40 independent back-to-back launches over distinct weight copies")
+def capture(torch, fn, stream, branches: int = 0):
+    """A CUDA graph of fn(stream_ptr) (or fn(stream_ptr, [branch stream ptrs])
+    forked over `branches` side streams and joined again)."""
+    with torch.cuda.stream(stream):
+        if branches:
+            side = [torch.cuda.Stream() for _ in range(branches)]
+            fn(stream.cuda_stream, [s.cuda_stream for s in side])  # eager warm-up
+        else:
+            fn(stream.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        if branches:
+            fork = torch.cuda.Event()
+            fork.record(stream)
+            for s in side:
+                s.wait_event(fork)
+            fn(stream.cuda_stream, [s.cuda_stream for s in side])
+            for s in side:
+                join = torch.cuda.Event()
+                join.record(s)
+                stream.wait_event(join)
+        else:
+            fn(stream.cuda_stream)
+    torch.cuda.synchronize()
+    return g
+
+
+def time_replays(torch, g, steps: int, warmup: int, dist) -> float:
+    """Device time of `steps` back-to-back replays (max over ranks), in ms."""
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    s.record(cur)
+    for _ in range(steps):
+        g.replay()
+    e.record(cur)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(dist, s.elapsed_time(e))
+    if dist:
+        dist.barrier()
+    return ms
+
+
+def hbm_roofline(bytes_per_launch: float, launch_us: float, kernel: str, note: str) -> dict:
+    peak, kind = measured_peak()
+    achieved = bytes_per_launch / (launch_us * 1e-6) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_kind": f"{kind} copy bandwidth",
+            "traffic": round(K1_TRAFFIC_PER_ALGO_BYTE * bytes_per_launch),
+            "traffic_note": "DRAM read+write bytes per launch, scaled from the ncu capture of "
+                            "the 4096x1024 linear (0.985 of algorithmic)",
+            "kernel": kernel, "avg_launch_us": round(launch_us, 3), "note": note}
+
+
+def linear_object(torch, cq, args, local_rank: int, dist) -> dict:
+    """Config 1 (the 4096x1024 linear at M = 14) and K1's streaming sweep."""
+    res = {"workload": ("single INT8 affine quantized linear x bf16 [14,1024] . W[4096,1024]^T, "
+                        "group 64, 40 distinct weight copies (184 MB, larger than L2) per step"),
+           "metric": "GB/s", "bytes_per_launch": linear_bytes(4096, 1024, M_FRAMES)}
+    lin = SingleLinear(torch, cq, local_rank)
+    stream = torch.cuda.Stream()
+    steps = max(args.steps, 20)
+    for key, branches in (("serial", 0), ("concurrent", 4)):
+        g = capture(torch, lin.launch_step, stream, branches)
+        ms = time_replays(torch, g, steps, args.warmup, dist) / steps
+        us = ms * 1e3 / lin.copies
+        res[key] = {
+            "value": round(lin.copies * lin.bytes / (ms * 1e-3) / 1e9, 2), "us_per_linear": round(us, 3),
+            "how": ("40 launches back to back on one stream (programmatic dependent launch)"
+                    if not branches else
+                    "the 40 independent launches spread over 4 streams of one graph "
+                    "(fork / join), so launches overlap")}
+        del g
+    res["roofline"] = hbm_roofline(lin.bytes, res["concurrent"]["us_per_linear"], "qgemv_kernel (K1)",
+                                   "per-linear time of the concurrent launches")
+    del lin
+    # streaming sweep: per-launch time against bytes, serial launches over
+    # enough distinct copies to exceed L2 twice
+    pts = []
+    for n in (4096, 16384, 65536):
+        b = linear_bytes(n, 1024, M_FRAMES)
+        copies = max(3, -(-260_000_000 // b))
+        lin = SingleLinear(torch, cq, local_rank, n=n, copies=copies, seed=n)
+        g = capture(torch, lin.launch_step, stream)
+        ms = time_replays(torch, g, max(10, steps // 2), args.warmup, dist)
+        pts.append((b, ms * 1e3 / max(10, steps // 2) / copies))
+        del g, lin
+    xs, ys = [p[0] for p in pts], [p[1] for p in pts]
+    xm, ym = sum(xs) / len(xs), sum(ys) / len(ys)
+    slope = sum((x - xm) * (y - ym) for x, y in zip(xs, ys)) / sum((x - xm) ** 2 for x in xs)
+    peak, kind = measured_peak()
+    stream_gbs = 1e-3 / slope if slope > 0 else None  # bytes per us -> GB/s
+    res["sweep"] = {
+        "points": [{"N": n, "bytes": b, "us_per_launch": round(t, 3), "GB_per_s": round(b / t / 1e3, 1)}
+                   for n, (b, t) in zip((4096, 16384, 65536), pts)],
+        "streaming_GB_per_s": round(stream_gbs, 1) if stream_gbs else None,
+        "streaming_frac": round(stream_gbs / peak, 4) if stream_gbs else None,
+        "fixed_us_per_launch": round(ym - slope * xm, 3),
+        "how": "K = 1024, M = 14, serial launches; least-squares line through (bytes, us): the "
+               "slope is K1's streaming rate, the intercept its fixed cost per launch"}
+    return res
+
+
+def batched_object(torch, cq, args, local_rank: int, dist) -> dict:
+    """The 24 blocks at M = 896 (64 streams' chunks stacked: K2) and the FFN-up
+    GEMM alone."""
+    rows = 64 * M_FRAMES
+    enc = EncoderLinears(torch, cq, local_rank, rows=rows)
+    stream = torch.cuda.Stream()
+    g = capture(torch, enc.launch_step, stream)
+    steps = max(args.steps, 20)
+    ms = time_replays(torch, g, steps, args.warmup, dist) / steps
+    flops = N_BLOCKS * sum(2 * rows * n * k for _, n, k, _, _, _ in BLOCK)
+    tpeak, tkind = measured_tensor_peak(sustained=True)
+    tf = flops / (ms * 1e-3) / 1e12
+    res = {"workload": ("quantized linears of the 24-block FastConformer encoder for one chunk of "
+                        "64 concurrent streams (M=896 rows per linear), bf16, INT8 group 64"),
+           "ms_per_chunk": round(ms, 4), "tflops": round(tf, 2),
+           "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": tpeak, "unit": "TFLOP/s",
+                        "frac": round(tf / tpeak, 4), "peak_kind": f"{tkind} dense bf16 (sustained)",
+                        "kernel": "qgemm_kernel (K2) + activation prepass",
+                        "note": "all 192 linears of the chunk, one CUDA graph"}}
+    del g, enc
+    # FFN up alone: 32 distinct weight copies (145 MB) back to back
+    copies = 32
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(5)
+    layers = []
+    for _ in range(copies):
+        w = torch.randn((4096, 1024), generator=gen, device="cuda") * 0.02
+        q, s, b = cq.quantize(w, GROUP, "bf16")
+        L = cq.QuantizedLinear.from_device(q, s, b, None, GROUP, "bf16", local_rank)
+        L.reserve(rows)
+        layers.append(L)
+    x = torch.randn((rows, 1024), generator=gen, device="cuda").to(torch.bfloat16)
+    y = torch.empty((rows, 4096), dtype=torch.bfloat16, device="cuda")
+
+    def run(sp):
+        for L in layers:
+            L.forward_raw(x.data_ptr(), 1024, rows, y.data_ptr(), 4096, "silu", sp)
+
+    g = capture(torch, run, stream)
+    ms = time_replays(torch, g, steps, args.warmup, dist) / steps / copies
+    bpeak, bkind = measured_tensor_peak(sustained=False)
+    tf = 2 * rows * 4096 * 1024 / (ms * 1e-3) / 1e12
+    res["ffn_up"] = {"shape": "M=896 x N=4096 x K=1024, SiLU epilogue", "us_per_call": round(ms * 1e3, 3),
+                     "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": bpeak,
+                                  "unit": "TFLOP/s", "frac": round(tf / bpeak, 4),
+                                  "peak_kind": f"{bkind} dense bf16 (burst)",
+                                  "kernel": "qgemm_kernel (K2) + activation prepass",
+                                  "note": "32 distinct weight copies (145 MB) back to back"}}
+    del g, layers
+    return res
 
 
 CHUNK_MEL = 112          # log-mel frames per chunk (lookahead 13: 8 * (13 + 1))
@@ -299,11 +476,10 @@ ENC_STREAMS = 64         # concurrent streams per GPU (64 x 14 = 896 rows per li
 def encoder_flops_per_chunk(streams: int) -> int:
     """Algorithmic FLOPs (2 * rows * N * K) of every quantized linear in one
     chunk of `streams` streams: 24 blocks, subsampling and prompt projector.
-    The position projection (83 rows) is shared by the streams of a state."""
+    (The position projection is made once per state, not per chunk.)"""
     q = 14
     block = (2 * 4096 * 1024 * 2 + 3072 * 1024 + 1024 * 1024 + 2048 * 1024 + 1024 * 1024)
     f = streams * q * block * ENCODER_LAYERS
-    f += (56 + 14 + 14 - 1) * 1024 * 1024 * ENCODER_LAYERS  # relative_k_proj
     f += streams * (28 * 33 * 256 * 256 + 14 * 17 * 256 * 256 + q * 4352 * 1024)
     f += streams * q * (1152 * 2048 + 2048 * 1024)
     return 2 * f
@@ -609,6 +785,7 @@ def cpu_encoder_baseline(target_s: float = 8.0, with_rnnt: bool = True) -> dict:
     import encoder_oracle as eo
     import oracle
     import rnnt_oracle as ro
+    oracle.set_threads(host_threads())
     cfg = eo.EncoderConfig()
     enc = eo.Encoder(cfg, eo.random_params(cfg, 3, "bf16"), "bf16")
     cache = enc.new_cache()
@@ -703,75 +880,81 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                            "parallelism": f"dp{world} (replicated weights, independent streams)",
                            "l2": "weights (7.6 MB) L2-resident; every step reads them again"},
                 "e2e": res["e2e"], "clocks": res["clocks"], "gpu_launches": res["gpu_launches"]}
-    step_flops = None
     if args.workload == "linear":
-        enc = SingleLinear(torch, cq, local_rank)
-        step_bytes, launches, workload = LINEAR_BYTES * SingleLinear.COPIES, SingleLinear.COPIES, LINEAR_WORKLOAD
-        in_shape = (M_FRAMES, SingleLinear.K)
-    elif args.workload == "batched":
-        enc = EncoderLinears(torch, cq, local_rank, rows=BATCH_ROWS)
-        step_bytes = N_BLOCKS * sum(linear_bytes(n, k, m) for _, n, k, m, _, _ in enc.spec)
-        step_flops = N_BLOCKS * sum(2 * m * n * k for _, n, k, m, _, _ in enc.spec)
-        launches, workload = LAUNCHES_PER_STEP, BATCHED_WORKLOAD
-        in_shape = (BATCH_ROWS, 1024)
-    else:
-        enc = EncoderLinears(torch, cq, local_rank)
-        step_bytes, launches, workload = STEP_BYTES, LAUNCHES_PER_STEP, WORKLOAD
-        in_shape = (M_FRAMES, 1024)
-        if args.chain:
-            enc.use_chain()
-            launches = 1
+        res = linear_object(torch, cq, args, local_rank, dist)
+        if dist:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        best = res["concurrent"]
+        return {"metric": "INT8 qlinear HBM GB/s (M=14)", "value": best["value"], "unit": UNIT,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(best["us_per_linear"] * 40 / 1e3, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (random-init INT8 weights N(0,0.02) quantised on device)",
+                "config": {"workload": res["workload"], "group_size": GROUP,
+                           "l2": "inputs larger than L2 (184 MB of distinct weights per step)"},
+                "roofline": res["roofline"], "linear": res, "gpu_launches": 40 * args.steps}
+    if args.workload == "batched":
+        res = batched_object(torch, cq, args, local_rank, dist)
+        if dist:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        return {"metric": "INT8 qlinear TFLOP/s (M=896)", "value": res["tflops"], "unit": "TFLOP/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": res["ms_per_chunk"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": res["workload"], "group_size": GROUP,
+                           "l2": "inputs larger than L2 (640 MB of weights per step)"},
+                "roofline": res["roofline"], "batched": res}
 
-    # eager warm-up (sets kernel attributes before capture), then capture.
+    # ---- default: the batch-1 chain, one 60 s stream (54 chunks) per step
+    enc = EncoderLinears(torch, cq, local_rank)
+    chunks = args.chunks_per_step
+    step_bytes, launches = CHUNK_BYTES * chunks, LAUNCHES_PER_CHUNK * chunks
     stream = torch.cuda.Stream()
-    with torch.cuda.stream(stream):
-        enc.launch_step(stream.cuda_stream)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        enc.launch_step(stream.cuda_stream)
-    # end-to-end graph: pinned host input -> device, chain, device -> pinned host
-    final = enc.final if args.workload == "linear" else enc.out["ffn2_down"]
-    host_in = torch.empty(in_shape, dtype=torch.bfloat16).pin_memory()
-    host_in.copy_(enc.x0.cpu())
-    host_out = torch.empty(tuple(final.shape), dtype=torch.bfloat16).pin_memory()
-    graph_e2e = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph_e2e, stream=stream):
-        enc.x0.copy_(host_in, non_blocking=True)
-        enc.launch_step(stream.cuda_stream)
-        host_out.copy_(final, non_blocking=True)
-    torch.cuda.synchronize()
-
-    def timed(g) -> float:
-        for _ in range(args.warmup):
-            g.replay()
-        torch.cuda.synchronize()
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        cur = torch.cuda.current_stream()
-        s.record(cur)
-        for _ in range(args.steps):
-            g.replay()
-        e.record(cur)
-        torch.cuda.synchronize()
-        ms = s.elapsed_time(e)
-        ms = max_over_ranks(dist, ms)
-        if dist:
-            dist.barrier()
-        return ms
+    graph = capture(torch, lambda sp: enc.launch_step(sp, chunks), stream)
 
     clocks = ClockSampler(local_rank)
     clocks.start()
-    ms = timed(graph)
+    ms = time_replays(torch, graph, args.steps, args.warmup, dist)
     clock_info = clocks.stop()
-    ms_e2e = timed(graph_e2e)
-    status = cq.device_status(local_rank)
+    del graph
 
-    del graph, graph_e2e
-    encoder = None
-    if args.workload == "block" and not args.no_encoder:
+    # end to end: every chunk copies its input from pinned host memory, calls
+    # the C ABI once per linear (no graph: the host cost of each call is in
+    # the timed region) and reads the chunk's output back to pinned memory
+    host_in = torch.empty((M_FRAMES, 1024), dtype=torch.bfloat16).pin_memory()
+    host_in.copy_(enc.x0.cpu())
+    host_out = torch.empty((M_FRAMES, 1024), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_steps(n: int) -> None:
+        with torch.cuda.stream(stream):
+            for _ in range(n * chunks):
+                enc.x0.copy_(host_in, non_blocking=True)
+                enc.launch_chunk(stream.cuda_stream)
+                host_out.copy_(enc.final, non_blocking=True)
+
+    e2e_steps(args.warmup)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    e2e_steps(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(dist, e0.elapsed_time(e1))
+    status = cq.device_status(local_rank)
+    del enc
+
+    linear = batched = encoder = None
+    if not args.no_extras:
+        linear = linear_object(torch, cq, args, local_rank, dist)
+        batched = batched_object(torch, cq, args, local_rank, dist)
+    if not args.no_encoder:
         encoder = bench_encoder(torch, cq, args, world, local_rank, dist, ENC_STREAMS,
                                 args.encoder_chunks, with_rnnt=True)
         for key, streams in (("encoder_only", ENC_STREAMS), ("batch1", 1)):
@@ -788,57 +971,36 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
     ms_step = ms / args.steps
     value = weak_scaling_value(world, step_bytes, ms_step) / 1e9
     value_e2e = weak_scaling_value(world, step_bytes, ms_e2e / args.steps) / 1e9
-    peak, peak_kind = measured_peak()
     per_launch_us = ms_step * 1e3 / launches
-    achieved = (step_bytes / launches) / (per_launch_us * 1e-6) / 1e9
-    roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_kind": f"{peak_kind} copy bandwidth",
-                "traffic": round(K1_TRAFFIC_PER_ALGO_BYTE * step_bytes / launches),
-                "traffic_note": "bytes per launch, scaled from the ncu capture of the 4096x1024 "
-                                "linear (dram read+write / algorithmic = 0.985)",
-                "kernel": "qgemv_kernel (K1)", "avg_launch_us": round(per_launch_us, 3)}
-    chained = getattr(enc, "chain", None) is not None
-    if chained:
-        roofline.update({
-            "traffic": round(CHAIN_TRAFFIC_PER_ALGO_BYTE * step_bytes),
-            "traffic_note": "bytes per launch, scaled by blocks from the ncu capture of a "
-                            "2-block chain (dram read+write / algorithmic bytes)",
-            "kernel": "qchain_kernel (persistent linear chain, one launch per step)"})
-    if step_flops is not None:
-        tpeak, tkind = measured_tensor_peak()
-        tflops = step_flops / (ms_step * 1e-3) / 1e12
-        roofline = {"bound": "tensor", "achieved": round(tflops, 2), "peak": tpeak,
-                    "unit": "TFLOP/s", "frac": round(tflops / tpeak, 4),
-                    "peak_kind": f"{tkind} dense bf16 (sustained: a step is a long run)",
-                    "traffic": None, "kernel": "qgemm_kernel (K2)",
-                    "avg_launch_us": round(per_launch_us, 3)}
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (random-init INT8 weights N(0,0.02) quantised on device; bf16 x ~ N(0,1))",
-        "config": {"workload": workload, "group_size": GROUP, "rows": M_FRAMES,
-                   "bytes_per_step_per_gpu": step_bytes, "launches_per_step": launches,
-                   "l2": "inputs larger than L2 (distinct weights per step exceed 126 MB)",
+        "config": {"workload": WORKLOAD, "group_size": GROUP, "rows": M_FRAMES,
+                   "chunks_per_step": chunks, "bytes_per_chunk_per_gpu": CHUNK_BYTES,
+                   "launches_per_chunk": LAUNCHES_PER_CHUNK,
+                   "l2": "inputs larger than L2 (every chunk re-reads 640 MB of distinct weights)",
                    "parallelism": f"dp{world} (replicated weights, independent streams)",
-                   "graph": ("one CUDA graph per step holding one persistent cooperative "
-                             "launch of all 216 linears" if chained else
-                             "one CUDA graph per step, programmatic dependent launch edges")},
+                   "graph": "one CUDA graph per step (54 chunks x 192 linears), programmatic "
+                            "dependent launch edges"},
         "e2e": {"value": round(value_e2e, 2), "unit": UNIT,
-                "h2d_bytes_per_step": host_in.numel() * 2,
-                "d2h_bytes_per_step": host_out.numel() * 2,
-                "path": ("C-ABI cq_linear_chain_run" if chained else
-                         "C-ABI cq_linear_forward_ex calls") +
-                        " captured in a CUDA graph with the pinned-host input copy and output "
-                        "read inside the timed region"},
+                "h2d_bytes_per_step": host_in.numel() * 2 * chunks,
+                "d2h_bytes_per_step": host_out.numel() * 2 * chunks,
+                "path": "per chunk: pinned host input -> device, one C-ABI cq_linear_forward_ex call "
+                        "per linear (eager, no graph), output -> pinned host; all inside the timed "
+                        "region"},
         "gpu_launches": launches * args.steps,
-        "roofline": roofline,
+        "roofline": hbm_roofline(step_bytes / launches, per_launch_us, "qgemv_kernel (K1)",
+                                 "the dependent batch-1 chain: average bytes and device time per "
+                                 "linear"),
         "clocks": clock_info,
     }
-    if step_flops is not None:
-        line["tflops"] = round(step_flops / (ms_step * 1e-3) / 1e12 * world, 2)
-    if world == 1 and not args.no_cpu_baseline and args.workload != "batched":
-        line["cpu_baseline"] = cpu_baseline(target_s=args.cpu_seconds, workload=args.workload)
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(target_s=args.cpu_seconds)
+    if linear is not None:
+        line["linear"] = linear
+        line["batched"] = batched
     if encoder is not None:
         if world == 1 and not args.no_cpu_baseline:
             encoder["cpu_baseline"] = cpu_encoder_baseline(args.cpu_seconds)
@@ -849,82 +1011,87 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
 # ----------------------------------------------------------------- CPU arms
 
 
-class OracleBlocks:
-    """Host copies of a few blocks' packed weights for the CPU restatement
-    (workload "linear": each block is the single 4096x1024 linear)."""
+class OracleChain:
+    """The 24-block chain on the host for the CPU restatement: every block's
+    weights drawn N(0, 0.02) and quantised by the oracle's quantiser (the same
+    algorithm, bit for bit, as the device quantiser of the GPU arm), bf16."""
 
-    def __init__(self, n_blocks: int, seed: int = 1, workload: str = "block"):
+    def __init__(self, seed: int = 1, blocks: int | None = None):
         import numpy as np
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle
         self.oracle = oracle
+        oracle.set_threads(host_threads())
         rng = np.random.default_rng(seed)
-        self.spec = BLOCK if workload == "block" else [
-            ("linear", SingleLinear.N, SingleLinear.K, M_FRAMES, "none", "x0")]
-        self.bytes = sum(linear_bytes(n, k, m) for _, n, k, m, _, _ in self.spec)
         self.blocks = []
-        for _ in range(n_blocks):
+        for _ in range(N_BLOCKS if blocks is None else blocks):
             blk = []
-            for _, n, k, m, act, _ in self.spec:
-                q = rng.integers(0, 256, size=(n, k), dtype=np.uint8).view(np.uint32)
-                s = oracle.to_t((rng.random((n, k // GROUP)) * 1e-3).astype(np.float32), "bf16")
-                b = oracle.to_t((rng.random((n, k // GROUP)) * -0.1).astype(np.float32), "bf16")
-                blk.append((q, s, b))
+            for _, n, k, _, _, _ in BLOCK:
+                w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+                blk.append(oracle.quantize(w, GROUP, "bf16"))
             self.blocks.append(blk)
-        self.x = {name: oracle.to_t(rng.standard_normal((m, k)).astype(np.float32), "bf16")
-                  for name, n, k, m, _, _ in self.spec}
+        self.x0 = oracle.to_t(rng.standard_normal((M_FRAMES, 1024)).astype(np.float32), "bf16")
+        self.bytes = len(self.blocks) * block_bytes()
 
-    def run_block(self, i: int) -> None:
-        for (q, s, b), (name, n, k, m, act, _) in zip(self.blocks[i % len(self.blocks)], self.spec):
-            self.oracle.qmatmul(self.x[name], q, s, b, GROUP, "bf16", None, act)
+    def run_chunk(self) -> None:
+        O = self.oracle
+        outs = {}
+        for b, blk in enumerate(self.blocks):
+            for (q, s, sb), (name, n, k, m, act, src) in zip(blk, BLOCK):
+                x = (self.x0 if b == 0 else outs["ffn2_down"]) if src == "x0" else outs[src]
+                outs[name] = O.qmatmul(x, q, s, sb, GROUP, "bf16", None, act)
 
 
-def cpu_baseline(target_s: float = 12.0, workload: str = "block") -> dict:
-    ob = OracleBlocks(4 if workload == "block" else 40, workload=workload)
-    ob.run_block(0)  # warm
+def cpu_baseline(target_s: float = 12.0) -> dict:
+    ob = OracleChain()
+    ob.run_chunk()  # warm
     t0 = time.perf_counter()
     n = 0
     while True:
-        ob.run_block(n)
+        ob.run_chunk()
         n += 1
         if time.perf_counter() - t0 >= target_s and n >= 2:
             break
     dt = time.perf_counter() - t0
-    what = ("blocks x 9 linears (M=14, pos M=139) rotating over 4 weight sets"
-            if workload == "block" else "4096x1024 linears (M=14) rotating over 40 weight sets")
     return {"value": round(n * ob.bytes / dt / 1e9, 3), "unit": UNIT,
             "cores": ob.oracle.max_threads(), "kind": "port",
-            "sample": f"{n} {what}, {dt:.1f} s, OpenMP C restatement of quantized_matmul "
-                      f"(oracle/)"}
+            "sample": f"{n} chunks of the 24-block chain (192 linears, M=14, 640 MB of weights), "
+                      f"{dt:.1f} s, OpenMP C restatement of quantized_matmul (oracle/)"}
 
 
 def run_reference(args, rank: int) -> dict | None:
     if rank != 0:
         return None
-    ob = OracleBlocks(4 if args.workload == "block" else 40, workload=args.workload)
-    reps = 1 if args.workload == "block" else SingleLinear.COPIES
-    for i in range(args.warmup):
-        ob.run_block(i)
+    ob = OracleChain()
+    for _ in range(args.warmup):
+        ob.run_chunk()
     t0 = time.perf_counter()
-    for i in range(args.steps * reps):
-        ob.run_block(i)
+    for _ in range(args.steps):
+        ob.run_chunk()
     dt = time.perf_counter() - t0
-    value = args.steps * reps * ob.bytes / dt / 1e9
+    value = args.steps * ob.bytes / dt / 1e9
     enc = None if args.no_encoder else cpu_encoder_baseline(args.cpu_seconds)
+    cores = ob.oracle.max_threads()
     return {
         "encoder": enc,
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD if args.workload == "block" else LINEAR_WORKLOAD,
-                   "group_size": GROUP, "rows": M_FRAMES,
-                   "step": ("one block's 9 linears (1/24 of the GPU arm's step; same metric)"
-                            if args.workload == "block" else "40 linears, as the GPU arm")},
-        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": ob.oracle.max_threads(),
-                         "kind": "port",
-                         "sample": "OpenMP C restatement of MLX quantized_matmul (oracle/); "
-                                   "MLX itself cannot run on this host"},
+        "data": "synthetic (random-init INT8 weights N(0,0.02); bf16 x ~ N(0,1))", "impl": "reference",
+        "config": {"workload": WORKLOAD, "group_size": GROUP, "rows": M_FRAMES,
+                   "chunks_per_step": args.chunks_per_step, "bytes_per_chunk_per_gpu": CHUNK_BYTES,
+                   "launches_per_chunk": LAUNCHES_PER_CHUNK,
+                   "l2": "inputs larger than L2 (every chunk re-reads 640 MB of distinct weights)",
+                   "parallelism": f"dp{args.gpus} (replicated weights, independent streams)",
+                   "graph": "one CUDA graph per step (54 chunks x 192 linears), programmatic "
+                            "dependent launch edges"},
+        "sample": "each step is one chunk of the 24-block chain (1/54 of the GPU arm's step; the "
+                  "metric is a rate, so the values compare)",
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} chunks of the 24-block chain (192 linears, M=14, "
+                                   f"640 MB of weights), {dt:.1f} s, OpenMP C restatement of MLX "
+                                   f"quantized_matmul (oracle/) on {cores} host threads; MLX itself "
+                                   f"cannot run on this host"},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -938,29 +1105,31 @@ def main() -> None:
     sys.stdout = sys.stderr
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["block", "linear", "batched", "encoder", "rnnt", "logmel"],
                     default="block",
-                    help="block: the 24-block M=14 linear chain (default, plus the full "
-                         "encoder at 64 streams and at 1 stream as the line's 'encoder' "
-                         "object); linear: one 4096x1024 linear, independent back-to-back "
-                         "launches; batched: the 24-block chain at M=896 (64 streams), "
-                         "tensor-core path; encoder: the full streaming encoder alone "
-                         "(value in audio-s/s); rnnt: the batched RNNT greedy decoder alone; "
-                         "logmel: the GPU log-mel frontend alone")
+                    help="block: the 24-block M=14 linear chain, one 60 s stream per step "
+                         "(default; the line also carries the 'linear', 'batched' and 'encoder' "
+                         "objects); linear: config 1 alone (one 4096x1024 linear, serial and "
+                         "concurrent launches, N sweep); batched: the 24-block chain at M=896 "
+                         "(64 streams, tensor-core path) and the FFN-up GEMM; encoder: the full "
+                         "streaming encoder alone (value in audio-s/s); rnnt: the batched RNNT "
+                         "greedy decoder alone; logmel: the GPU log-mel frontend alone")
     ap.add_argument("--streams", type=int, default=ENC_STREAMS,
                     help="streams per GPU of the encoder, rnnt and logmel workloads")
-    ap.add_argument("--encoder-chunks", type=int, default=20,
-                    help="timed chunks of the encoder measurement in the default run")
+    ap.add_argument("--chunks-per-step", type=int, default=CHUNKS_PER_STEP,
+                    help="chunks of the batch-1 chain per step (54: one 60 s stream)")
+    ap.add_argument("--encoder-chunks", type=int, default=CHUNKS_PER_STEP,
+                    help="timed chunks of the encoder measurement in the default run (54: a "
+                         "60 s stream per stream)")
     ap.add_argument("--no-encoder", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default run without the 'linear' and 'batched' objects")
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,
                     help="FastConformer blocks in the linear workloads (24 in the encoder; "
                          "fewer only for small profiling captures)")
-    ap.add_argument("--chain", action="store_true",
-                    help="block workload: the persistent linear chain (one launch per step) "
-                         "instead of one K1 launch per linear")
     ap.add_argument("--no-rnnt", action="store_true",
                     help="encoder workload without the RNNT decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")

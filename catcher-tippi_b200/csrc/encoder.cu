@@ -385,7 +385,7 @@ EncoderState::EncoderState(Encoder& enc, int streams, int max_mel_frames)
   scale16_ = DeviceBuffer(S * Q * sizeof(float));
   qkv_ = DeviceBuffer(S * Q * 3 * D * es);
   pin_ = DeviceBuffer(S * Q * (D + c.num_prompts) * es);
-  relk_ = DeviceBuffer(static_cast<size_t>(pmax_) * D * es);
+  relk_ = DeviceBuffer(L * static_cast<size_t>(pmax_) * D * es);  // per layer, projected once
   pos_table_ = DeviceBuffer(static_cast<size_t>(pmax_) * D * es);
   kring_ = DeviceBuffer(L * S * ring_ * D * es);
   vring_ = DeviceBuffer(L * S * ring_ * D * es);
@@ -433,6 +433,15 @@ EncoderState::EncoderState(Encoder& enc, int streams, int max_mel_frames)
              "upload positions");
   check_cuda(cq::launch_f32_to_t(enc_.dtype(), tmp.as<float>(), table.size(), pos_table_.get(), nullptr),
              "round positions");
+  // relative_k_proj of the position table (encoder.rs:262-264): the table
+  // depends only on the position values and the weights are fixed once a
+  // state exists, so every layer's projection is made here, once, instead of
+  // in every chunk (same kernel and inputs: the same bits)
+  for (size_t l = 0; l < L; ++l)
+    enc_.blocks()[l].pos->forward_array(pos_table_.get(), static_cast<int>(D), pmax_,
+                                        static_cast<char*>(relk_.get()) + l * pmax_ * D * es,
+                                        static_cast<int>(D), CQ_ACT_NONE, nullptr);
+  check_cuda(cudaDeviceSynchronize(), "position projections");
   check_cuda(cudaStreamCreateWithFlags(&capture_stream_, cudaStreamNonBlocking), "capture stream");
   reset();
   std::vector<int> ids(S_, c.num_prompts > 101 ? 101 : 0);
@@ -605,11 +614,10 @@ void EncoderState::launch_chunk(const float* mel, const Geometry& g, void* out, 
     add_ln(0.5f, b.norm_att_w, b.norm_att_b);
     // self-attention
     block_linear(b.qkv, xn_.get(), D, qkv_.get(), 3 * D, CQ_ACT_NONE);
-    linear(b.pos, pos_table_.get(), D, pmax_, relk_.get(), D, CQ_ACT_NONE, st);
     cq::AttnArgs at{};
     at.qkv = qkv_.get();
     at.ldqkv = 3 * D;
-    at.relk = relk_.get();
+    at.relk = static_cast<const char*>(relk_.get()) + static_cast<size_t>(l) * pmax_ * D * es;
     at.bias_u = b.bias_u;
     at.bias_v = b.bias_v;
     at.kring = static_cast<char*>(kring_.get()) + static_cast<size_t>(l) * S * ring_ * D * es;

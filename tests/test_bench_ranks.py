@@ -86,5 +86,22 @@ def test_reference_arm_works_on_rank_zero_only():
 
     import bench
     args = argparse.Namespace(workload="block", warmup=3, steps=1, gpus=2, no_encoder=True,
-                              cpu_seconds=0.1)
+                              cpu_seconds=0.1, chunks_per_step=54)
     assert bench.run_reference(args, rank=1) is None
+
+
+def test_reference_arm_uses_every_host_core_under_torchrun_settings():
+    """torchrun sets OMP_NUM_THREADS=1 in every rank; the reference arm still
+    times the oracle on all the host cores it may use, and reports them."""
+    import json
+    import subprocess
+    env = dict(os.environ, OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                        "--blocks", "1", "--steps", "1", "--warmup", "3", "--no-encoder"],
+                       env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    cores = len(os.sched_getaffinity(0))
+    assert line["impl"] == "reference" and line["cpu_baseline"]["cores"] == cores
+    assert line["cpu_baseline"]["kind"] == "port" and line["value"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["config"]["chunks_per_step"] == 54
