@@ -880,6 +880,26 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> dict | None:
                            "parallelism": f"dp{world} (replicated weights, independent streams)",
                            "l2": "weights (7.6 MB) L2-resident; every step reads them again"},
                 "e2e": res["e2e"], "clocks": res["clocks"], "gpu_launches": res["gpu_launches"]}
+    if args.workload == "linear" and args.linear_n:
+        # one N alone, serial launches (for profiling captures of K1 at large N)
+        b = linear_bytes(args.linear_n, 1024, M_FRAMES)
+        copies = max(3, -(-260_000_000 // b))
+        lin = SingleLinear(torch, cq, local_rank, n=args.linear_n, copies=copies)
+        g = capture(torch, lin.launch_step, torch.cuda.Stream())
+        ms = time_replays(torch, g, args.steps, args.warmup, dist)
+        us = ms * 1e3 / args.steps / copies
+        if dist:
+            dist.destroy_process_group()
+        if rank != 0:
+            return None
+        return {"metric": "INT8 qlinear HBM GB/s (M=14)", "value": round(b / us / 1e3, 2),
+                "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"x bf16 [14,1024] . W[{args.linear_n},1024]^T, group 64, "
+                                       f"{copies} distinct weight copies, serial launches"},
+                "roofline": hbm_roofline(b, us, "qgemv_kernel (K1)", "serial launches"),
+                "gpu_launches": copies * args.steps}
     if args.workload == "linear":
         res = linear_object(torch, cq, args, local_rank, dist)
         if dist:
@@ -1130,6 +1150,9 @@ def main() -> None:
     ap.add_argument("--blocks", type=int, default=N_BLOCKS,
                     help="FastConformer blocks in the linear workloads (24 in the encoder; "
                          "fewer only for small profiling captures)")
+    ap.add_argument("--linear-n", type=int, default=0,
+                    help="linear workload: only serial launches of x[14,1024] . W[N,1024]^T "
+                         "(profiling captures of K1 at large N)")
     ap.add_argument("--no-rnnt", action="store_true",
                     help="encoder workload without the RNNT decode")
     ap.add_argument("--no-cpu-baseline", action="store_true")
