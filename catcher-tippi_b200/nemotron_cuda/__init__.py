@@ -64,6 +64,7 @@ def lib() -> ctypes.CDLL:
         "cq_quantize": ([vp, i32, i32, i32, i32, i32, vp, vp, vp, vp], i32),
         "cq_dequantize": ([vp, vp, vp, i32, i32, i32, i32, vp, vp], i32),
         "cq_device_status": ([i32, ctypes.POINTER(ctypes.c_int32)], i32),
+        "cq_device_watchdog_check": ([i32], i32),
         # streaming encoder (include/cqencoder.h)
         "cq_encoder_default_config": ([vp], None),
         "cq_encoder_create": ([vp, i32, i32, pp], i32),
@@ -136,6 +137,32 @@ def lib() -> ctypes.CDLL:
         "cq_logmel_filters": ([vp, vp, sz], i32),
         "cq_logmel_extract": ([vp, vp, i32, ctypes.c_int64, ctypes.c_int64, i32, vp, vp], i32),
         "cq_logmel_destroy": ([vp], None),
+        # streaming scheduler and tokenizer (include/cqstream.h)
+        "cq_chunk_scheduler_create": ([i32, pp], i32),
+        "cq_chunk_scheduler_push": ([vp, vp, sz, ctypes.POINTER(ctypes.c_int32)], i32),
+        "cq_chunk_scheduler_finish": ([vp, ctypes.POINTER(ctypes.c_int32)], i32),
+        "cq_chunk_scheduler_window": ([vp, i32, vp, sz, ctypes.POINTER(ctypes.c_size_t),
+                                       ctypes.POINTER(ctypes.c_int32),
+                                       ctypes.POINTER(ctypes.c_int32)], i32),
+        "cq_chunk_scheduler_reset": ([vp], i32),
+        "cq_chunk_scheduler_destroy": ([vp], None),
+        "cq_tokenizer_from_json": ([ctypes.c_char_p, ctypes.c_uint32, ctypes.c_uint32, pp], i32),
+        "cq_tokenizer_decode": ([vp, vp, sz, i32, ctypes.POINTER(ctypes.c_char_p)], i32),
+        "cq_tokenizer_destroy": ([vp], None),
+        # transcription ABI (include/catcher.h)
+        "catcher_create": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint32], vp),
+        "catcher_create_config": ([ctypes.c_char_p, ctypes.c_char_p, ctypes.c_uint32, vp, vp, i32,
+                                   i32], vp),
+        "catcher_start": ([vp], i32),
+        "catcher_push_audio": ([vp, vp, sz], i32),
+        "catcher_finish": ([vp], i32),
+        "catcher_finish_before": ([vp, ctypes.c_uint64], i32),
+        "catcher_text": ([vp], ctypes.c_char_p),
+        "catcher_text_before": ([vp, ctypes.c_uint64], ctypes.c_char_p),
+        "catcher_segments": ([vp], ctypes.c_char_p),
+        "catcher_warning": ([vp], ctypes.c_char_p),
+        "catcher_last_error": ([vp], ctypes.c_char_p),
+        "catcher_destroy": ([vp], None),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

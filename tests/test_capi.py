@@ -23,7 +23,7 @@ def declared_symbols() -> set[str]:
             continue
         text = open(os.path.join(inc, f)).read()
         text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-        for m in re.finditer(r"\b(cq_[a-z0-9_]+)\s*\(", text):
+        for m in re.finditer(r"\b((?:cq|catcher)_[a-z0-9_]+)\s*\(", text):
             names.add(m.group(1))
     return names
 
@@ -31,7 +31,9 @@ def declared_symbols() -> set[str]:
 def test_header_declares_the_boundary():
     names = declared_symbols()
     for required in ("cq_linear_create", "cq_linear_forward", "cq_linear_forward_f32",
-                     "cq_linear_destroy", "cq_last_error", "cq_quantized_matmul"):
+                     "cq_linear_destroy", "cq_last_error", "cq_quantized_matmul",
+                     "catcher_create", "catcher_push_audio", "catcher_finish", "catcher_text",
+                     "catcher_last_error", "catcher_destroy"):
         assert required in names
 
 
@@ -41,7 +43,7 @@ def test_library_exports_every_declared_symbol(cq):
     assert not missing, missing
     out = subprocess.run(["nm", "-D", "--defined-only", cq.LIB_PATH], capture_output=True,
                          text=True).stdout
-    exported = set(re.findall(r" T (cq_[a-z0-9_]+)$", out, flags=re.M))
+    exported = set(re.findall(r" T ((?:cq|catcher)_[a-z0-9_]+)$", out, flags=re.M))
     assert declared_symbols() <= exported
 
 
