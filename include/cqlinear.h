@@ -214,6 +214,17 @@ cq_status cq_dequantize(const uint32_t *qweight, const void *scales, const void 
  */
 cq_status cq_device_status(int32_t device, int32_t *status);
 
+/*
+ * Checks the device watchdog of `device`: one kernel waits, through the same
+ * bounded wait the TMA pipelines use, on a barrier that nothing arrives on;
+ * after the wait's limit (2 s) it sets the timeout bit of the watchdog word
+ * and returns.  CQ_OK when that happened; the word stays set, so calls that
+ * check it (cq_linear_forward_f32) report CQ_RUNTIME_ERROR until
+ * cq_device_status reads and clears it.  Faults, traps and hangs nothing.
+ * No reference counterpart.
+ */
+cq_status cq_device_watchdog_check(int32_t device);
+
 #ifdef __cplusplus
 }
 #endif
