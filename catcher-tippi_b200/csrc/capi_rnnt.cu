@@ -111,6 +111,13 @@ cq_status cq_rnnt_init_random(cq_rnnt* dec, uint64_t seed) {
   });
 }
 
+cq_status cq_rnnt_set_fused_lstm(cq_rnnt* dec, int32_t enable) {
+  return guarded([&] {
+    need_handle(dec, "decoder");
+    dec->impl->set_fused_lstm(enable != 0);
+  });
+}
+
 int32_t cq_rnnt_tensor_count(const cq_rnnt* dec) {
   return dec ? static_cast<int32_t>(dec->impl->specs().size()) : -1;
 }

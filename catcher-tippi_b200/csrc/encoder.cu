@@ -17,14 +17,6 @@ namespace nemotron_cuda {
 
 namespace {
 
-bool graphs_on() {
-  static const bool on = [] {
-    const char* e = std::getenv("CQ_ENCODER_GRAPH");
-    return e == nullptr || std::strcmp(e, "0") != 0;
-  }();
-  return on;
-}
-
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Output length of the stride-2 kernel-3 convolution over `combined` frames
@@ -706,7 +698,7 @@ void EncoderState::encode_chunk(const float* mel, int mel_frames, void* out, cud
   if (g.T3 <= 0)
     throw_invalid("chunk of " + std::to_string(mel_frames) + " mel frames produces no encoder frame");
   DeviceGuard guard(enc_.device());
-  if (first || !graphs_on()) {
+  if (first) {
     launch_chunk(mel, g, out, stream);
   } else {
     cudaGraphExec_t exec = nullptr;

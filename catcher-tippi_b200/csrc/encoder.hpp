@@ -89,8 +89,8 @@ class EncoderState {
   int output_frames(int mel_frames) const;
   void encode_chunk(const float* mel, int mel_frames, void* out, cudaStream_t stream);
   void reset();
-  // Programmatic dependent launch between this state's kernels (default: on
-  // unless CQ_PDL=0).  Changing it drops the captured chunk graphs.
+  // Programmatic dependent launch between this state's kernels (default:
+  // on).  Changing it drops the captured chunk graphs.
   void set_pdl(bool on);
   bool pdl() const { return pdl_; }
   int chunks() const { return chunks_; }

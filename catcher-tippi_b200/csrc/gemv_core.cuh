@@ -1,5 +1,4 @@
-// Shared arithmetic of the small-M dequant-GEMV kernels (K1 in qgemv.cu and
-// the persistent linear-chain executor in qchain.cu): activation loads and
+// Arithmetic of the small-M dequant-GEMV (K1, qgemv.cu): activation loads and
 // their conversion to f16 MMA operands, the per-64-k-sub-block tensor-core
 // step over a weight tile in shared memory, and the output rounding.
 //

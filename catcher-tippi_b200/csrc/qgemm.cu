@@ -598,11 +598,6 @@ cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, 
 }
 
 int gemm_splits(int M, int N, int K, int num_sms) {
-  static const int forced = [] {
-    const char* e = std::getenv("CQ_GEMM_SPLITS");  // 1 disables the K split
-    return e == nullptr ? 0 : std::atoi(e);
-  }();
-  if (forced == 1) return 1;
   const int tiles = ((N + kGemmBN - 1) / kGemmBN) * ((M + kBM - 1) / kBM);
   const int KT = (K + kBK - 1) / kBK;
   // A CTA's k-tiles run at a fixed cadence set by its copy ring, whatever the

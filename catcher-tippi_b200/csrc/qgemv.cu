@@ -23,8 +23,7 @@
 //    epilogue.  No global scratch, no atomics, deterministic order.
 //  * Tensor cores via mma.m16n8k16 on the exact f16 image 1024 + q of each
 //    weight byte, with the offset folded into the group bias term; the
-//    per-sub-block arithmetic is shared with the chain executor
-//    (gemv_core.cuh).
+//    per-sub-block arithmetic lives in gemv_core.cuh.
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "qgemv.hpp"
@@ -462,13 +461,6 @@ bool plan_ok(int nsb, int s, int spc) {
 
 GemvPlan plan_gemv(int N, int K, int num_sms) {
   const int nsb = (K + 63) / 64;
-  if (const char* env = std::getenv("CQ_GEMV_PLAN")) {
-    int rt = 0, s = 0;
-    if (std::sscanf(env, "%d,%d", &rt, &s) == 2 && (rt == 1 || rt == 2 || rt == 4)) {
-      const int spc = (nsb + s - 1) / std::max(s, 1);
-      if (plan_ok(nsb, s, spc)) return GemvPlan{rt, s, spc, num_sms};
-    }
-  }
   // Measured on B200 (back-to-back launches, M = 14): the cluster reduction
   // costs more than it saves, so K is split only as far as the 16 sub-blocks
   // a CTA can hold require; rows per CTA grow only to stay within one wave of
@@ -488,7 +480,7 @@ GemvPlan plan_gemv(int N, int K, int num_sms) {
 
 GemvPlan plan_gemv_rows(const GemvPlan& base, int N, int M) {
   const int mtiles = (M + 15) / 16;
-  if (mtiles <= 1 || std::getenv("CQ_GEMV_PLAN") != nullptr) return base;
+  if (mtiles <= 1) return base;
   for (int rt : {1, 2, 4}) {
     if (rt < base.rt) continue;
     const int bands = (N + 16 * rt - 1) / (16 * rt);

@@ -20,25 +20,11 @@ std::string fmt_shape_error(const char* prefix, const std::string& msg) {
   return std::string(prefix) + msg;
 }
 
-bool gemm_allowed() {
-  static const bool on = [] {
-    const char* e = std::getenv("CQ_GEMM");
-    return e == nullptr || std::strcmp(e, "0") != 0;
-  }();
-  return on;
-}
-
 thread_local int t_pdl = -1;  // -1: the default
 
 }  // namespace
 
-bool pdl_default() {
-  static const bool on = [] {
-    const char* e = std::getenv("CQ_PDL");
-    return e == nullptr || std::strcmp(e, "0") != 0;
-  }();
-  return on;
-}
+bool pdl_default() { return true; }
 
 bool pdl_enabled() { return t_pdl >= 0 ? t_pdl != 0 : pdl_default(); }
 
@@ -272,7 +258,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
 }
 
 bool QuantizedLinear::gemm_for(int rows) const {
-  return dtype_ == CQ_BF16 && gemm_ok_ && gemm_allowed() && rows >= cq::kGemmMinRows;
+  return dtype_ == CQ_BF16 && gemm_ok_ && rows >= cq::kGemmMinRows;
 }
 
 void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale, int rows, void* y,
@@ -309,7 +295,7 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
 }
 
 size_t QuantizedLinear::scratch_bytes_for(int rows) const {
-  if (dtype_ != CQ_BF16 || !gemm_ok_ || !gemm_allowed() || rows < cq::kGemmMinRows) return 0;
+  if (dtype_ != CQ_BF16 || !gemm_ok_ || rows < cq::kGemmMinRows) return 0;
   return align_up(static_cast<size_t>(rows) * K_ * 2, 256) + static_cast<size_t>(rows) * 4;
 }
 
@@ -512,7 +498,7 @@ void QuantizedLinear::forward_array(const void* x, int ldx, int rows, void* y, i
   }
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0)
     throw_invalid("input rows must be 16-byte aligned (x % 16 == 0 and ldx % 8 == 0)");
-  if (rows >= cq::kGemmMinRows && gemm_ok_ && gemm_allowed()) {
+  if (rows >= cq::kGemmMinRows && gemm_ok_) {
     const_cast<QuantizedLinear*>(this)->forward_gemm(x, ldx, rows, y, ldy, act, stream);
     return;
   }

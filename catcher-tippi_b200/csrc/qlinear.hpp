@@ -59,8 +59,8 @@ class DeviceGuard {
 CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
                         int box_rows, int box_cols, CUtensorMapSwizzle swizzle);
 
-// Programmatic dependent launch (PDL) on this thread's kernel launches: on
-// unless CQ_PDL=0, or as the innermost live PdlScope says.  Encoder and RNNT
+// Programmatic dependent launch (PDL) on this thread's kernel launches: on,
+// or as the innermost live PdlScope says.  Encoder and RNNT
 // states set it per chunk (streams that overlap on one GPU can run faster
 // without it: CTAs launched early wait on the GPU holding their SM's room).
 bool pdl_default();

@@ -17,22 +17,6 @@ namespace nemotron_cuda {
 
 namespace {
 
-bool graphs_on() {
-  static const bool on = [] {
-    const char* e = std::getenv("CQ_RNNT_GRAPH");
-    return e == nullptr || std::strcmp(e, "0") != 0;
-  }();
-  return on;
-}
-
-bool lstm_fused_disabled() {
-  static const bool off = [] {
-    const char* e = std::getenv("CQ_RNNT_FUSED_LSTM");
-    return e != nullptr && std::strcmp(e, "0") == 0;
-  }();
-  return off;
-}
-
 // A copy of a [4H, K] gate weight with rows interleaved: row 4j + q holds
 // gate q of hidden unit j (source row q * H + j); same codes, scales, biases.
 std::unique_ptr<QuantizedLinear> interleave_gates(const QuantizedLinear& L, int H, cq_dtype dtype,
@@ -233,7 +217,7 @@ void RnntDecoder::finalize() {
   hh_il_.clear();
   gate_bias_il_.clear();
   const int g = ih(0)->group_size();
-  bool fits = cq::lstm_step_fits(H, g) && !lstm_fused_disabled();
+  bool fits = cq::lstm_step_fits(H, g) && fused_lstm_;
   for (int l = 0; l < cfg_.lstm_layers && fits; ++l)
     fits = ih(l)->group_size() == g && hh(l)->group_size() == g && ih(l)->input_dims() == H;
   if (fits) {
@@ -616,10 +600,6 @@ void RnntState::decode_chunk(const void* encoded, int ld, int frames, int* token
                   std::to_string(max_frames_));
   if (ld < c.enc_hidden) throw_invalid("encoder row stride is smaller than enc_hidden");
   DeviceGuard guard(dec_.device());
-  if (!graphs_on()) {
-    launch_chunk(encoded, ld, frames, tokens, token_frames, counts, stream);
-    return;
-  }
   cudaGraphExec_t exec = nullptr;
   for (auto& e : graphs_)
     if (e.encoded == encoded && e.ld == ld && e.frames == frames && e.tokens == tokens &&

@@ -45,6 +45,13 @@ class RnntDecoder {
   // Checks every tensor is bound; dequantises the embedding and adds the LSTM
   // bias pairs.
   void finalize();
+  // The one-launch LSTM step (default on where the shapes fit it); off, each
+  // step runs the ih and hh products and the cell as separate launches.
+  // Takes effect for states created afterwards.
+  void set_fused_lstm(bool on) {
+    fused_lstm_ = on;
+    finalized_ = false;
+  }
   QuantizedLinear* enc_proj() const { return linear("encoder_projector.weight"); }
   QuantizedLinear* dec_proj() const { return linear("decoder.decoder_projector.weight"); }
   QuantizedLinear* head() const { return linear("joint.head.weight"); }
@@ -83,6 +90,7 @@ class RnntDecoder {
   std::vector<std::unique_ptr<QuantizedLinear>> ih_il_, hh_il_;
   std::vector<DeviceBuffer> gate_bias_il_;
   bool finalized_ = false;
+  bool fused_lstm_ = true;
 };
 
 class RnntState {
@@ -101,8 +109,8 @@ class RnntState {
   // launch per op (false, the default).  Throws if the persistent kernel does
   // not fit this state's shapes.
   void set_persistent(bool on);
-  // Programmatic dependent launch between this state's kernels (default: on
-  // unless CQ_PDL=0).  Changing it drops the captured chunk graphs.
+  // Programmatic dependent launch between this state's kernels (default:
+  // on).  Changing it drops the captured chunk graphs.
   void set_pdl(bool on);
   bool pdl() const { return pdl_; }
   bool persistent() const { return use_persistent_; }

@@ -237,6 +237,15 @@ StreamingTranscriber::StreamingTranscriber(const Artifact& art, const cq_encoder
   enc_state_->set_prompts(&prompt_id_, 1);
   const int max_frames = lookahead + 1;  // encoder frames of one window
   dec_state_ = std::make_unique<RnntState>(decoder_, 1, max_frames);
+  // one stream whose frames mostly end at their first symbol: the persistent
+  // decode (one launch per chunk, frames skipped once every stream emitted
+  // blank) is the faster path here -- measured 1.64 against 2.25 ms per
+  // 14-frame chunk at one stream; it loses at 16 streams and more.  Models
+  // whose weights do not fit it resident keep the per-step launches.
+  try {
+    dec_state_->set_persistent(true);
+  } catch (const Error&) {
+  }
   const size_t max_samples = std::max(scheduler_.first_audio_samples(), scheduler_.subsequent_audio_samples());
   audio_ = DeviceBuffer(max_samples * sizeof(float));
   mel_ = DeviceBuffer(static_cast<size_t>(max_mel) * ecfg.mel_bins * sizeof(float));

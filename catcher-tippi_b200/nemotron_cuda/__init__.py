@@ -93,6 +93,7 @@ def lib() -> ctypes.CDLL:
         "cq_rnnt_get_tensor": ([vp, ctypes.c_char_p, vp, sz], i32),
         "cq_rnnt_linear": ([vp, ctypes.c_char_p], vp),
         "cq_rnnt_init_random": ([vp, ctypes.c_uint64], i32),
+        "cq_rnnt_set_fused_lstm": ([vp, i32], i32),
         "cq_rnnt_tensor_count": ([vp], i32),
         "cq_rnnt_tensor_name": ([vp, i32], ctypes.c_char_p),
         "cq_rnnt_destroy": ([vp], None),
@@ -104,15 +105,6 @@ def lib() -> ctypes.CDLL:
         "cq_rnnt_state_set_pdl": ([vp, i32], i32),
         "cq_rnnt_state_reset": ([vp], i32),
         "cq_rnnt_state_destroy": ([vp], None),
-        # persistent linear chains (include/cqchain.h)
-        "cq_linear_chain_create": ([vp, i32, pp], i32),
-        "cq_linear_chain_run": ([vp, vp], i32),
-        "cq_linear_chain_step_info": ([vp, i32] + [ctypes.POINTER(ctypes.c_int32)] * 7, i32),
-        "cq_linear_chain_profile": ([vp, i32], i32),
-        "cq_linear_chain_read_profile": ([vp, vp, sz], i32),
-        "cq_linear_chain_items": ([vp], i32),
-        "cq_linear_chain_grid": ([vp], i32),
-        "cq_linear_chain_destroy": ([vp], None),
         # release artifacts (include/cqartifact.h)
         "cq_artifact_open": ([ctypes.c_char_p, pp], i32),
         "cq_artifact_close": ([vp], None),
@@ -336,78 +328,6 @@ class QuantizedLinear:
             self.close()
         except Exception:
             pass
-
-
-class _ChainStep(ctypes.Structure):
-    _fields_ = [("layer", ctypes.c_void_p), ("x", ctypes.c_void_p), ("ldx", ctypes.c_int32),
-                ("rows", ctypes.c_int32), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int32),
-                ("act", ctypes.c_int32)]
-
-
-class LinearChain:
-    """A fixed sequence of small-M linear calls run as one persistent launch
-    (include/cqchain.h).  steps: (layer, x, y, act[, rows]) with torch device
-    tensors; x [rows, >=K] and y [rows, >=N] in the layers' dtype."""
-
-    def __init__(self, steps):
-        arr = (_ChainStep * len(steps))()
-        self._keep = []
-        for i, st in enumerate(steps):
-            layer, x, y, act = st[:4]
-            rows = st[4] if len(st) > 4 else x.shape[0]
-            arr[i] = _ChainStep(layer._h.value if isinstance(layer._h, ctypes.c_void_p) else layer._h,
-                                x.data_ptr(), x.stride(0), rows, y.data_ptr(), y.stride(0),
-                                ACTS[act])
-            self._keep.append((layer, x, y))
-        h = ctypes.c_void_p()
-        _check(lib().cq_linear_chain_create(ctypes.cast(arr, ctypes.c_void_p), len(steps),
-                                            ctypes.byref(h)))
-        self._h = h
-
-    def run(self, stream=None) -> None:
-        _check(lib().cq_linear_chain_run(self._h, _stream_ptr(stream)))
-
-    def run_raw(self, stream: int) -> None:
-        _check(lib().cq_linear_chain_run(self._h, ctypes.c_void_p(stream)))
-
-    @property
-    def items(self) -> int:
-        return int(lib().cq_linear_chain_items(self._h))
-
-    @property
-    def grid(self) -> int:
-        return int(lib().cq_linear_chain_grid(self._h))
-
-    def step_info(self, index: int) -> dict:
-        r, sb, ks, first, n, tg = (ctypes.c_int32() for _ in range(6))
-        deps = (ctypes.c_int32 * 3)()
-        _check(lib().cq_linear_chain_step_info(self._h, index, ctypes.byref(r), ctypes.byref(sb),
-                                               ctypes.byref(ks), ctypes.byref(first),
-                                               ctypes.byref(n), ctypes.byref(tg), deps))
-        return {"rows_per_item": r.value, "subblocks_per_item": sb.value, "kslices": ks.value,
-                "first_item": first.value, "items": n.value, "reads_tagged": tg.value,
-                "waits_for": [d for d in deps if d >= 0]}
-
-    def enable_profile(self, on: bool = True) -> None:
-        _check(lib().cq_linear_chain_profile(self._h, int(on)))
-
-    def read_profile(self) -> np.ndarray:
-        """[items, 6] ns stamps of the last run: copies issued, started, inputs
-        ready, weights ready, slot released, done.  Item t ran on CTA t % grid."""
-        out = np.zeros((self.items, 6), dtype=np.uint64)
-        _check(lib().cq_linear_chain_read_profile(self._h, _ptr(out), out.size))
-        return out
-
-    def close(self) -> None:
-        if getattr(self, "_h", None):
-            try:
-                lib().cq_linear_chain_destroy(self._h)
-            except TypeError:  # interpreter shutdown
-                pass
-            self._h = None
-
-    def __del__(self):
-        self.close()
 
 
 class PointwiseConv1d:

@@ -55,6 +55,11 @@ class Rnnt:
         _check(lib().cq_rnnt_init_random(r._h, ctypes.c_uint64(seed)))
         return r
 
+    def set_fused_lstm(self, enable: bool = True) -> None:
+        """One launch per LSTM layer step, or separate ih / hh / cell launches
+        (same bits); for states created afterwards."""
+        _check(lib().cq_rnnt_set_fused_lstm(self._h, int(enable)))
+
     def bind_artifact(self, artifact) -> None:
         """Binds every tensor from an opened Artifact (from_artifact)."""
         _check(lib().cq_rnnt_bind_artifact(self._h, artifact._h))

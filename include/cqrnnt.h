@@ -65,6 +65,11 @@ const cq_linear *cq_rnnt_linear(const cq_rnnt *dec, const char *name);
  * embedding N(0, 1), LSTM biases N(0, 0.02). */
 cq_status cq_rnnt_init_random(cq_rnnt *dec, uint64_t seed);
 
+/* One launch per LSTM layer step (enable != 0, the default where the shapes
+ * fit) or separate ih, hh and cell launches; both give the same bits.  For
+ * states created afterwards.  No reference counterpart. */
+cq_status cq_rnnt_set_fused_lstm(cq_rnnt *dec, int32_t enable);
+
 int32_t cq_rnnt_tensor_count(const cq_rnnt *dec);
 const char *cq_rnnt_tensor_name(const cq_rnnt *dec, int32_t index);
 void cq_rnnt_destroy(cq_rnnt *dec);

@@ -128,6 +128,7 @@ def _direct(model_dir, audio):
     est = enc.state(1, 8 * (LOOKAHEAD + 1))
     est.set_prompts([PROMPT])
     rst = dec.state(1, LOOKAHEAD + 1)
+    rst.set_persistent(True)  # as the handle's single-stream decoder
     fe = LogMelFrontend.nemotron()
     mel = torch.empty((1, 8 * (LOOKAHEAD + 1), 128), device="cuda")
     out = torch.empty((LOOKAHEAD + 1, ENC["hidden"]), dtype=torch.float16, device="cuda")

@@ -226,50 +226,32 @@ def test_rnnt_binding_errors(cq):
         st.set_persistent(True)
 
 
-_PATHS_SCRIPT = r"""
-import json, sys
-sys.path[:0] = [sys.argv[1] + "/catcher-tippi_b200"]
-import numpy as np, torch
-from nemotron_cuda.rnnt import Rnnt, RnntConfig
-cfg = RnntConfig.default(**json.loads(sys.argv[2]))
-dec = Rnnt.random(cfg, seed=31, dtype=sys.argv[3])
-S, F = int(sys.argv[4]), int(sys.argv[5])
-st = dec.state(S, F)
-rng = np.random.default_rng(4)
-out = []
-for _ in range(3):
-    enc = torch.from_numpy(rng.standard_normal((S * F, cfg.enc_hidden)).astype(np.float32)).cuda()
-    paths = st.decode_chunk(enc.to(torch.bfloat16 if sys.argv[3] == "bf16" else torch.float16), F)
-    out.append([[list(map(int, t)) for t in p] for p in paths])
-print(json.dumps(out))
-"""
-
-
 @pytest.mark.parametrize("dtype,size,streams,frames", [
     ("bf16", "small", 3, 5), ("f16", "small", 3, 5),
     # full size at 64 streams: the second layer's step runs 80-row bands at two
     # CTAs per SM, the first layer's reads the per-token table (two per SM)
     ("bf16", "full", 64, 2)])
-def test_one_launch_lstm_step_matches_separate_launches(cq, tmp_path, dtype, size, streams, frames):
+def test_one_launch_lstm_step_matches_separate_launches(cq, dtype, size, streams, frames):
     """The LSTM step as one launch (ih and hh products on a CTA pair, the cell in
     the leader's epilogue, gate-interleaved weights; layer 0's ih product from
     the per-token table) does K1's arithmetic and the cell kernel's: the greedy
     paths equal those of the separate ih, hh and cell launches
-    (CQ_RNNT_FUSED_LSTM=0, in another process) token for token."""
-    import json
-    import os
-    import subprocess
-    import sys
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    script = tmp_path / "paths.py"
-    script.write_text(_PATHS_SCRIPT)
-    cfg = json.dumps(SMALL if size == "small" else {})
+    (cq_rnnt_set_fused_lstm(0)) token for token."""
+    import torch
+    from nemotron_cuda.rnnt import Rnnt, RnntConfig
+    cfg = RnntConfig.default(**(SMALL if size == "small" else {}))
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
     outs = []
-    for fused in ("1", "0"):
-        env = dict(os.environ, CQ_RNNT_FUSED_LSTM=fused)
-        r = subprocess.run([sys.executable, str(script), root, cfg, dtype, str(streams), str(frames)],
-                           env=env, capture_output=True, text=True, timeout=300)
-        assert r.returncode == 0, r.stderr[-2000:]
-        outs.append(json.loads(r.stdout.strip().splitlines()[-1]))
+    for fused in (True, False):
+        dec = Rnnt.random(cfg, seed=31, dtype=dtype)
+        dec.set_fused_lstm(fused)
+        st = dec.state(streams, frames)
+        rng = np.random.default_rng(4)
+        out = []
+        for _ in range(3):
+            enc = rng.standard_normal((streams * frames, cfg.enc_hidden)).astype(np.float32)
+            out.append(st.decode_chunk(torch.from_numpy(enc).cuda().to(tdt), frames))
+        outs.append(out)
+        del st, dec
     assert outs[0] == outs[1]
     assert sum(len(p) for chunk in outs[0] for p in chunk) > 0
