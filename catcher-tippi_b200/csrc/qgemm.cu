@@ -6,18 +6,24 @@
 // the operation behind QuantizedLinear::forward_array
 // (crates/nemotron-mlx/src/model/layers.rs:298-310) at batched row counts.
 //
-// Per CTA: one 128 x BN output tile over the full K, 18 warps:
-//   warp 0   TMA producer: x tile [128 x 64] f16 (128B swizzle) and the packed
-//            weight tile [BN x 64] u8 (64B swizzle) into a 4-stage ring
+// Per CTA: one 128 x BN output tile over the full K, 19 warps:
+//   warp 0   weight producer: the packed weight tile [BN x 64] u8 (64B
+//            swizzle) and its (scale, bias) pairs into a 3-stage ring that the
+//            dequant warps free, starting before griddepcontrol.wait (weights
+//            do not depend on the previous kernel)
 //   warp 1   tcgen05.mma issuer (one elected lane), kind::f16, M=128, N=BN,
 //            K=16 per instruction, fp32 accumulator in tensor memory; owns the
 //            tensor-memory allocation
-//   warps 2-17 dequantisers: half a weight row per thread (sixteen warps, so
+//   warp 2   activation producer, after the wait: the x tile [128 x 64] f16
+//            (128B swizzle) into a 4-stage ring that the MMA frees (a warp of
+//            its own: two producers spinning in one warp starve each other)
+//   warps 3-18 dequantisers: half a weight row per thread (sixteen warps, so
 //            that the PRMT -> subtract -> FMA chains of four warps per
 //            scheduler hide each other's latency), w = s * q + b in f16
 //            (the byte becomes the exact f16 1024 + q by one PRMT, 1024 is
 //            subtracted exactly, then one fused multiply-add), written into
-//            the 128B-swizzled K-major layout the MMA reads; after the last
+//            one of three 128B-swizzled K-major buffers the MMA reads, so the
+//            dequantisation runs up to two k-tiles ahead; after the last
 //            k-tile the same warps run the epilogue (tcgen05.ld, row scale,
 //            rounding to T, output bias, activation, stores).
 // Both MMA operands are f16 (A and B of one MMA share the type): bf16
@@ -36,28 +42,40 @@ namespace cq {
 
 namespace {
 
-constexpr int kBM = 128;  // MMA M (tokens)
-constexpr int kBK = 64;   // k per stage: one 128-byte swizzle atom of f16
-constexpr int kStages = 4;  // TMA ring depth
-constexpr int kBBufs = 2;   // dequantised weight tiles (double buffer)
+constexpr int kBM = kGemmBN;  // weight rows per CTA: the MMA's M (A operand, in tensor memory)
+constexpr int kTN = kGemmTN;  // tokens per CTA: the MMA's N (B operand, in shared memory)
+constexpr int kBK = 64;       // k per stage: one 128-byte swizzle atom of f16 (four K=16 MMAs)
+constexpr int kXStages = 4;   // activation ring (a stage is freed by the MMA)
+constexpr int kQStages = 4;   // packed-weight ring (freed by the dequant warps)
+constexpr int kABufs = 3;     // dequantised weight tiles in tensor memory
 constexpr int kDequantWarps = 16;
-constexpr int kThreads = (2 + kDequantWarps) * 32;
-constexpr int kDequantWarp0 = 2;
+constexpr int kThreads = (3 + kDequantWarps) * 32;
+constexpr int kDequantWarp0 = 3;
+// tensor memory: the fp32 accumulator D [128 lanes][kTN columns] at column 0,
+// the dequantised weight buffers [128 lanes][32 columns] (64 f16 along K) from
+// column 256
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA0 = 256;
+static_assert(kTN <= 256 && kTN % 32 == 0 && kBM == 128, "tile shape");
 
-template <int BN, int SUBG>
+template <int SUBG>
 struct GemmSmem {
-  static constexpr int kA = kBM * kBK * 2;   // x tile, f16, 128B swizzle (16 KB)
-  static constexpr int kQ = BN * kBK;        // packed u8 weights, 64B swizzle
-  static constexpr int kSB = BN * SUBG * 4;  // f16 (scale, bias) per row and group
-  static constexpr int kStage = kA + kQ + 2048;  // TMA stage, 1024-aligned
-  static constexpr int kB = BN * kBK * 2;    // dequantised f16 weights, 128B swizzle
-  static constexpr int kBOff = kStages * kStage;
-  static constexpr int kBiasOff = kBOff + kBBufs * kB;  // [BN] output bias (fp32)
-  static constexpr int kBarOff = kBiasOff + BN * 4;
-  // full[S], empty[S], bfull[2], bempty[2], accum; tmem address word
-  static constexpr int kBytes = kBarOff + (2 * kStages + 2 * kBBufs + 1) * 8 + 16;
-  static_assert(kSB <= 2048, "scale/bias slot");
-  static_assert(kStage % 1024 == 0 && kB % 1024 == 0, "swizzled tiles stay 1024-aligned");
+  static constexpr int kX = kTN * kBK * 2;    // x tile, f16, 128B swizzle
+  static constexpr int kQ = kBM * kBK;        // packed u8 weights, 64B swizzle
+  static constexpr int kSB = kBM * SUBG * 4;  // f16 (scale, bias) per row and group
+  static constexpr int kQStage = kQ + 1024;   // packed tile + its (scale, bias) slot
+  static constexpr int kQOff = kXStages * kX;
+  static constexpr int kRsOff = kQOff + kQStages * kQStage;  // [kTN] row scales (fp32)
+  static constexpr int kBiasOff = kRsOff + kTN * 4;          // [kBM] output bias (fp32)
+  static constexpr int kBarOff = kBiasOff + kBM * 4;
+  // xfull/xempty[X], qfull/qempty[Q], afull/aempty[A], accum; tmem address word
+  static constexpr int kBytes =
+      kBarOff + (2 * kXStages + 2 * kQStages + 2 * kABufs + 1) * 8 + 16;
+  static_assert(kSB <= 1024, "scale/bias slot");
+  static_assert(kX % 1024 == 0 && kQStage % 1024 == 0, "swizzled tiles stay 1024-aligned");
+  // the epilogue stages its output [kTN][kBM] T, or its K-split partial
+  // [kTN][kBM + 4] fp32, in the idle rings
+  static_assert(kTN * (kBM * 4 + 16) <= kRsOff, "epilogue staging fits the rings");
 };
 
 // --------------------------------------------------------------- tcgen05
@@ -90,6 +108,41 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D (+)= A * B with A in tensor memory ([128 lanes][K/2 columns] of f16
+// pairs) and B in shared memory (descriptor)
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_f16_ts_acc(uint32_t d_tmem, uint32_t a_tmem,
+                                                  uint64_t b_desc, uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, 1;" ::"r"(d_tmem),
+               "r"(a_tmem), "l"(b_desc), "r"(idesc)
+               : "memory");
+}
+// 32 lanes x 8 columns of 32-bit: thread i of the warp writes lane (quarter*32+i)
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D += A * B (the accumulate flag set): every MMA of a k-tile after its first
+__device__ __forceinline__ void tc_mma_f16_acc(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc) {
+  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d_tmem), "l"(a_desc),
+               "l"(b_desc), "r"(idesc)
+               : "memory");
+}
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -121,37 +174,36 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
          (static_cast<uint64_t>(2) << 61);
 }
 
-// Instruction descriptor: f32 accumulate, f16 A and B, both K-major, M=128, N=BN.
-template <int BN>
+// Instruction descriptor: f32 accumulate, f16 A and B, both K-major, M = kBM,
+// N = kTN.
 __host__ __device__ constexpr uint32_t idesc_f16_f32() {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(BN >> 3) << 17) |
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
-template <int DT, int G, int BN>
+template <int DT, int G>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap qmap,
                  const GemmArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
-  // each dequant thread takes kChunks of the four 16-byte chunks of one row
-  constexpr int kChunks = 4 * BN / (kDequantWarps * 32);
-  static_assert(kChunks >= 1 && 4 % kChunks == 0 && (kDequantWarps * 32) % BN == 0,
-                "chunks per dequant thread");
-  using L = GemmSmem<BN, SUBG>;
+  using L = GemmSmem<SUBG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
-  uint64_t* empty = full + kStages;
-  uint64_t* bfull = empty + kStages;
-  uint64_t* bempty = bfull + kBBufs;
-  uint64_t* accum = bempty + kBBufs;
+  uint64_t* xfull = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint64_t* xempty = xfull + kXStages;
+  uint64_t* qfull = xempty + kXStages;
+  uint64_t* qempty = qfull + kQStages;
+  uint64_t* afull = qempty + kQStages;
+  uint64_t* aempty = afull + kABufs;
+  uint64_t* accum = aempty + kABufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum + 1);
+  float* rs_s = reinterpret_cast<float*>(smem + L::kRsOff);
   float* bias_s = reinterpret_cast<float*>(smem + L::kBiasOff);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+  const int n0 = blockIdx.x * kBM, m0 = blockIdx.y * kTN;
   const int KT = (a.K + kBK - 1) / kBK;
   // this CTA's k tiles: all of them, or its slice of a cluster's K split
   // (the host guarantees every slice is non-empty)
@@ -163,19 +215,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     prefetch_tensormap(&amap);
     prefetch_tensormap(&qmap);
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kDequantWarps + 1);  // dequant warps (q, scales) + MMA commit (x)
+    for (int s = 0; s < kXStages; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);  // tcgen05.commit
     }
-    for (int b = 0; b < kBBufs; ++b) {
-      mbar_init(&bfull[b], kDequantWarps);  // one arrival per dequant warp
-      mbar_init(&bempty[b], 1);  // tcgen05.commit
+    for (int s = 0; s < kQStages; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qempty[s], kDequantWarps);  // one arrival per dequant warp
+    }
+    for (int b = 0; b < kABufs; ++b) {
+      mbar_init(&afull[b], kDequantWarps);
+      mbar_init(&aempty[b], 1);  // tcgen05.commit
     }
     mbar_init(accum, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -183,193 +239,197 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_d = *tmem_slot;
 
+  // Only the activations (and the row scales, and the output's readers) tie
+  // this kernel to the previous one: the weights stream and are dequantised
+  // ahead of griddepcontrol.wait, so a CTA launched early under programmatic
+  // dependent launch has its first weight tiles ready when the activations
+  // arrive.
   pdl_launch_dependents();
-  pdl_wait();
 
   bool ok = true;
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ weights
     if (lane == 0) {
+      // packed weights and the k-tile's (scale, bias) pairs of the kBM rows
+      // (one contiguous block)
       const uint64_t pol = l2_policy_evict_normal();
       for (int i = 0; i < NKT; ++i) {
         const int kt = kt0 + i;
-        const int s = i % kStages;
-        const uint32_t ph = (i / kStages) & 1;
-        ok = mbar_wait_bounded(&empty[s], ph ^ 1, a.status) && ok;
-        uint8_t* st = smem + s * L::kStage;
-        mbar_arrive_expect_tx(&full[s], L::kA + L::kQ + L::kSB);
-        tma_load_2d(st, &amap, kt * kBK, m0, &full[s], pol);
-        tma_load_2d(st + L::kA, &qmap, kt * kBK, n0, &full[s], pol);
-        // the k-tile's (scale, bias) pairs of the BN rows: one contiguous block
-        bulk_copy_g2s(st + L::kA + L::kQ,
+        const int s = i % kQStages;
+        const uint32_t ph = ((i / kQStages) & 1) ^ 1;
+        if (!mbar_try_wait(&qempty[s], ph)) ok = mbar_wait_bounded(&qempty[s], ph, a.status) && ok;
+        uint8_t* st = smem + L::kQOff + s * L::kQStage;
+        mbar_arrive_expect_tx(&qfull[s], L::kQ + L::kSB);
+        tma_load_2d(st, &qmap, kt * kBK, n0, &qfull[s], pol);
+        bulk_copy_g2s(st + L::kQ,
                       reinterpret_cast<const uint8_t*>(a.sb_tiles) +
                           (static_cast<size_t>(blockIdx.x) * KT + kt) * L::kSB,
-                      L::kSB, &full[s]);
+                      L::kSB, &qfull[s]);
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ activations
+    // (the previous kernel's output; a warp of its own: two producers spinning
+    // in one warp starve each other)
+    if (lane == 0) {
+      pdl_wait();
+      const uint64_t pol = l2_policy_evict_normal();
+      for (int i = 0; i < NKT; ++i) {
+        const int kt = kt0 + i;
+        const int s = i % kXStages;
+        const uint32_t ph = ((i / kXStages) & 1) ^ 1;
+        if (!mbar_try_wait(&xempty[s], ph)) ok = mbar_wait_bounded(&xempty[s], ph, a.status) && ok;
+        mbar_arrive_expect_tx(&xfull[s], L::kX);
+        tma_load_2d(smem + s * L::kX, &amap, kt * kBK, m0, &xfull[s], pol);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32<BN>();
+      // The tensor pipe keeps only a few MMAs queued: scalar work between two
+      // MMAs idles it (measured: 128 cycles per 128x256x16 MMA back to back,
+      // twice that with per-MMA descriptor arithmetic and out-of-line waits).
+      // So the waits take an inline fast path and the operand addresses
+      // advance by constants: the descriptor's start address field (bits
+      // 0-13) holds address >> 4 and every buffer lies below 227 KB, so adding
+      // never carries out of it; a tensor-memory column is the address's low
+      // half.
+      constexpr uint32_t idesc = idesc_f16_f32();
+      const uint64_t db0 = sw128_kmajor_desc(smem_u32(smem));
+      const uint32_t ta0 = tmem_d + kTmemA0;
       for (int i = 0; i < NKT; ++i) {
-        const int s = i % kStages, b = i % kBBufs;
-        ok = mbar_wait_bounded(&full[s], (i / kStages) & 1, a.status) && ok;
-        ok = mbar_wait_bounded(&bfull[b], (i / kBBufs) & 1, a.status) && ok;
+        const int s = i % kXStages, b = i % kABufs;
+        const uint32_t px = (i / kXStages) & 1, pa = (i / kABufs) & 1;
+        if (!mbar_try_wait(&xfull[s], px)) ok = mbar_wait_bounded(&xfull[s], px, a.status) && ok;
+        if (!mbar_try_wait(&afull[b], pa)) ok = mbar_wait_bounded(&afull[b], pa, a.status) && ok;
         tc_fence_after();
-        const uint32_t a_addr = smem_u32(smem + s * L::kStage);
-        const uint32_t b_addr = smem_u32(smem + L::kBOff + b * L::kB);
-#pragma unroll
-        for (int ks = 0; ks < kBK / 16; ++ks) {
-          // advancing K by 16 f16 = 32 bytes inside the swizzle atom
-          tc_mma_f16(tmem_d, sw128_kmajor_desc(a_addr + 32 * ks), sw128_kmajor_desc(b_addr + 32 * ks),
-                     idesc, (i | ks) != 0);
-        }
-        tc_commit(&empty[s]);   // x tile consumed
-        tc_commit(&bempty[b]);  // dequantised tile consumed
+        // K advances by 16 f16: 32 bytes (2 descriptor units) of the x tile,
+        // 8 columns of the weight tile
+        const uint64_t db = db0 + static_cast<uint64_t>(s * (L::kX >> 4));
+        const uint32_t ta = ta0 + static_cast<uint32_t>(b * 32);
+        tc_mma_f16_ts(tmem_d, ta, db, idesc, i != 0);
+        tc_mma_f16_ts_acc(tmem_d, ta + 8, db + 2, idesc);
+        tc_mma_f16_ts_acc(tmem_d, ta + 16, db + 4, idesc);
+        tc_mma_f16_ts_acc(tmem_d, ta + 24, db + 6, idesc);
+        tc_commit(&xempty[s]);  // x tile consumed
+        tc_commit(&aempty[b]);  // dequantised tile consumed
       }
       tc_commit(accum);
     }
   } else {
     // ------------------------------------------------------------ dequant
-    constexpr int kDT = kDequantWarps * 32;
+    // Warp w writes tensor-memory lanes 32 (w % 4) .. + 31 (the lanes a warp
+    // may access): weight row r = 32 (w % 4) + lane of the tile, and of its 64
+    // k the 16 of column group cg = (w - 3) / 4, i.e. columns 8 cg .. 8 cg + 7.
+    // w = s * q + b in f16: the byte becomes the exact f16 1024 + q by one
+    // PRMT, 1024 is subtracted exactly, then one fused multiply-add (one
+    // rounding).
+    const int dw = warp - kDequantWarp0;
+    const int quarter = warp & 3;
+    const int cg = dw >> 2;
+    const int row = quarter * 32 + lane;
     const int t = threadIdx.x - kDequantWarp0 * 32;
-    const int row = t % BN, cfirst = (t / BN) * kChunks;  // chunks cfirst .. cfirst + kChunks - 1
-    for (int r = t; r < BN; r += kDT) {
+    for (int r = t; r < kBM; r += kDequantWarps * 32) {
       const int n = n0 + r;
       bias_s[r] = (a.bias != nullptr && n < a.N) ? ld_t<DT>(a.bias, n) : 0.0f;
     }
     const __half2 k1024 = __float2half2_rn(1024.0f);
+    const int h = (G == 32) ? (cg >> 1) : 0;  // which 32-wide group of the k-tile
+    const int sw64 = (row >> 1) & 3;
+    const uint32_t ta_row = tmem_d + kTmemA0 + (static_cast<uint32_t>(quarter * 32) << 16) +
+                            static_cast<uint32_t>(cg * 8);
     for (int i = 0; i < NKT; ++i) {
-      const int s = i % kStages, b = i % kBBufs;
-      ok = mbar_wait_bounded(&full[s], (i / kStages) & 1, a.status) && ok;
-      ok = mbar_wait_bounded(&bempty[b], ((i / kBBufs) & 1) ^ 1, a.status) && ok;
-      const uint8_t* st = smem + s * L::kStage;
-      const __half2* sbp = reinterpret_cast<const __half2*>(st + L::kA + L::kQ);
-      uint8_t* bt = smem + L::kBOff + b * L::kB;
-      // this row's (scale, bias) for the k-tile's group(s), f16
-      __half2 s2[2], b2[2];
+      const int s = i % kQStages, b = i % kABufs;
+      const uint32_t pq = (i / kQStages) & 1, pa = ((i / kABufs) & 1) ^ 1;
+      if (!mbar_try_wait(&qfull[s], pq)) ok = mbar_wait_bounded(&qfull[s], pq, a.status) && ok;
+      if (!mbar_try_wait(&aempty[b], pa)) ok = mbar_wait_bounded(&aempty[b], pa, a.status) && ok;
+      tc_fence_after();
+      const uint8_t* st = smem + L::kQOff + s * L::kQStage;
+      const __half2 p = reinterpret_cast<const __half2*>(st + L::kQ)[row * SUBG + h];
+      const __half2 s2 = __low2half2(p), b2 = __high2half2(p);
+      // logical 16-byte chunk cg of the 64B-swizzled packed row
+      const uint4 qv = *reinterpret_cast<const uint4*>(st + row * 64 + ((cg ^ sw64) << 4));
+      const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+      uint32_t out[8];
 #pragma unroll
-      for (int h = 0; h < SUBG; ++h) {
-        const __half2 p = sbp[row * SUBG + h];
-        s2[h] = __low2half2(p);
-        b2[h] = __high2half2(p);
+      for (int j = 0; j < 4; ++j) {
+        uint32_t lo = __byte_perm(qw[j], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
+        uint32_t hi = __byte_perm(qw[j], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
+        const __half2 wl = __hfma2(s2, __hsub2(*reinterpret_cast<__half2*>(&lo), k1024), b2);
+        const __half2 wh = __hfma2(s2, __hsub2(*reinterpret_cast<__half2*>(&hi), k1024), b2);
+        out[2 * j] = *reinterpret_cast<const uint32_t*>(&wl);
+        out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&wh);
       }
-      if constexpr (SUBG == 1) {
-        s2[1] = s2[0];
-        b2[1] = b2[0];
-      }
-      const uint8_t* qrow = st + L::kA + row * 64;  // 64B-swizzled u8 row
-      uint8_t* brow = bt + row * 128;               // 128B-swizzled f16 row
-      const int sw64 = (row >> 1) & 3, sw128 = row & 7;
-#pragma unroll
-      for (int cc = 0; cc < kChunks; ++cc) {
-        const int c = cfirst + cc;
-        // logical 16-byte chunk c of the packed row = k0 + 16c .. k0 + 16c + 15
-        const uint4 qv = *reinterpret_cast<const uint4*>(qrow + ((c ^ sw64) << 4));
-        const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-        const int h = (G == 32) ? (c >> 1) : 0;
-        uint32_t out[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          uint32_t lo = __byte_perm(qw[i], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
-          uint32_t hi = __byte_perm(qw[i], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
-          const __half2 ql = __hsub2(*reinterpret_cast<__half2*>(&lo), k1024);
-          const __half2 qh = __hsub2(*reinterpret_cast<__half2*>(&hi), k1024);
-          const __half2 wl = __hfma2(s2[h], ql, b2[h]);
-          const __half2 wh = __hfma2(s2[h], qh, b2[h]);
-          out[2 * i] = *reinterpret_cast<const uint32_t*>(&wl);
-          out[2 * i + 1] = *reinterpret_cast<const uint32_t*>(&wh);
-        }
-        // 16 f16 = two 16-byte chunks (2c, 2c+1) of the 128-byte row
-        *reinterpret_cast<uint4*>(brow + (((2 * c) ^ sw128) << 4)) =
-            make_uint4(out[0], out[1], out[2], out[3]);
-        *reinterpret_cast<uint4*>(brow + (((2 * c + 1) ^ sw128) << 4)) =
-            make_uint4(out[4], out[5], out[6], out[7]);
-      }
-      fence_proxy_async_shared();  // generic-proxy writes -> tensor-core reads
+      tmem_st_32x32b_x8(ta_row + static_cast<uint32_t>(b * 32), out);
+      tmem_wait_st();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(&bfull[b]);
-        mbar_arrive(&empty[s]);  // packed weights and scales of stage s consumed
+        mbar_arrive(&afull[b]);
+        mbar_arrive(&qempty[s]);  // packed weights and scales of stage s consumed
       }
     }
 
     // ------------------------------------------------------------ epilogue
-    // the dequant warps wrote bias_s; make it visible to each other
+    // the row scales come from the previous kernel, and the output may be
+    // one of its inputs
+    pdl_wait();
+    for (int r = t; r < kTN; r += kDequantWarps * 32) {
+      const int m = m0 + r;
+      rs_s[r] = (a.row_scale != nullptr && m < a.M) ? a.row_scale[m] : 1.0f;
+    }
     asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
     ok = mbar_wait_bounded(accum, 0, a.status) && ok;
     tc_fence_after();
-    const int quarter = warp & 3;  // TMEM lanes this warp may read
-    // warps sharing a lane quarter split the columns
-    constexpr int kColSplit = kDequantWarps / 4;
-    const int csub = (warp - kDequantWarp0) / 4;
-    const int m = m0 + quarter * 32 + lane;
-    const float rs = (a.row_scale != nullptr && m < a.M) ? a.row_scale[m] : 1.0f;
+    // D [n = lane][m = column]: this warp's 32 lanes (weight rows) and every
+    // fourth 32-token chunk from cg on
+    const int nl = quarter * 32 + lane;
     const bool has_bias = a.bias != nullptr;
-    const bool vec_ok = (a.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+    const float bias_v = bias_s[nl];
     if (nsplit > 1) {
-      // K split: park this CTA's partial tile [128][BN] in the (now idle)
-      // stage buffers, rows padded by 4 floats so a warp's 16-byte writes of
-      // 32 rows spread over all banks; the cluster reduces it below.
+      // K split: park this CTA's fp32 partial [kTN][kBM + 4] in the idle
+      // rings (a warp's 32 lanes write 32 consecutive floats of a row); the
+      // cluster reduces it below
       float* part = reinterpret_cast<float*>(smem);
-      const int row = quarter * 32 + lane;
 #pragma unroll 1
-      for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
+      for (int c = cg; c < kTN / 32; c += 4) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
+        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
         tmem_wait_ld();
-        float4* dst = reinterpret_cast<float4*>(part + row * (BN + 4) + c0);
 #pragma unroll
-        for (int v = 0; v < 8; ++v)
-          dst[v] = make_float4(__uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
-                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+        for (int j = 0; j < 32; ++j) part[(c * 32 + j) * (kBM + 4) + nl] = __uint_as_float(r[j]);
       }
     } else {
-      // Finished T values go to a [128][BN] tile in the (idle) stage buffers,
-      // rows padded by 16 bytes so a warp's 16-byte writes of 8 rows hit all
-      // banks; the tile then leaves in whole rows (each warp writes 32
-      // consecutive 16-byte pieces of one row: fully coalesced).
-      constexpr int kRowBytes = BN * 2 + 16;
-      uint8_t* ot = smem;
-      const int row = quarter * 32 + lane;
+      // finished T values go to a [kTN][kBM] tile (rows padded by 16 bytes)
+      // in the idle rings, then leave in whole rows (16-byte stores)
+      constexpr int kRowBytes = kBM * 2 + 16;
+      uint16_t* ot = reinterpret_cast<uint16_t*>(smem);
 #pragma unroll 1
-      for (int c0 = csub * 32; c0 < BN; c0 += 32 * kColSplit) {
+      for (int c = cg; c < kTN / 32; c += 4) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c0, r);
+        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
         tmem_wait_ld();
-        uint32_t pk[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float o2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int jj = 2 * j + e;
-            float v = round_t<DT>(__uint_as_float(r[jj]) * rs);
-            if (has_bias) v = round_t<DT>(v + bias_s[c0 + jj]);
-            if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
-            else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
-            o2[e] = v;
-          }
-          if constexpr (DT == kBF16) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(o2[0], o2[1]);
-            pk[j] = *reinterpret_cast<const uint32_t*>(&h);
-          } else {
-            const __half2 h = __floats2half2_rn(o2[0], o2[1]);
-            pk[j] = *reinterpret_cast<const uint32_t*>(&h);
-          }
+        for (int j = 0; j < 32; ++j) {
+          float v = round_t<DT>(__uint_as_float(r[j]) * rs_s[c * 32 + j]);
+          if (has_bias) v = round_t<DT>(v + bias_v);
+          if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
+          else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
+          uint16_t bits;
+          if constexpr (DT == kBF16) bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+          else bits = __half_as_ushort(__float2half_rn(v));
+          ot[(c * 32 + j) * (kRowBytes / 2) + nl] = bits;
         }
-        uint4* dst = reinterpret_cast<uint4*>(ot + row * kRowBytes + c0 * 2);
-#pragma unroll
-        for (int v = 0; v < 4; ++v) dst[v] = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
-      constexpr int kPieces = BN / 8;  // 16-byte pieces per row
-      const int t = threadIdx.x - kDequantWarp0 * 32;
-      for (int e = t; e < kBM * kPieces; e += kDequantWarps * 32) {
+      const bool vec_ok = (a.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
+      constexpr int kPieces = kBM / 8;  // 16-byte pieces per row
+      const uint8_t* otb = reinterpret_cast<const uint8_t*>(smem);
+      for (int e = t; e < kTN * kPieces; e += kDequantWarps * 32) {
         const int rr = e / kPieces, pc = e % kPieces;
         const int mm = m0 + rr, n = n0 + pc * 8;
         if (mm >= a.M) continue;
-        const uint4 v = *reinterpret_cast<const uint4*>(ot + rr * kRowBytes + pc * 16);
+        const uint4 v = *reinterpret_cast<const uint4*>(otb + rr * kRowBytes + pc * 16);
         if (vec_ok && n + 8 <= a.N) {
           *reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(a.y) + static_cast<size_t>(mm) * a.ldy + n) = v;
         } else {
@@ -393,13 +453,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // this CTA reduces columns [rank * W, (rank + 1) * W) of the tile over
       // the cluster's partials in rank order, then applies the epilogue
       const int t = threadIdx.x - kDequantWarp0 * 32;
-      const int W = BN / nsplit, groups = W / 4;
+      const int W = kBM / nsplit, groups = W / 4;
       const int cbase = static_cast<int>(cluster_ctarank()) * W;
       const uint32_t part_s = smem_u32(smem);
       const bool vec4 = (a.ldy % 4) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 7) == 0;
-      for (int item = t; item < kBM * groups; item += kDequantWarps * 32) {
+      for (int item = t; item < kTN * groups; item += kDequantWarps * 32) {
         const int row = item / groups, col = cbase + (item % groups) * 4;
-        const uint32_t off = static_cast<uint32_t>(row * (BN + 4) + col) * 4u;
+        const uint32_t off = static_cast<uint32_t>(row * (kBM + 4) + col) * 4u;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         for (int r = 0; r < nsplit; ++r) {
           const float4 v = ld_dsmem_v4(mapa_shared(part_s + off, static_cast<uint32_t>(r)));
@@ -410,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int m = m0 + row;
         if (m >= a.M) continue;
-        const float rs = a.row_scale != nullptr ? a.row_scale[m] : 1.0f;
+        const float rs = rs_s[row];
         float o[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -426,11 +486,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             if constexpr (DT == kBF16) {
-              const __nv_bfloat162 h = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
-              pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+              const __nv_bfloat162 hh = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
+              pk[j] = *reinterpret_cast<const uint32_t*>(&hh);
             } else {
-              const __half2 h = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
-              pk[j] = *reinterpret_cast<const uint32_t*>(&h);
+              const __half2 hh = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
+              pk[j] = *reinterpret_cast<const uint32_t*>(&hh);
             }
           }
           *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(a.y) + static_cast<size_t>(m) * a.ldy +
@@ -449,7 +509,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_d, BN);
+    tmem_dealloc(tmem_d, kTmemCols);
   }
   (void)ok;
 }
@@ -515,14 +575,14 @@ __global__ void __launch_bounds__(kPrepassThreads)
   }
 }
 
-template <int DT, int G, int BN>
+template <int DT, int G>
 cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, const GemmArgs& a,
                               cudaStream_t stream, bool pdl) {
-  using L = GemmSmem<BN, (G == 32) ? 2 : 1>;
-  auto kern = qgemm_kernel<DT, G, BN>;
+  using L = GemmSmem<(G == 32) ? 2 : 1>;
+  auto kern = qgemm_kernel<DT, G>;
   static bool configured = false;
   const int smem = L::kBytes + 1024;  // + alignment slack
-  static_assert(GemmSmem<BN, (G == 32) ? 2 : 1>::kBytes + 1024 <= 227 * 1024, "smem budget");
+  static_assert(GemmSmem<(G == 32) ? 2 : 1>::kBytes + 1024 <= 227 * 1024, "smem budget");
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -536,7 +596,7 @@ cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, 
     if ((splits - 1) * per >= KT) return cudaErrorInvalidValue;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + BN - 1) / BN, (a.M + kBM - 1) / kBM, splits);
+  cfg.gridDim = dim3((a.N + kBM - 1) / kBM, (a.M + kTN - 1) / kTN, splits);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -563,9 +623,9 @@ template <int DT>
 cudaError_t launch_gemm_g(int group, const CUtensorMap& amap, const CUtensorMap& qmap,
                           const GemmArgs& a, cudaStream_t stream, bool pdl) {
   switch (group) {
-    case 32: return launch_gemm_typed<DT, 32, kGemmBN>(amap, qmap, a, stream, pdl);
-    case 64: return launch_gemm_typed<DT, 64, kGemmBN>(amap, qmap, a, stream, pdl);
-    case 128: return launch_gemm_typed<DT, 128, kGemmBN>(amap, qmap, a, stream, pdl);
+    case 32: return launch_gemm_typed<DT, 32>(amap, qmap, a, stream, pdl);
+    case 64: return launch_gemm_typed<DT, 64>(amap, qmap, a, stream, pdl);
+    case 128: return launch_gemm_typed<DT, 128>(amap, qmap, a, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -598,7 +658,7 @@ cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, 
 }
 
 int gemm_splits(int M, int N, int K, int num_sms) {
-  const int tiles = ((N + kGemmBN - 1) / kGemmBN) * ((M + kBM - 1) / kBM);
+  const int tiles = ((N + kBM - 1) / kBM) * ((M + kTN - 1) / kTN);
   const int KT = (K + kBK - 1) / kBK;
   // A CTA's k-tiles run at a fixed cadence set by its copy ring, whatever the
   // number of CTAs in flight, so splitting K over a cluster shortens the call
@@ -610,7 +670,7 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   return 1;
 }
 
-size_t gemm_smem_bytes() { return GemmSmem<kGemmBN, 2>::kBytes + 1024; }
+size_t gemm_smem_bytes() { return GemmSmem<2>::kBytes + 1024; }
 
 // (scale, bias) pairs as f16 in the GEMM's k-tile order:
 // out[ntile][ktile][row][h], h over the 32-wide halves of a 64-wide k-tile

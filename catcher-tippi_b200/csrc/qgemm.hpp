@@ -7,7 +7,8 @@
 
 namespace cq {
 
-constexpr int kGemmBN = 256;       // output columns per CTA
+constexpr int kGemmBN = 128;       // output columns (weight rows) per CTA
+constexpr int kGemmTN = 224;       // rows (tokens) per CTA: 896 = 4 x 224
 constexpr int kGemmMinRows = 256;  // below this the GEMV (K1) is used
 
 struct GemmArgs {
@@ -26,7 +27,7 @@ struct GemmArgs {
 // distributed shared memory (gemm_splits returns 1, 2 or 4).
 int gemm_splits(int M, int N, int K, int num_sms);
 
-// amap: f16 activations [M, K] (box 64 x 128, 128B swizzle);
+// amap: f16 activations [M, K] (box 64 x kGemmTN, 128B swizzle);
 // qmap: packed weights u8 [N, K] (box 64 x kGemmBN, 64B swizzle).
 cudaError_t launch_gemm(int dtype, int group, const CUtensorMap& amap, const CUtensorMap& qmap,
                         const GemmArgs& args, cudaStream_t stream, bool pdl);

@@ -237,7 +237,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
     row_scale = rs;
   }
   if (a_ptr != amap_ptr_ || a_ld != amap_ld_ || rows != amap_rows_) {
-    amap_ = make_map_2d(a_ptr, 2, rows, K_, a_ld, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_ = make_map_2d(a_ptr, 2, rows, K_, a_ld, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     amap_ptr_ = a_ptr;
     amap_ld_ = a_ld;
     amap_rows_ = rows;
@@ -274,7 +274,7 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
   DeviceContext& ctx = device_context(device_);
   DeviceGuard guard(device_);
   if (x16 != amap_pre_ptr_ || rows != amap_pre_rows_) {
-    amap_pre_ = make_map_2d(x16, 2, rows, K_, K_, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_pre_ = make_map_2d(x16, 2, rows, K_, K_, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     amap_pre_ptr_ = x16;
     amap_pre_rows_ = rows;
   }
@@ -329,7 +329,7 @@ void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows,
   check_cuda(cq::launch_gemm_prepass(x, ldx, rows, K_, scratch, K_, rs, stream, pdl_enabled()),
              "qgemm prepass");
   if (scratch != amap_scratch_ptr_ || rows != amap_scratch_rows_) {
-    amap_scratch_ = make_map_2d(scratch, 2, rows, K_, K_, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_scratch_ = make_map_2d(scratch, 2, rows, K_, K_, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
     amap_scratch_ptr_ = scratch;
     amap_scratch_rows_ = rows;
   }
