@@ -6,26 +6,30 @@
 // the operation behind QuantizedLinear::forward_array
 // (crates/nemotron-mlx/src/model/layers.rs:298-310) at batched row counts.
 //
-// Per CTA: one 128 x BN output tile over the full K, 19 warps:
-//   warp 0   weight producer: the packed weight tile [BN x 64] u8 (64B
-//            swizzle) and its (scale, bias) pairs into a 3-stage ring that the
+// Per CTA: one output tile of 128 weight rows x 224 tokens over the full K
+// (or its slice of a cluster's K split), 19 warps:
+//   warp 0   weight producer: the packed weight tile [128 x 64] u8 (64B
+//            swizzle) and its (scale, bias) pairs into a ring that the
 //            dequant warps free, starting before griddepcontrol.wait (weights
 //            do not depend on the previous kernel)
-//   warp 1   tcgen05.mma issuer (one elected lane), kind::f16, M=128, N=BN,
-//            K=16 per instruction, fp32 accumulator in tensor memory; owns the
+//   warp 1   tcgen05.mma issuer (one elected lane), kind::f16, M = 128 weight
+//            rows (the A operand, read from tensor memory), N = 224 tokens
+//            (the B operand, in shared memory), K = 16 per instruction; fp32
+//            accumulator in tensor-memory columns 0..223; owns the
 //            tensor-memory allocation
-//   warp 2   activation producer, after the wait: the x tile [128 x 64] f16
-//            (128B swizzle) into a 4-stage ring that the MMA frees (a warp of
-//            its own: two producers spinning in one warp starve each other)
-//   warps 3-18 dequantisers: half a weight row per thread (sixteen warps, so
-//            that the PRMT -> subtract -> FMA chains of four warps per
-//            scheduler hide each other's latency), w = s * q + b in f16
-//            (the byte becomes the exact f16 1024 + q by one PRMT, 1024 is
-//            subtracted exactly, then one fused multiply-add), written into
-//            one of three 128B-swizzled K-major buffers the MMA reads, so the
-//            dequantisation runs up to two k-tiles ahead; after the last
-//            k-tile the same warps run the epilogue (tcgen05.ld, row scale,
-//            rounding to T, output bias, activation, stores).
+//   warp 2   activation producer, after the wait: the x tile [224 x 64] f16
+//            (128B swizzle, K-major) into a ring that the MMA frees (a warp
+//            of its own: two producers spinning in one warp starve each other)
+//   warps 3-18 dequantisers: thread (w, lane) owns weight row
+//            32 (w % 4) + lane -- the tensor-memory lanes its warp may write --
+//            and 16 of the k-tile's 64 k; w = s * q + b in f16 (the byte
+//            becomes the exact f16 1024 + q by one PRMT, 1024 is subtracted
+//            exactly, then one fused multiply-add), stored with tcgen05.st
+//            into one of three A buffers in tensor memory, so the
+//            dequantisation runs up to two k-tiles ahead of the MMA and the
+//            dequantised weights never pass through shared memory; after the
+//            last k-tile the same warps run the epilogue (tcgen05.ld, row
+//            scale, rounding to T, output bias, activation, stores).
 // Both MMA operands are f16 (A and B of one MMA share the type): bf16
 // activations are converted beforehand by qgemm_prepass (per-row power-of-two
 // scale, undone in the epilogue), and the weights are dequantised to f16, whose
@@ -179,6 +183,66 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
 __host__ __device__ constexpr uint32_t idesc_f16_f32() {
   return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
          (static_cast<uint32_t>(kBM >> 4) << 24);
+}
+
+template <int DT>
+__device__ __forceinline__ uint16_t t_bits(float v) {
+  if constexpr (DT == kBF16) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  else return __half_as_ushort(__float2half_rn(v));
+}
+
+// forward_array's epilogue for one accumulator value: the product rounded to
+// T, plus the bias rounded to T, the activation rounded to T; returns T's
+// bits (the last rounding is the conversion itself).  SiLU uses the fast
+// exponential and division (a few fp32 ulps, far inside T's rounding step).
+template <int DT, int ACT, bool BIAS>
+__device__ __forceinline__ uint16_t finish_value(float acc, float rs, float bias) {
+  float v = acc * rs;
+  if constexpr (BIAS) v = round_t<DT>(v) + bias;
+  if constexpr (ACT == kActSilu) {
+    v = round_t<DT>(v);
+    v = __fdividef(v, 1.0f + __expf(-v));
+  } else if constexpr (ACT == kActRelu) {
+    v = v > 0.f ? v : 0.f;  // relu commutes with the rounding
+  }
+  return t_bits<DT>(v);
+}
+
+template <int DT>
+__device__ __forceinline__ uint16_t finish_value_any(float acc, float rs, float bias, bool has_bias,
+                                                     int act) {
+  if (act == kActSilu)
+    return has_bias ? finish_value<DT, kActSilu, true>(acc, rs, bias)
+                    : finish_value<DT, kActSilu, false>(acc, rs, bias);
+  if (act == kActRelu)
+    return has_bias ? finish_value<DT, kActRelu, true>(acc, rs, bias)
+                    : finish_value<DT, kActRelu, false>(acc, rs, bias);
+  return has_bias ? finish_value<DT, kActNone, true>(acc, rs, bias)
+                  : finish_value<DT, kActNone, false>(acc, rs, bias);
+}
+
+// The single-CTA epilogue of one thread: its weight row (tensor-memory lane)
+// over every fourth 32-token chunk from cg on, into the [token][row] staging
+// tile (`out` already points at the row's column; `pitch` in elements).
+template <int DT, int ACT, bool BIAS>
+__device__ __forceinline__ void finish_rows(uint32_t tq, int cg, const float* rs_s, float bias,
+                                            uint16_t* out, int pitch) {
+#pragma unroll 1
+  for (int c = cg; c < kTN / 32; c += 4) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tq + static_cast<uint32_t>(c * 32), r);
+    tmem_wait_ld();
+    const float4* rs4 = reinterpret_cast<const float4*>(rs_s + c * 32);
+    uint16_t* o = out + c * 32 * pitch;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 s = rs4[j / 4];
+      o[(j + 0) * pitch] = finish_value<DT, ACT, BIAS>(__uint_as_float(r[j + 0]), s.x, bias);
+      o[(j + 1) * pitch] = finish_value<DT, ACT, BIAS>(__uint_as_float(r[j + 1]), s.y, bias);
+      o[(j + 2) * pitch] = finish_value<DT, ACT, BIAS>(__uint_as_float(r[j + 2]), s.z, bias);
+      o[(j + 3) * pitch] = finish_value<DT, ACT, BIAS>(__uint_as_float(r[j + 3]), s.w, bias);
+    }
+  }
 }
 
 template <int DT, int G>
@@ -403,23 +467,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // finished T values go to a [kTN][kBM] tile (rows padded by 16 bytes)
       // in the idle rings, then leave in whole rows (16-byte stores)
       constexpr int kRowBytes = kBM * 2 + 16;
-      uint16_t* ot = reinterpret_cast<uint16_t*>(smem);
-#pragma unroll 1
-      for (int c = cg; c < kTN / 32; c += 4) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_d + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          float v = round_t<DT>(__uint_as_float(r[j]) * rs_s[c * 32 + j]);
-          if (has_bias) v = round_t<DT>(v + bias_v);
-          if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
-          else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
-          uint16_t bits;
-          if constexpr (DT == kBF16) bits = __bfloat16_as_ushort(__float2bfloat16_rn(v));
-          else bits = __half_as_ushort(__float2half_rn(v));
-          ot[(c * 32 + j) * (kRowBytes / 2) + nl] = bits;
-        }
+      uint16_t* ot = reinterpret_cast<uint16_t*>(smem) + nl;
+      const uint32_t tq = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
+      // the activation and the bias are uniform: one specialised loop each
+      if (a.act == kActSilu) {
+        if (has_bias) finish_rows<DT, kActSilu, true>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        else finish_rows<DT, kActSilu, false>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+      } else if (a.act == kActRelu) {
+        if (has_bias) finish_rows<DT, kActRelu, true>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        else finish_rows<DT, kActRelu, false>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+      } else {
+        if (has_bias) finish_rows<DT, kActNone, true>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        else finish_rows<DT, kActNone, false>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
       const bool vec_ok = (a.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
@@ -471,33 +530,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m = m0 + row;
         if (m >= a.M) continue;
         const float rs = rs_s[row];
-        float o[4];
+        uint16_t o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float v = round_t<DT>(acc[j] * rs);
-          if (a.bias != nullptr) v = round_t<DT>(v + bias_s[col + j]);
-          if (a.act == kActSilu) v = round_t<DT>(v / (1.0f + expf(-v)));
-          else if (a.act == kActRelu) v = v > 0.f ? v : 0.f;
-          o[j] = v;
-        }
+        for (int j = 0; j < 4; ++j)
+          o[j] = finish_value_any<DT>(acc[j], rs, bias_s[col + j], a.bias != nullptr, a.act);
         const int n = n0 + col;
+        uint16_t* yr = reinterpret_cast<uint16_t*>(a.y) + static_cast<size_t>(m) * a.ldy;
         if (vec4 && n + 4 <= a.N) {
-          uint32_t pk[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            if constexpr (DT == kBF16) {
-              const __nv_bfloat162 hh = __floats2bfloat162_rn(o[2 * j], o[2 * j + 1]);
-              pk[j] = *reinterpret_cast<const uint32_t*>(&hh);
-            } else {
-              const __half2 hh = __floats2half2_rn(o[2 * j], o[2 * j + 1]);
-              pk[j] = *reinterpret_cast<const uint32_t*>(&hh);
-            }
-          }
-          *reinterpret_cast<uint2*>(reinterpret_cast<uint16_t*>(a.y) + static_cast<size_t>(m) * a.ldy +
-                                    n) = make_uint2(pk[0], pk[1]);
+          *reinterpret_cast<uint2*>(yr + n) =
+              make_uint2(o[0] | (static_cast<uint32_t>(o[1]) << 16),
+                         o[2] | (static_cast<uint32_t>(o[3]) << 16));
         } else {
           for (int j = 0; j < 4; ++j)
-            if (n + j < a.N) st_t<DT>(a.y, static_cast<size_t>(m) * a.ldy + n + j, o[j]);
+            if (n + j < a.N) yr[n + j] = o[j];
         }
       }
     }
