@@ -7,9 +7,14 @@
 // (crates/nemotron-mlx/src/model/layers.rs:298-310) at batched row counts.
 //
 // Per CTA: one output tile of 128 weight rows x 224 tokens over the full K
-// (or its slice of a cluster's K split), 19 warps:
-//   warp 0   weight producer: the packed weight tile [128 x 64] u8 (64B
-//            swizzle) and its (scale, bias) pairs into a ring that the
+// (or its slice of a cluster's K split), 19 warps.  Everything moves in
+// pairs of 64-wide k-tiles (128 k): one copy per pair for the activations
+// and for the weights, one hand-off per pair from the dequantisers, and the
+// MMA issuer waits and commits once per pair around eight MMAs (measured on
+// B200: an issuer loop of four MMAs per wait/commit round leaves the tensor
+// pipe idle ~35 % of the time, eight per round keeps it busy).
+//   warp 0   weight producer: the packed weight pair [128 x 128] u8 (128B
+//            swizzle) and its (scale, bias) blocks into a ring that the
 //            dequant warps free, starting before griddepcontrol.wait (weights
 //            do not depend on the previous kernel)
 //   warp 1   tcgen05.mma issuer (one elected lane), kind::f16, M = 128 weight
@@ -17,18 +22,19 @@
 //            (the B operand, in shared memory), K = 16 per instruction; fp32
 //            accumulator in tensor-memory columns 0..223; owns the
 //            tensor-memory allocation
-//   warp 2   activation producer, after the wait: the x tile [224 x 64] f16
-//            (128B swizzle, K-major) into a ring that the MMA frees (a warp
-//            of its own: two producers spinning in one warp starve each other)
+//   warp 2   activation producer, after the wait: the x pair [2][224 x 64]
+//            f16 (128B swizzle, K-major) in one 3-D copy into a ring that
+//            the MMA frees (a warp of its own: two producers spinning in one
+//            warp starve each other)
 //   warps 3-18 dequantisers: thread (w, lane) owns weight row
 //            32 (w % 4) + lane -- the tensor-memory lanes its warp may write --
-//            and 16 of the k-tile's 64 k; w = s * q + b in f16 (the byte
+//            and 16 of each k-tile's 64 k; w = s * q + b in f16 (the byte
 //            becomes the exact f16 1024 + q by one PRMT, 1024 is subtracted
 //            exactly, then one fused multiply-add), stored with tcgen05.st
-//            into one of three A buffers in tensor memory, so the
-//            dequantisation runs up to two k-tiles ahead of the MMA and the
+//            into one of three A pair buffers in tensor memory, so the
+//            dequantisation runs up to two pairs ahead of the MMA and the
 //            dequantised weights never pass through shared memory; after the
-//            last k-tile the same warps run the epilogue (tcgen05.ld, row
+//            last pair the same warps run the epilogue (tcgen05.ld, row
 //            scale, rounding to T, output bias, activation, stores).
 // Both MMA operands are f16 (A and B of one MMA share the type): bf16
 // activations are converted beforehand by qgemm_prepass (per-row power-of-two
@@ -48,27 +54,29 @@ namespace {
 
 constexpr int kBM = kGemmBN;  // weight rows per CTA: the MMA's M (A operand, in tensor memory)
 constexpr int kTN = kGemmTN;  // tokens per CTA: the MMA's N (B operand, in shared memory)
-constexpr int kBK = 64;       // k per stage: one 128-byte swizzle atom of f16 (four K=16 MMAs)
-constexpr int kXStages = 4;   // activation ring (a stage is freed by the MMA)
-constexpr int kQStages = 4;   // packed-weight ring (freed by the dequant warps)
-constexpr int kABufs = 3;     // dequantised weight tiles in tensor memory
+constexpr int kBK = 64;       // k per MMA group: one 128-byte swizzle atom of f16 (four K=16 MMAs)
+constexpr int kXStages = 3;   // activation ring of k-tile pairs (a stage is freed by the MMA)
+constexpr int kQStages = 3;   // packed-weight ring of k-tile pairs (freed by the dequant warps)
+constexpr int kABufs = 3;     // dequantised weight pairs in tensor memory
 constexpr int kDequantWarps = 16;
 constexpr int kThreads = (3 + kDequantWarps) * 32;
 constexpr int kDequantWarp0 = 3;
 // tensor memory: the fp32 accumulator D [128 lanes][kTN columns] at column 0,
-// the dequantised weight buffers [128 lanes][32 columns] (64 f16 along K) from
-// column 256
+// the dequantised weight pair buffers [128 lanes][64 columns] (128 f16 along
+// K) from column 256
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA0 = 256;
 static_assert(kTN <= 256 && kTN % 32 == 0 && kBM == 128, "tile shape");
+static_assert(kTmemA0 + 64 * kABufs <= kTmemCols, "tensor memory budget");
 
 template <int SUBG>
 struct GemmSmem {
-  static constexpr int kX = kTN * kBK * 2;    // x tile, f16, 128B swizzle
-  static constexpr int kQ = kBM * kBK;        // packed u8 weights, 64B swizzle
-  static constexpr int kSB = kBM * SUBG * 4;  // f16 (scale, bias) per row and group
-  static constexpr int kQStage = kQ + 1024;   // packed tile + its (scale, bias) slot
-  static constexpr int kQOff = kXStages * kX;
+  static constexpr int kX = kTN * kBK * 2;    // one k-tile of x, f16, 128B swizzle
+  static constexpr int kXStage = 2 * kX;      // a k-tile pair: [2][kTN][64] f16
+  static constexpr int kQ = kBM * 2 * kBK;    // packed u8 weights of a pair, [kBM][128], 128B swizzle
+  static constexpr int kSB = kBM * SUBG * 4;  // f16 (scale, bias) per row and group, one k-tile
+  static constexpr int kQStage = kQ + 2 * 1024;  // packed pair + its two (scale, bias) blocks
+  static constexpr int kQOff = kXStages * kXStage;
   static constexpr int kRsOff = kQOff + kQStages * kQStage;  // [kTN] row scales (fp32)
   static constexpr int kBiasOff = kRsOff + kTN * 4;          // [kBM] output bias (fp32)
   static constexpr int kBarOff = kBiasOff + kBM * 4;
@@ -103,15 +111,6 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                           uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
 // D (+)= A * B with A in tensor memory ([128 lanes][K/2 columns] of f16
 // pairs) and B in shared memory (descriptor)
 __device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
@@ -140,13 +139,6 @@ __device__ __forceinline__ void tmem_wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// D += A * B (the accumulate flag set): every MMA of a k-tile after its first
-__device__ __forceinline__ void tc_mma_f16_acc(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                               uint32_t idesc) {
-  asm volatile("tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 1;" ::"r"(d_tmem), "l"(a_desc),
-               "l"(b_desc), "r"(idesc)
-               : "memory");
-}
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -247,8 +239,9 @@ __device__ __forceinline__ void finish_rows(uint32_t tq, int cg, const float* rs
 
 template <int DT, int G>
 __global__ void __launch_bounds__(kThreads, 1)
-    qgemm_kernel(const __grid_constant__ CUtensorMap amap, const __grid_constant__ CUtensorMap qmap,
-                 const GemmArgs a) {
+    qgemm_kernel(const __grid_constant__ CUtensorMap xmap_tile,
+                 const __grid_constant__ CUtensorMap xmap_pair,
+                 const __grid_constant__ CUtensorMap qmap, const GemmArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
   using L = GemmSmem<SUBG>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -275,9 +268,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int per = (KT + nsplit - 1) / nsplit;
   const int kt0 = split * per;
   const int NKT = min(KT, kt0 + per) - kt0;
+  const int NP = (NKT + 1) / 2;  // k-tile pairs (the last may hold one k-tile)
 
   if (threadIdx.x == 0) {
-    prefetch_tensormap(&amap);
+    prefetch_tensormap(&xmap_tile);
+    prefetch_tensormap(&xmap_pair);
     prefetch_tensormap(&qmap);
     for (int s = 0; s < kXStages; ++s) {
       mbar_init(&xfull[s], 1);
@@ -314,21 +309,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ weights
     if (lane == 0) {
-      // packed weights and the k-tile's (scale, bias) pairs of the kBM rows
-      // (one contiguous block)
+      // per k-tile pair: the packed weights [kBM][128] (zero past K) and the
+      // pair's (scale, bias) blocks (contiguous in sb_tiles; the second only
+      // inside K)
       const uint64_t pol = l2_policy_evict_normal();
-      for (int i = 0; i < NKT; ++i) {
-        const int kt = kt0 + i;
-        const int s = i % kQStages;
-        const uint32_t ph = ((i / kQStages) & 1) ^ 1;
+      for (int j = 0; j < NP; ++j) {
+        const int kt = kt0 + 2 * j;
+        const int s = j % kQStages;
+        const uint32_t ph = ((j / kQStages) & 1) ^ 1;
         if (!mbar_try_wait(&qempty[s], ph)) ok = mbar_wait_bounded(&qempty[s], ph, a.status) && ok;
         uint8_t* st = smem + L::kQOff + s * L::kQStage;
-        mbar_arrive_expect_tx(&qfull[s], L::kQ + L::kSB);
+        const int nsb = kt + 1 < KT ? 2 : 1;
+        mbar_arrive_expect_tx(&qfull[s], L::kQ + nsb * L::kSB);
         tma_load_2d(st, &qmap, kt * kBK, n0, &qfull[s], pol);
         bulk_copy_g2s(st + L::kQ,
                       reinterpret_cast<const uint8_t*>(a.sb_tiles) +
                           (static_cast<size_t>(blockIdx.x) * KT + kt) * L::kSB,
-                      L::kSB, &qfull[s]);
+                      nsb * L::kSB, &qfull[s]);
       }
     }
   } else if (warp == 2) {
@@ -338,13 +335,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       pdl_wait();
       const uint64_t pol = l2_policy_evict_normal();
-      for (int i = 0; i < NKT; ++i) {
-        const int kt = kt0 + i;
-        const int s = i % kXStages;
-        const uint32_t ph = ((i / kXStages) & 1) ^ 1;
+      for (int j = 0; j < NP; ++j) {
+        const int kt = kt0 + 2 * j;
+        const int s = j % kXStages;
+        const uint32_t ph = ((j / kXStages) & 1) ^ 1;
         if (!mbar_try_wait(&xempty[s], ph)) ok = mbar_wait_bounded(&xempty[s], ph, a.status) && ok;
-        mbar_arrive_expect_tx(&xfull[s], L::kX);
-        tma_load_2d(smem + s * L::kX, &amap, kt * kBK, m0, &xfull[s], pol);
+        uint8_t* st = smem + s * L::kXStage;
+        mbar_arrive_expect_tx(&xfull[s], L::kXStage);
+        if (kt + 1 < a.pair_tiles) {
+          tma_load_3d(st, &xmap_pair, 0, m0, kt, &xfull[s], pol);
+        } else {
+          // the ragged end: one copy per k-tile, zero past K
+          tma_load_2d(st, &xmap_tile, kt * kBK, m0, &xfull[s], pol);
+          tma_load_2d(st + L::kX, &xmap_tile, (kt + 1) * kBK, m0, &xfull[s], pol);
+        }
       }
     }
   } else if (warp == 1) {
@@ -361,22 +365,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc = idesc_f16_f32();
       const uint64_t db0 = sw128_kmajor_desc(smem_u32(smem));
       const uint32_t ta0 = tmem_d + kTmemA0;
-      for (int i = 0; i < NKT; ++i) {
-        const int s = i % kXStages, b = i % kABufs;
-        const uint32_t px = (i / kXStages) & 1, pa = (i / kABufs) & 1;
+      for (int j = 0; j < NP; ++j) {
+        const int s = j % kXStages, b = j % kABufs;
+        const uint32_t px = (j / kXStages) & 1, pa = (j / kABufs) & 1;
         if (!mbar_try_wait(&xfull[s], px)) ok = mbar_wait_bounded(&xfull[s], px, a.status) && ok;
         if (!mbar_try_wait(&afull[b], pa)) ok = mbar_wait_bounded(&afull[b], pa, a.status) && ok;
         tc_fence_after();
         // K advances by 16 f16: 32 bytes (2 descriptor units) of the x tile,
-        // 8 columns of the weight tile
-        const uint64_t db = db0 + static_cast<uint64_t>(s * (L::kX >> 4));
-        const uint32_t ta = ta0 + static_cast<uint32_t>(b * 32);
-        tc_mma_f16_ts(tmem_d, ta, db, idesc, i != 0);
+        // 8 columns of the weight pair buffer
+        const uint64_t db = db0 + static_cast<uint64_t>(s * (L::kXStage >> 4));
+        const uint32_t ta = ta0 + static_cast<uint32_t>(b * 64);
+        tc_mma_f16_ts(tmem_d, ta, db, idesc, j != 0);
         tc_mma_f16_ts_acc(tmem_d, ta + 8, db + 2, idesc);
         tc_mma_f16_ts_acc(tmem_d, ta + 16, db + 4, idesc);
         tc_mma_f16_ts_acc(tmem_d, ta + 24, db + 6, idesc);
-        tc_commit(&xempty[s]);  // x tile consumed
-        tc_commit(&aempty[b]);  // dequantised tile consumed
+        if (2 * j + 1 < NKT) {  // the pair's second k-tile
+          const uint64_t db2 = db + static_cast<uint64_t>(L::kX >> 4);
+          tc_mma_f16_ts_acc(tmem_d, ta + 32, db2, idesc);
+          tc_mma_f16_ts_acc(tmem_d, ta + 40, db2 + 2, idesc);
+          tc_mma_f16_ts_acc(tmem_d, ta + 48, db2 + 4, idesc);
+          tc_mma_f16_ts_acc(tmem_d, ta + 56, db2 + 6, idesc);
+        }
+        tc_commit(&xempty[s]);  // the x pair consumed
+        tc_commit(&aempty[b]);  // the dequantised pair consumed
       }
       tc_commit(accum);
     }
@@ -399,38 +410,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const __half2 k1024 = __float2half2_rn(1024.0f);
     const int h = (G == 32) ? (cg >> 1) : 0;  // which 32-wide group of the k-tile
-    const int sw64 = (row >> 1) & 3;
+    const int sw = row & 7;  // 128B swizzle phase of the packed row
     const uint32_t ta_row = tmem_d + kTmemA0 + (static_cast<uint32_t>(quarter * 32) << 16) +
                             static_cast<uint32_t>(cg * 8);
-    for (int i = 0; i < NKT; ++i) {
-      const int s = i % kQStages, b = i % kABufs;
-      const uint32_t pq = (i / kQStages) & 1, pa = ((i / kABufs) & 1) ^ 1;
+    for (int j = 0; j < NP; ++j) {
+      const int s = j % kQStages, b = j % kABufs;
+      const uint32_t pq = (j / kQStages) & 1, pa = ((j / kABufs) & 1) ^ 1;
       if (!mbar_try_wait(&qfull[s], pq)) ok = mbar_wait_bounded(&qfull[s], pq, a.status) && ok;
       if (!mbar_try_wait(&aempty[b], pa)) ok = mbar_wait_bounded(&aempty[b], pa, a.status) && ok;
       tc_fence_after();
       const uint8_t* st = smem + L::kQOff + s * L::kQStage;
-      const __half2 p = reinterpret_cast<const __half2*>(st + L::kQ)[row * SUBG + h];
-      const __half2 s2 = __low2half2(p), b2 = __high2half2(p);
-      // logical 16-byte chunk cg of the 64B-swizzled packed row
-      const uint4 qv = *reinterpret_cast<const uint4*>(st + row * 64 + ((cg ^ sw64) << 4));
-      const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
-      uint32_t out[8];
+      const int nh = min(2, NKT - 2 * j);  // k-tiles in this pair
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t lo = __byte_perm(qw[j], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
-        uint32_t hi = __byte_perm(qw[j], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
-        const __half2 wl = __hfma2(s2, __hsub2(*reinterpret_cast<__half2*>(&lo), k1024), b2);
-        const __half2 wh = __hfma2(s2, __hsub2(*reinterpret_cast<__half2*>(&hi), k1024), b2);
-        out[2 * j] = *reinterpret_cast<const uint32_t*>(&wl);
-        out[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&wh);
+      for (int hh = 0; hh < 2; ++hh) {
+        if (hh < nh) {
+          const __half2 p = reinterpret_cast<const __half2*>(st + L::kQ + hh * L::kSB)[row * SUBG + h];
+          const __half2 s2 = __low2half2(p), b2 = __high2half2(p);
+          // logical 16-byte chunk 4 hh + cg of the 128B-swizzled packed row
+          const uint4 qv =
+              *reinterpret_cast<const uint4*>(st + row * 128 + ((((hh << 2) | cg) ^ sw) << 4));
+          const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w};
+          uint32_t out[8];
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t lo = __byte_perm(qw[q4], 0x64646464u, 0x4140);  // 1024 + q0, 1024 + q1
+            uint32_t hi = __byte_perm(qw[q4], 0x64646464u, 0x4342);  // 1024 + q2, 1024 + q3
+            const __half2 wl = __hfma2(s2, __hsub2(*reinterpret_cast<__half2*>(&lo), k1024), b2);
+            const __half2 wh = __hfma2(s2, __hsub2(*reinterpret_cast<__half2*>(&hi), k1024), b2);
+            out[2 * q4] = *reinterpret_cast<const uint32_t*>(&wl);
+            out[2 * q4 + 1] = *reinterpret_cast<const uint32_t*>(&wh);
+          }
+          tmem_st_32x32b_x8(ta_row + static_cast<uint32_t>(b * 64 + hh * 32), out);
+        }
       }
-      tmem_st_32x32b_x8(ta_row + static_cast<uint32_t>(b * 32), out);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(&afull[b]);
-        mbar_arrive(&qempty[s]);  // packed weights and scales of stage s consumed
+        mbar_arrive(&qempty[s]);  // the pair's packed weights and scales consumed
       }
     }
 
@@ -621,7 +639,7 @@ __global__ void __launch_bounds__(kPrepassThreads)
 }
 
 template <int DT, int G>
-cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, const GemmArgs& a,
+cudaError_t launch_gemm_typed(const GemmActMaps& amaps, const CUtensorMap& qmap, const GemmArgs& a,
                               cudaStream_t stream, bool pdl) {
   using L = GemmSmem<(G == 32) ? 2 : 1>;
   auto kern = qgemm_kernel<DT, G>;
@@ -661,26 +679,26 @@ cudaError_t launch_gemm_typed(const CUtensorMap& amap, const CUtensorMap& qmap, 
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  return cudaLaunchKernelEx(&cfg, kern, amap, qmap, a);
+  return cudaLaunchKernelEx(&cfg, kern, amaps.tile, amaps.pair, qmap, a);
 }
 
 template <int DT>
-cudaError_t launch_gemm_g(int group, const CUtensorMap& amap, const CUtensorMap& qmap,
+cudaError_t launch_gemm_g(int group, const GemmActMaps& amaps, const CUtensorMap& qmap,
                           const GemmArgs& a, cudaStream_t stream, bool pdl) {
   switch (group) {
-    case 32: return launch_gemm_typed<DT, 32>(amap, qmap, a, stream, pdl);
-    case 64: return launch_gemm_typed<DT, 64>(amap, qmap, a, stream, pdl);
-    case 128: return launch_gemm_typed<DT, 128>(amap, qmap, a, stream, pdl);
+    case 32: return launch_gemm_typed<DT, 32>(amaps, qmap, a, stream, pdl);
+    case 64: return launch_gemm_typed<DT, 64>(amaps, qmap, a, stream, pdl);
+    case 128: return launch_gemm_typed<DT, 128>(amaps, qmap, a, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
 
-cudaError_t launch_gemm(int dtype, int group, const CUtensorMap& amap, const CUtensorMap& qmap,
+cudaError_t launch_gemm(int dtype, int group, const GemmActMaps& amaps, const CUtensorMap& qmap,
                         const GemmArgs& a, cudaStream_t stream, bool pdl) {
-  if (dtype == kF16) return launch_gemm_g<kF16>(group, amap, qmap, a, stream, pdl);
-  if (dtype == kBF16) return launch_gemm_g<kBF16>(group, amap, qmap, a, stream, pdl);
+  if (dtype == kF16) return launch_gemm_g<kF16>(group, amaps, qmap, a, stream, pdl);
+  if (dtype == kBF16) return launch_gemm_g<kBF16>(group, amaps, qmap, a, stream, pdl);
   return cudaErrorInvalidValue;
 }
 

@@ -20,6 +20,17 @@ struct GemmArgs {
   int M, N, K, ldy;
   int act;                 // cq::Act
   int splits;              // K split over a (1, 1, splits) cluster: 1, 2 or 4
+  int pair_tiles;          // full 64-wide k-tiles the `pair` activation map covers (0: none)
+};
+
+// The activation maps the GEMM reads (f16 [M, K], 128B swizzle): `tile`
+// copies one 64-wide k-tile of kGemmTN rows (2-D, zero past K and M);
+// `pair` copies two consecutive full k-tiles in one copy (3-D view
+// {64, M, K / 64} with the k-tile stride 128 bytes).
+struct GemmActMaps {
+  CUtensorMap tile;
+  CUtensorMap pair;
+  int pair_tiles;  // K / 64 when K >= 128, else 0 (`pair` unused)
 };
 
 // K split that fills the GPU when the output tiles alone leave most SMs idle:
@@ -27,9 +38,9 @@ struct GemmArgs {
 // distributed shared memory (gemm_splits returns 1, 2 or 4).
 int gemm_splits(int M, int N, int K, int num_sms);
 
-// amap: f16 activations [M, K] (box 64 x kGemmTN, 128B swizzle);
-// qmap: packed weights u8 [N, K] (box 64 x kGemmBN, 64B swizzle).
-cudaError_t launch_gemm(int dtype, int group, const CUtensorMap& amap, const CUtensorMap& qmap,
+// qmap: packed weights u8 [N, K] (box 128 x kGemmBN, 128B swizzle: two
+// k-tiles per copy).
+cudaError_t launch_gemm(int dtype, int group, const GemmActMaps& amaps, const CUtensorMap& qmap,
                         const GemmArgs& args, cudaStream_t stream, bool pdl);
 // bf16 [M, ldx] -> f16 [M, ldo] with row_scale[m] = 2^e (power-of-two per row).
 cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, int ldo,

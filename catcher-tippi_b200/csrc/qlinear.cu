@@ -103,8 +103,9 @@ DeviceContext& device_context(int device) {
   return *contexts[device];
 }
 
-CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
-                        int box_rows, int box_cols, CUtensorMapSwizzle swizzle) {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (encode == nullptr) {
     void* fn = nullptr;
@@ -115,19 +116,53 @@ CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, in
       throw Error(CQ_RUNTIME_ERROR, "cuTensorMapEncodeTiled is unavailable");
     encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
   }
+  return encode;
+}
+
+CUtensorMap encode_map(CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+                       const cuuint64_t* strides, const cuuint32_t* box,
+                       CUtensorMapSwizzle swizzle) {
   CUtensorMap map{};
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};  // bytes per row
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
-  const cuuint32_t estr[2] = {1u, 1u};
-  const CUtensorMapDataType dt =
-      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = encode(&map, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = tensor_map_encoder()(&map, dt, rank, const_cast<void*>(base), dims, strides, box,
+                                    estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     throw Error(CQ_RUNTIME_ERROR, "cuTensorMapEncodeTiled failed with " + std::to_string(r));
   return map;
+}
+
+}  // namespace
+
+CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
+                        int box_rows, int box_cols, CUtensorMapSwizzle swizzle) {
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * elem_bytes};  // bytes per row
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(box_cols), static_cast<cuuint32_t>(box_rows)};
+  const CUtensorMapDataType dt =
+      elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return encode_map(dt, 2, base, dims, strides, box, swizzle);
+}
+
+cq::GemmActMaps make_act_maps(const void* base, int rows, int K, int ld) {
+  cq::GemmActMaps m{};
+  m.tile = make_map_2d(base, 2, rows, K, ld, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int full = K / 64;
+  if (full >= 2) {
+    // {64 k, rows, k-tile}: element (k, r, t) at r * ld + 64 t + k; only the
+    // full k-tiles, so no copy reaches past a row's K elements
+    const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(full)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, 128};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(cq::kGemmTN), 2};
+    m.pair = encode_map(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+    m.pair_tiles = full;
+  } else {
+    m.pair = m.tile;
+    m.pair_tiles = 0;
+  }
+  return m;
 }
 
 // ------------------------------------------------------------------ layer
@@ -169,9 +204,10 @@ void QuantizedLinear::finalize() {
   wmap_ = make_map_2d(q_, 1, N_, K_, K_, 16 * plan_.rt, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
   for (int i = 0; i < 3; ++i)
     wmap_rt_[i] = make_map_2d(q_, 1, N_, K_, K_, 16 << i, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
-  qmap_gemm_ = make_map_2d(q_, 1, N_, K_, K_, cq::kGemmBN, 64, CU_TENSOR_MAP_SWIZZLE_64B);
-  gemm_ok_ = check_f16_range();
+  // K2 copies two 64-wide k-tiles of packed weights at a time
+  gemm_ok_ = K_ >= 128 && check_f16_range();
   if (gemm_ok_) {
+    qmap_gemm_ = make_map_2d(q_, 1, N_, K_, K_, cq::kGemmBN, 128, CU_TENSOR_MAP_SWIZZLE_128B);
     check_cuda(cudaMalloc(&sb_tiles_, cq::sb_tiles_bytes(N_, K_, group_)), "cudaMalloc(sb tiles)");
     check_cuda(cq::build_sb_tiles(dtype_, scales_, biases_, N_, K_, group_, sb_tiles_, nullptr),
                "build sb tiles");
@@ -237,7 +273,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
     row_scale = rs;
   }
   if (a_ptr != amap_ptr_ || a_ld != amap_ld_ || rows != amap_rows_) {
-    amap_ = make_map_2d(a_ptr, 2, rows, K_, a_ld, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_ = make_act_maps(a_ptr, rows, K_, a_ld);
     amap_ptr_ = a_ptr;
     amap_ld_ = a_ld;
     amap_rows_ = rows;
@@ -254,6 +290,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
   g.ldy = ldy;
   g.act = act;
   g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  g.pair_tiles = amap_.pair_tiles;
   check_cuda(cq::launch_gemm(dtype_, group_, amap_, qmap_gemm_, g, stream, pdl_enabled()), "qgemm");
 }
 
@@ -274,7 +311,7 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
   DeviceContext& ctx = device_context(device_);
   DeviceGuard guard(device_);
   if (x16 != amap_pre_ptr_ || rows != amap_pre_rows_) {
-    amap_pre_ = make_map_2d(x16, 2, rows, K_, K_, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_pre_ = make_act_maps(x16, rows, K_, K_);
     amap_pre_ptr_ = x16;
     amap_pre_rows_ = rows;
   }
@@ -290,6 +327,7 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
   g.ldy = ldy;
   g.act = act;
   g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  g.pair_tiles = amap_pre_.pair_tiles;
   check_cuda(cq::launch_gemm(dtype_, group_, amap_pre_, qmap_gemm_, g, stream, pdl_enabled()),
              "qgemm");
 }
@@ -329,7 +367,7 @@ void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows,
   check_cuda(cq::launch_gemm_prepass(x, ldx, rows, K_, scratch, K_, rs, stream, pdl_enabled()),
              "qgemm prepass");
   if (scratch != amap_scratch_ptr_ || rows != amap_scratch_rows_) {
-    amap_scratch_ = make_map_2d(scratch, 2, rows, K_, K_, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    amap_scratch_ = make_act_maps(scratch, rows, K_, K_);
     amap_scratch_ptr_ = scratch;
     amap_scratch_rows_ = rows;
   }
@@ -345,6 +383,7 @@ void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows,
   g.ldy = ldy;
   g.act = act;
   g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  g.pair_tiles = amap_scratch_.pair_tiles;
   check_cuda(cq::launch_gemm(dtype_, group_, amap_scratch_, qmap_gemm_, g, stream, pdl_enabled()),
              "qgemm");
 }

@@ -59,6 +59,9 @@ class DeviceGuard {
 CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, int ld,
                         int box_rows, int box_cols, CUtensorMapSwizzle swizzle);
 
+// The K2 GEMM's activation maps over f16 [rows, K] with row stride ld.
+cq::GemmActMaps make_act_maps(const void* base, int rows, int K, int ld);
+
 // Programmatic dependent launch (PDL) on this thread's kernel launches: on,
 // or as the innermost live PdlScope says.  Encoder and RNNT
 // states set it per chunk (streams that overlap on one GPU can run faster
@@ -170,7 +173,7 @@ class QuantizedLinear {
   cq::GemvPlan plan_{};
   CUtensorMap wmap_{};
   CUtensorMap wmap_rt_[3]{};  // weight maps with 16, 32 and 64-row boxes (plan_gemv_rows)
-  // K2: packed weights with a 64-byte swizzle; scales/biases fit f16
+  // K2: packed weights with a 128-byte swizzle; scales/biases fit f16
   CUtensorMap qmap_gemm_{};
   bool gemm_ok_ = false;
   void* sb_tiles_ = nullptr;  // (scale, bias) pairs in the GEMM's k-tile order
@@ -179,18 +182,18 @@ class QuantizedLinear {
   void* ws_ = nullptr;
   size_t ws_bytes_ = 0;
   int ws_rows_ = 0;
-  // cached activation tensor map
-  CUtensorMap amap_{};
+  // cached activation tensor maps
+  cq::GemmActMaps amap_{};
   const void* amap_ptr_ = nullptr;
   int amap_ld_ = 0, amap_rows_ = 0;
   void forward_gemm(const void* x, int ldx, int rows, void* y, int ldy, int act,
                     cudaStream_t stream);
   // activation tensor map of the scratch-staged path, cached separately
-  CUtensorMap amap_scratch_{};
+  cq::GemmActMaps amap_scratch_{};
   const void* amap_scratch_ptr_ = nullptr;
   int amap_scratch_rows_ = 0;
   // activation tensor map of the prescaled path, cached separately
-  CUtensorMap amap_pre_{};
+  cq::GemmActMaps amap_pre_{};
   const void* amap_pre_ptr_ = nullptr;
   int amap_pre_rows_ = 0;
   bool check_f16_range() const;
