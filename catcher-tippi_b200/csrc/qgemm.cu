@@ -724,11 +724,16 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   const int tiles = ((N + kBM - 1) / kBM) * ((M + kTN - 1) / kTN);
   const int KT = (K + kBK - 1) / kBK;
   // A CTA's k-tiles run at a fixed cadence set by its copy ring, whatever the
-  // number of CTAs in flight, so splitting K over a cluster shortens the call
-  // as long as every slice still has an SM of its own (one wave).
+  // number of CTAs in flight, so splitting K over a cluster shortens the
+  // mainloop as long as every slice still has an SM of its own (one wave);
+  // the cluster reduction and the extra ring fill cost about as much as 16
+  // k-tiles save.  Measured at M = 896 (prepass + GEMM per call, in a graph):
+  // 1024 x 1024: 12.0 / 12.9 / 12.7 us unsplit / 2 / 4; 2048 x 1024: 12.8 /
+  // 14.1 us unsplit / 2; 1024 x 4096: 27.6 / 21.3 / 18.0 us.
+  constexpr int kMinTilesPerSlice = 16;
   for (int s : {4, 2}) {
     const int per = (KT + s - 1) / s;
-    if (tiles * s <= num_sms && KT >= 2 * s && (s - 1) * per < KT) return s;
+    if (tiles * s <= num_sms && per >= kMinTilesPerSlice && (s - 1) * per < KT) return s;
   }
   return 1;
 }
