@@ -103,6 +103,24 @@ cq_status cq_linear_forward_ex(cq_linear* layer, const void* x, int32_t ldx, int
   });
 }
 
+cq_status cq_linear_prescale_activations(cq_linear* layer, const void* x, int32_t ldx,
+                                         int32_t rows, void* x16, float* row_scale, void* stream) {
+  return guarded([&] {
+    need_handle(layer, "layer");
+    layer->impl->prescale(x, ldx, rows, x16, row_scale, static_cast<cudaStream_t>(stream));
+  });
+}
+
+cq_status cq_linear_forward_prescaled(cq_linear* layer, const void* x16, const float* row_scale,
+                                      int32_t rows, void* y, int32_t ldy, cq_act act,
+                                      void* stream) {
+  return guarded([&] {
+    need_handle(layer, "layer");
+    layer->impl->forward_prescaled(x16, row_scale, rows, y, ldy, act,
+                                   static_cast<cudaStream_t>(stream));
+  });
+}
+
 cq_status cq_linear_forward_f32(cq_linear* layer, const float* input, size_t input_len,
                                 int32_t rows, float* output, size_t output_len) {
   return guarded([&] {

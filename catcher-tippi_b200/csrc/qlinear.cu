@@ -332,6 +332,22 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
              "qgemm");
 }
 
+void QuantizedLinear::prescale(const void* x, int ldx, int rows, void* x16, float* row_scale,
+                               cudaStream_t stream) {
+  if (!gemm_for(rows))
+    throw_invalid("the tensor-core activation format applies to bf16 layers at >= " +
+                  std::to_string(cq::kGemmMinRows) + " rows");
+  if (x == nullptr || x16 == nullptr || row_scale == nullptr)
+    throw_invalid("input, prescaled output and row scales must not be null");
+  if (ldx < K_) throw_invalid("input leading dimension is smaller than the layer");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0 || (ldx % 8) != 0 ||
+      (reinterpret_cast<uintptr_t>(x16) & 15) != 0 || (K_ % 8) != 0)
+    throw_invalid("input and prescaled rows must be 16-byte aligned");
+  DeviceGuard guard(device_);
+  check_cuda(cq::launch_gemm_prepass(x, ldx, rows, K_, x16, K_, row_scale, stream, pdl_enabled()),
+             "qgemm prepass");
+}
+
 size_t QuantizedLinear::scratch_bytes_for(int rows) const {
   if (dtype_ != CQ_BF16 || !gemm_ok_ || rows < cq::kGemmMinRows) return 0;
   return align_up(static_cast<size_t>(rows) * K_ * 2, 256) + static_cast<size_t>(rows) * 4;

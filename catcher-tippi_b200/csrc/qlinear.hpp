@@ -128,6 +128,11 @@ class QuantizedLinear {
   // x16 f16 [rows, K] (row stride K) and the per-row inverse scales.
   void forward_prescaled(const void* x16, const float* row_scale, int rows, void* y, int ldy,
                          int act, cudaStream_t stream);
+  // The conversion forward_array does before such a call: x bf16 [rows, ldx]
+  // -> x16 f16 [rows, K] (row stride K) and row_scale [rows], for producers
+  // that hand forward_prescaled their own copy.  Same restriction.
+  void prescale(const void* x, int ldx, int rows, void* x16, float* row_scale,
+                cudaStream_t stream);
 
   // forward_array on the GEMV with one of the RNNT decoder's epilogues
   // (cq::kGemvJointInput / kGemvGreedy, see qgemv.hpp); rows below the GEMM

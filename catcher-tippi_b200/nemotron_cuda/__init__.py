@@ -53,6 +53,8 @@ def lib() -> ctypes.CDLL:
         "cq_linear_forward_f32": ([vp, vp, sz, i32, vp, sz], i32),
         "cq_linear_reserve": ([vp, i32], i32),
         "cq_linear_forward_noalloc": ([vp, vp, i32, i32, vp, i32, i32, vp], i32),
+        "cq_linear_prescale_activations": ([vp, vp, i32, i32, vp, vp, vp], i32),
+        "cq_linear_forward_prescaled": ([vp, vp, vp, i32, vp, i32, i32, vp], i32),
         "cq_linear_input_dims": ([vp], i32),
         "cq_linear_output_dims": ([vp], i32),
         "cq_linear_group_size": ([vp], i32),
@@ -310,6 +312,28 @@ class QuantizedLinear:
         _check(lib().cq_linear_forward_ex(self._h, ctypes.c_void_p(x_ptr), ldx, rows,
                                           ctypes.c_void_p(y_ptr), ldy, ACTS[act],
                                           ctypes.c_void_p(stream)))
+
+    def prescale_activations(self, x, rows: int | None = None, stream=None):
+        """The tensor-core GEMM's activation format for x bf16 [M, >=K] (bf16
+        layers, M >= 256): returns (x16 f16 [M, K], row_scale f32 [M])."""
+        import torch
+        m = x.shape[0] if rows is None else rows
+        x16 = torch.empty((m, self.input_dims), dtype=torch.float16, device=x.device)
+        rs = torch.empty((m,), dtype=torch.float32, device=x.device)
+        _check(lib().cq_linear_prescale_activations(self._h, _ptr(x), x.stride(0), m, _ptr(x16),
+                                                    _ptr(rs), _stream_ptr(stream)))
+        return x16, rs
+
+    def forward_prescaled(self, x16, row_scale, y=None, act: str = "none", stream=None,
+                          rows: int | None = None):
+        """forward on activations from prescale_activations (bit-identical to forward)."""
+        import torch
+        m = x16.shape[0] if rows is None else rows
+        if y is None:
+            y = torch.empty((m, self.output_dims), dtype=torch.bfloat16, device=x16.device)
+        _check(lib().cq_linear_forward_prescaled(self._h, _ptr(x16), _ptr(row_scale), m, _ptr(y),
+                                                 y.stride(0), ACTS[act], _stream_ptr(stream)))
+        return y
 
     def forward_f32(self, input, rows: int) -> np.ndarray:
         """Host f32 in / out (forward_f32, layers.rs:283-296)."""

@@ -122,6 +122,29 @@ cq_status cq_linear_forward_f32(cq_linear *layer, const float *input, size_t inp
                                 int32_t rows, float *output, size_t output_len);
 
 /*
+ * The tensor-core GEMM's activation format, for producers that can emit it
+ * directly (this library's encoder LayerNorm does): x bf16 [rows, ldx] ->
+ * x16 f16 [rows, input_dims] (row stride input_dims, 16-byte aligned) and
+ * row_scale fp32 [rows]; each row is scaled by the power of two that puts its
+ * largest magnitude in [2^14, 2^15), and row_scale holds the inverse, which
+ * the GEMM's epilogue applies.  Only for calls that run the tensor-core GEMM:
+ * bf16 layers at rows >= 256 whose scales fit f16 (else CQ_INVALID_ARGUMENT).
+ * Asynchronous on `stream`.  No reference counterpart: an implementation
+ * format of this library's batched path.
+ */
+cq_status cq_linear_prescale_activations(cq_linear *layer, const void *x, int32_t ldx,
+                                         int32_t rows, void *x16, float *row_scale, void *stream);
+
+/*
+ * cq_linear_forward_ex on activations already in the tensor-core format
+ * (cq_linear_prescale_activations): bit-identical results, without the
+ * conversion launch.  Same restrictions; asynchronous on `stream`.
+ */
+cq_status cq_linear_forward_prescaled(cq_linear *layer, const void *x16, const float *row_scale,
+                                      int32_t rows, void *y, int32_t ldy, cq_act act,
+                                      void *stream);
+
+/*
  * Sizes the layer's workspace for calls of up to max_rows rows.  Calls with
  * rows >= 256 run on the tensor-core GEMM; for bf16 layers that path stages
  * the activations as f16 in a per-layer workspace that is otherwise

@@ -105,3 +105,39 @@ def test_reserve_then_graph_capture(cq, torch_dev, oracle_mod):
 
 def test_device_status_clean_after_gemm(cq, torch_dev):
     assert cq.device_status(0) == 0
+
+
+@pytest.mark.parametrize("act", ["none", "silu"])
+def test_prescaled_path_is_bit_identical(cq, torch_dev, oracle_mod, act):
+    """cq_linear_prescale_activations + cq_linear_forward_prescaled (the
+    format the encoder's LayerNorm emits) give exactly cq_linear_forward_ex's
+    output, which matches the oracle."""
+    torch = torch_dev
+    q, s, b, x, bias = make_case(oracle_mod, 4096, 1024, 896, 64, "bf16", seed=77, with_bias=True)
+    layer = cq.QuantizedLinear.from_packed(q, s, b, bias, 64, "bf16")
+    xd = to_dev(torch, x, "bf16")
+    y_ref = layer.forward(xd, act=act)
+    x16, rs = layer.prescale_activations(xd)
+    y = layer.forward_prescaled(x16, rs, act=act)
+    torch.cuda.synchronize()
+    # row scales are powers of two that put each row's maximum in [2^14, 2^15)
+    amax = x16.float().abs().amax(dim=1)
+    assert bool(((amax >= 2.0 ** 14) & (amax < 2.0 ** 15)).all())
+    assert torch.equal(torch.log2(rs), torch.round(torch.log2(rs)))
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+    assert_parity(from_dev(y), oracle_mod.qmatmul(x, q, s, b, 64, "bf16", bias, act), "bf16",
+                  min_exact=0.6, floor_frac=GEMM_FLOOR, bias_bits=bias, act=act)
+
+
+def test_prescaled_path_rejects_gemv_calls(cq, torch_dev, oracle_mod):
+    torch = torch_dev
+    q, s, b, x, _ = make_case(oracle_mod, 1024, 1024, 100, 64, "bf16", seed=78)
+    layer = cq.QuantizedLinear.from_packed(q, s, b, None, 64, "bf16")
+    xd = to_dev(torch, x, "bf16")
+    with pytest.raises(cq.CQError) as ei:
+        layer.prescale_activations(xd)
+    assert "tensor-core activation format" in str(ei.value)
+    x16 = torch.zeros((100, 1024), dtype=torch.float16, device="cuda")
+    rs = torch.ones((100,), dtype=torch.float32, device="cuda")
+    with pytest.raises(cq.CQError):
+        layer.forward_prescaled(x16, rs)
