@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
 
 // ------------------------------------------------------------------ attention
 
-// Tensor-core attention core.  One CTA (eight warps) per (stream, head, query
+// Tensor-core attention core.  One CTA (sixteen warps) per (stream, head, query
 // group of at most 16): the group's queries with both position biases, the
 // window's keys and values and the position rows are staged as T in shared
 // memory, and three small products run on mma.m16n8k16 with fp32 accumulation:
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
 // K, R and V are T values already (exact MMA operands); the fp32 operands
 // (q + bias, probabilities) enter as a T "hi" part plus a T "lo" remainder,
 // two MMAs each, so products keep ~16 more bits than a single rounding.
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 512;
 constexpr int kAttnMaxQ = 16;
 
 struct AttnLayout {
@@ -312,27 +312,29 @@ __device__ __forceinline__ void ldmatrix_x2_trans(uint32_t& b0, uint32_t& b1, co
                : "r"(smem_u32(p)));
 }
 
-// Copies `rows` rows of hd T values (src(j) gives row j) into a staged tile,
-// zero-filling rows [rows, rows_pad); eight 16-byte loads in flight per thread.
+// Copies `rows` rows of hd T values (src(j) gives row j) into a staged tile
+// with asynchronous 16-byte copies (zero-filling rows [rows, rows_pad)), so
+// every tile of the CTA is in flight at once; the caller waits with
+// cp_async_wait_all before the barrier that publishes the tiles.
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 template <class Src>
 __device__ __forceinline__ void stage_t_rows(uint16_t* dst, int ld, int rows, int rows_pad, int hd,
                                              Src src) {
   const int per_row = hd / 8;
   const int n = rows_pad * per_row;
-  constexpr int kBatch = 8;
-  for (int base = threadIdx.x; base < n; base += blockDim.x * kBatch) {
-    uint4 u[kBatch];
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int i = base + b * blockDim.x;
-      u[b] = make_uint4(0, 0, 0, 0);
-      if (i < n && i / per_row < rows) u[b] = *reinterpret_cast<const uint4*>(src(i / per_row) + (i % per_row) * 8);
-    }
-#pragma unroll
-    for (int b = 0; b < kBatch; ++b) {
-      const int i = base + b * blockDim.x;
-      if (i < n) *reinterpret_cast<uint4*>(dst + (i / per_row) * ld + (i % per_row) * 8) = u[b];
-    }
+  const uint16_t* any = src(0);  // a readable address for the zero-fill copies
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int r = i / per_row, c8 = (i - r * per_row) * 8;
+    const bool valid = r < rows;
+    cp_async_16(dst + r * ld + c8, valid ? src(r) + c8 : any, valid);
   }
 }
 
@@ -341,7 +343,7 @@ __device__ __forceinline__ void stage_t_rows(uint16_t* dst, int ld, int rows, in
 // entries) reads raw[q][key + Q - 1 - q]; position rows depend only on the
 // position value, so one table of vmax + Q - 1 rows serves every V.
 template <int DT>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnArgs a) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int qsplit = a.qsplit;
   const int sh = blockIdx.x / qsplit, qg = blockIdx.x % qsplit;
@@ -424,6 +426,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     *reinterpret_cast<uint4*>(qvh + o) = make_uint4(wh[1][0], wh[1][1], wh[1][2], wh[1][3]);
     *reinterpret_cast<uint4*>(qvl + o) = make_uint4(wl[1][0], wl[1][1], wl[1][2], wl[1][3]);
   }
+  cp_async_wait_all();  // this thread's staged K, V and position rows have landed
   __syncthreads();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
