@@ -25,7 +25,10 @@ def torch_dev(cq):
 
 
 BATCHED = [(4096, 1024), (1024, 4096), (3072, 1024), (2048, 1024), (1025, 640), (2560, 640),
-           (640, 1024)]
+           (640, 1024),
+           # an odd number of k-tiles (the last pair holds one), and a K split
+           # into slices of 18 and 17 k-tiles (M = 896)
+           (640, 576), (1024, 2240)]
 
 
 @pytest.mark.parametrize("n,k", BATCHED)
