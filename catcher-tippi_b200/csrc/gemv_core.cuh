@@ -41,21 +41,15 @@ __device__ __forceinline__ void load_x_raw(const void* __restrict__ x, int ldx, 
 }
 
 // Converts this lane's 16 raw activation values into f16 MMA B-fragments and
-// returns the per-half sums of the converted values (reduced over the 4 lanes
-// of the quad) and the inverse of the power-of-two scale that was applied.
-template <int DT, int G>
+// returns the inverse of the power-of-two scale that was applied (bf16: one
+// scale per token and 64-wide sub-block, shared by the quad's 4 lanes).
+template <int DT>
 __device__ __forceinline__ void x_frag(const uint4& r0, const uint4& r1, uint32_t (&xb)[8],
-                                       float (&xs)[2], float& inv) {
+                                       float& inv) {
   const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-  float s0 = 0.f, s1 = 0.f;
   if constexpr (DT == kF16) {
 #pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      xb[p] = w[p];
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[p]));
-      if (p < 4) s0 += f.x + f.y;
-      else s1 += f.x + f.y;
-    }
+    for (int p = 0; p < 8; ++p) xb[p] = w[p];
     inv = 1.0f;
   } else {
     float v[16];
@@ -79,21 +73,7 @@ __device__ __forceinline__ void x_frag(const uint4& r0, const uint4& r1, uint32_
     for (int p = 0; p < 8; ++p) {
       const __half2 h = __floats2half2_rn(v[2 * p] * scale, v[2 * p + 1] * scale);
       xb[p] = *reinterpret_cast<const uint32_t*>(&h);
-      const float2 f = __half22float2(h);
-      if (p < 4) s0 += f.x + f.y;
-      else s1 += f.x + f.y;
     }
-  }
-  s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 1);
-  s0 += __shfl_xor_sync(0xFFFFFFFFu, s0, 2);
-  s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 1);
-  s1 += __shfl_xor_sync(0xFFFFFFFFu, s1, 2);
-  if constexpr (G >= 64) {
-    xs[0] = s0 + s1;
-    xs[1] = 0.f;
-  } else {
-    xs[0] = s0;
-    xs[1] = s1;
   }
 }
 
@@ -120,20 +100,37 @@ struct XOperands {
 };
 
 // xr: this lane's raw loads (load_x_raw) for tokens r4 and r4 + 8.
+// The per-(token, group) sums of the converted activations, which the group
+// term of the epilogue needs, come from the tensor pipe: an MMA with an
+// all-ones A fragment sums each token's sixteen k-slots of a k-step, and
+// lands them in the accumulator layout the epilogue reads (columns 2c and
+// 2c + 1 = tokens 2c and 2c + 1), so no unpacking, adds or shuffles are
+// needed for them.
 template <int DT, int G>
 __device__ __forceinline__ XOperands<G> x_operands(const uint4 (&xr)[2][2], int lane) {
   constexpr int SUBG = XOperands<G>::SUBG;
   const int c = lane & 3;
   XOperands<G> o;
-  float xs[2][2], inv[2];
-  x_frag<DT, G>(xr[0][0], xr[0][1], o.xb[0], xs[0], inv[0]);
-  x_frag<DT, G>(xr[1][0], xr[1][1], o.xb[1], xs[1], inv[1]);
+  float inv[2];
+  x_frag<DT>(xr[0][0], xr[0][1], o.xb[0], inv[0]);
+  x_frag<DT>(xr[1][0], xr[1][1], o.xb[1], inv[1]);
+  constexpr uint32_t kOnes = 0x3C003C00u;  // f16 1.0 twice
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
+    float sm[SUBG][4];
+#pragma unroll
+    for (int h = 0; h < SUBG; ++h)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sm[h][e] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const int h = (SUBG == 2) ? (s >> 1) : 0;  // k-steps 0, 1 / 2, 3: the two 32-wide groups
+      mma_16816_f16(sm[h], kOnes, kOnes, kOnes, kOnes, o.xb[nt][2 * s], o.xb[nt][2 * s + 1]);
+    }
 #pragma unroll
     for (int h = 0; h < SUBG; ++h) {
-      o.xsA[nt][h] = __shfl_sync(0xFFFFFFFFu, xs[nt][h], 8 * c);
-      o.xsB[nt][h] = __shfl_sync(0xFFFFFFFFu, xs[nt][h], 8 * c + 4);
+      o.xsA[nt][h] = sm[h][0];
+      o.xsB[nt][h] = sm[h][1];
     }
     o.ivA[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c);
     o.ivB[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c + 4);
