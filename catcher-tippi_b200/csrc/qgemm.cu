@@ -53,9 +53,7 @@ namespace cq {
 namespace {
 
 constexpr int kBM = kGemmBN;  // weight rows per CTA: the MMA's M (A operand, in tensor memory)
-constexpr int kTN = kGemmTN;  // tokens per CTA: the MMA's N (B operand, in shared memory)
 constexpr int kBK = 64;       // k per MMA group: one 128-byte swizzle atom of f16 (four K=16 MMAs)
-constexpr int kXStages = 3;   // activation ring of k-tile pairs (a stage is freed by the MMA)
 constexpr int kQStages = 3;   // packed-weight ring of k-tile pairs (freed by the dequant warps)
 constexpr int kABufs = 3;     // dequantised weight pairs in tensor memory
 constexpr int kDequantWarps = 16;
@@ -66,11 +64,22 @@ constexpr int kDequantWarp0 = 3;
 // K) from column 256
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA0 = 256;
-static_assert(kTN <= 256 && kTN % 32 == 0 && kBM == 128, "tile shape");
+// Tokens per CTA (the MMA's N, the B operand in shared memory): kGemmTN for
+// wide layers, kGemmTNSmall where kGemmTN-token tiles would leave most SMs
+// idle; the activation ring of k-tile pairs (a stage is freed by the MMA)
+// gets what the shared memory leaves.
+template <int TN>
+struct TileShape {
+  static constexpr int kTN = TN;
+  static constexpr int kXStages = TN > 128 ? 3 : 4;
+  static_assert(TN <= 256 && TN % 32 == 0 && kBM == 128, "tile shape");
+};
 static_assert(kTmemA0 + 64 * kABufs <= kTmemCols, "tensor memory budget");
 
-template <int SUBG>
+template <int SUBG, int TN>
 struct GemmSmem {
+  static constexpr int kTN = TileShape<TN>::kTN;
+  static constexpr int kXStages = TileShape<TN>::kXStages;
   static constexpr int kX = kTN * kBK * 2;    // one k-tile of x, f16, 128B swizzle
   static constexpr int kXStage = 2 * kX;      // a k-tile pair: [2][kTN][64] f16
   static constexpr int kQ = kBM * 2 * kBK;    // packed u8 weights of a pair, [kBM][128], 128B swizzle
@@ -171,9 +180,10 @@ __device__ __forceinline__ uint64_t sw128_kmajor_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor: f32 accumulate, f16 A and B, both K-major, M = kBM,
-// N = kTN.
+// N = TN.
+template <int TN>
 __host__ __device__ constexpr uint32_t idesc_f16_f32() {
-  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(TN >> 3) << 17) |
          (static_cast<uint32_t>(kBM >> 4) << 24);
 }
 
@@ -216,11 +226,11 @@ __device__ __forceinline__ uint16_t finish_value_any(float acc, float rs, float 
 // The single-CTA epilogue of one thread: its weight row (tensor-memory lane)
 // over every fourth 32-token chunk from cg on, into the [token][row] staging
 // tile (`out` already points at the row's column; `pitch` in elements).
-template <int DT, int ACT, bool BIAS>
+template <int DT, int ACT, bool BIAS, int TN>
 __device__ __forceinline__ void finish_rows(uint32_t tq, int cg, const float* rs_s, float bias,
                                             uint16_t* out, int pitch) {
 #pragma unroll 1
-  for (int c = cg; c < kTN / 32; c += 4) {
+  for (int c = cg; c < TN / 32; c += 4) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tq + static_cast<uint32_t>(c * 32), r);
     tmem_wait_ld();
@@ -237,13 +247,15 @@ __device__ __forceinline__ void finish_rows(uint32_t tq, int cg, const float* rs
   }
 }
 
-template <int DT, int G>
+template <int DT, int G, int TN>
 __global__ void __launch_bounds__(kThreads, 1)
     qgemm_kernel(const __grid_constant__ CUtensorMap xmap_tile,
                  const __grid_constant__ CUtensorMap xmap_pair,
                  const __grid_constant__ CUtensorMap qmap, const GemmArgs a) {
   constexpr int SUBG = (G == 32) ? 2 : 1;
-  using L = GemmSmem<SUBG>;
+  using L = GemmSmem<SUBG, TN>;
+  constexpr int kTN = L::kTN;
+  constexpr int kXStages = L::kXStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzled tiles
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -362,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // 0-13) holds address >> 4 and every buffer lies below 227 KB, so adding
       // never carries out of it; a tensor-memory column is the address's low
       // half.
-      constexpr uint32_t idesc = idesc_f16_f32();
+      constexpr uint32_t idesc = idesc_f16_f32<kTN>();
       const uint64_t db0 = sw128_kmajor_desc(smem_u32(smem));
       const uint32_t ta0 = tmem_d + kTmemA0;
       for (int j = 0; j < NP; ++j) {
@@ -489,14 +501,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tq = tmem_d + (static_cast<uint32_t>(quarter * 32) << 16);
       // the activation and the bias are uniform: one specialised loop each
       if (a.act == kActSilu) {
-        if (has_bias) finish_rows<DT, kActSilu, true>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
-        else finish_rows<DT, kActSilu, false>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        if (has_bias) finish_rows<DT, kActSilu, true, kTN>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        else finish_rows<DT, kActSilu, false, kTN>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
       } else if (a.act == kActRelu) {
-        if (has_bias) finish_rows<DT, kActRelu, true>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
-        else finish_rows<DT, kActRelu, false>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        if (has_bias) finish_rows<DT, kActRelu, true, kTN>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        else finish_rows<DT, kActRelu, false, kTN>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
       } else {
-        if (has_bias) finish_rows<DT, kActNone, true>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
-        else finish_rows<DT, kActNone, false>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        if (has_bias) finish_rows<DT, kActNone, true, kTN>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
+        else finish_rows<DT, kActNone, false, kTN>(tq, cg, rs_s, bias_v, ot, kRowBytes / 2);
       }
       asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
       const bool vec_ok = (a.ldy % 8) == 0 && (reinterpret_cast<uintptr_t>(a.y) & 15) == 0;
@@ -638,14 +650,15 @@ __global__ void __launch_bounds__(kPrepassThreads)
   }
 }
 
-template <int DT, int G>
+template <int DT, int G, int TN>
 cudaError_t launch_gemm_typed(const GemmActMaps& amaps, const CUtensorMap& qmap, const GemmArgs& a,
                               cudaStream_t stream, bool pdl) {
-  using L = GemmSmem<(G == 32) ? 2 : 1>;
-  auto kern = qgemm_kernel<DT, G>;
+  using L = GemmSmem<(G == 32) ? 2 : 1, TN>;
+  auto kern = qgemm_kernel<DT, G, TN>;
   static bool configured = false;
   const int smem = L::kBytes + 1024;  // + alignment slack
-  static_assert(GemmSmem<(G == 32) ? 2 : 1>::kBytes + 1024 <= 227 * 1024, "smem budget");
+  static_assert(L::kBytes + 1024 <= 227 * 1024, "smem budget");
+  if (amaps.tn != TN) return cudaErrorInvalidValue;  // the maps' boxes are TN rows
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
@@ -659,7 +672,7 @@ cudaError_t launch_gemm_typed(const GemmActMaps& amaps, const CUtensorMap& qmap,
     if ((splits - 1) * per >= KT) return cudaErrorInvalidValue;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + kBM - 1) / kBM, (a.M + kTN - 1) / kTN, splits);
+  cfg.gridDim = dim3((a.N + kBM - 1) / kBM, (a.M + TN - 1) / TN, splits);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
@@ -682,13 +695,21 @@ cudaError_t launch_gemm_typed(const GemmActMaps& amaps, const CUtensorMap& qmap,
   return cudaLaunchKernelEx(&cfg, kern, amaps.tile, amaps.pair, qmap, a);
 }
 
+template <int DT, int G>
+cudaError_t launch_gemm_tn(const GemmActMaps& amaps, const CUtensorMap& qmap, const GemmArgs& a,
+                           cudaStream_t stream, bool pdl) {
+  if (a.tn == kGemmTN) return launch_gemm_typed<DT, G, kGemmTN>(amaps, qmap, a, stream, pdl);
+  if (a.tn == kGemmTNSmall) return launch_gemm_typed<DT, G, kGemmTNSmall>(amaps, qmap, a, stream, pdl);
+  return cudaErrorInvalidValue;
+}
+
 template <int DT>
 cudaError_t launch_gemm_g(int group, const GemmActMaps& amaps, const CUtensorMap& qmap,
                           const GemmArgs& a, cudaStream_t stream, bool pdl) {
   switch (group) {
-    case 32: return launch_gemm_typed<DT, 32>(amaps, qmap, a, stream, pdl);
-    case 64: return launch_gemm_typed<DT, 64>(amaps, qmap, a, stream, pdl);
-    case 128: return launch_gemm_typed<DT, 128>(amaps, qmap, a, stream, pdl);
+    case 32: return launch_gemm_tn<DT, 32>(amaps, qmap, a, stream, pdl);
+    case 64: return launch_gemm_tn<DT, 64>(amaps, qmap, a, stream, pdl);
+    case 128: return launch_gemm_tn<DT, 128>(amaps, qmap, a, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -720,8 +741,21 @@ cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, 
                             ldx, M, K, reinterpret_cast<__half*>(xo), ldo, row_scale);
 }
 
-int gemm_splits(int M, int N, int K, int num_sms) {
-  const int tiles = ((N + kBM - 1) / kBM) * ((M + kTN - 1) / kTN);
+int gemm_tile_tokens(int M, int N, int K, int num_sms) {
+  // The narrower tile when its tiles still fit one wave: at M = 896, N = 1024
+  // and 2048 run on 56 / 112 CTAs instead of 32 / 64 (prepass + GEMM per
+  // call in a graph: 12.0 -> 10.4 us and 12.8 -> 10.9 us) -- unless the wide
+  // tile can split K four ways in one wave, which does better (1024 x 4096:
+  // 18.0 us against 18.8 us for the narrow tile split two ways).
+  const int nt = (N + kBM - 1) / kBM;
+  if (nt * ((M + kGemmTNSmall - 1) / kGemmTNSmall) > num_sms) return kGemmTN;
+  const int KT = (K + kBK - 1) / kBK;
+  if (nt * ((M + kGemmTN - 1) / kGemmTN) * 4 <= num_sms && (KT + 3) / 4 >= 16) return kGemmTN;
+  return kGemmTNSmall;
+}
+
+int gemm_splits(int M, int N, int K, int num_sms, int tn) {
+  const int tiles = ((N + kBM - 1) / kBM) * ((M + tn - 1) / tn);
   const int KT = (K + kBK - 1) / kBK;
   // A CTA's k-tiles run at a fixed cadence set by its copy ring, whatever the
   // number of CTAs in flight, so splitting K over a cluster shortens the
@@ -738,7 +772,9 @@ int gemm_splits(int M, int N, int K, int num_sms) {
   return 1;
 }
 
-size_t gemm_smem_bytes() { return GemmSmem<2>::kBytes + 1024; }
+size_t gemm_smem_bytes() {
+  return std::max(GemmSmem<2, kGemmTN>::kBytes, GemmSmem<2, kGemmTNSmall>::kBytes) + 1024;
+}
 
 // (scale, bias) pairs as f16 in the GEMM's k-tile order:
 // out[ntile][ktile][row][h], h over the 32-wide halves of a 64-wide k-tile

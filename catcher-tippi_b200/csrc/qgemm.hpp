@@ -9,6 +9,7 @@ namespace cq {
 
 constexpr int kGemmBN = 128;       // output columns (weight rows) per CTA
 constexpr int kGemmTN = 224;       // rows (tokens) per CTA: 896 = 4 x 224
+constexpr int kGemmTNSmall = 128;  // the narrower tile for layers whose kGemmTN tiles leave SMs idle
 constexpr int kGemmMinRows = 256;  // below this the GEMV (K1) is used
 
 struct GemmArgs {
@@ -21,22 +22,28 @@ struct GemmArgs {
   int act;                 // cq::Act
   int splits;              // K split over a (1, 1, splits) cluster: 1, 2 or 4
   int pair_tiles;          // full 64-wide k-tiles the `pair` activation map covers (0: none)
+  int tn;                  // tokens per CTA: kGemmTN or kGemmTNSmall (gemm_tile_tokens)
 };
 
 // The activation maps the GEMM reads (f16 [M, K], 128B swizzle): `tile`
-// copies one 64-wide k-tile of kGemmTN rows (2-D, zero past K and M);
+// copies one 64-wide k-tile of `tn` rows (2-D, zero past K and M);
 // `pair` copies two consecutive full k-tiles in one copy (3-D view
 // {64, M, K / 64} with the k-tile stride 128 bytes).
 struct GemmActMaps {
   CUtensorMap tile;
   CUtensorMap pair;
   int pair_tiles;  // K / 64 when K >= 128, else 0 (`pair` unused)
+  int tn;          // rows per box: the call's GemmArgs::tn
 };
 
 // K split that fills the GPU when the output tiles alone leave most SMs idle:
 // the CTAs of one cluster accumulate disjoint k ranges and reduce through
 // distributed shared memory (gemm_splits returns 1, 2 or 4).
-int gemm_splits(int M, int N, int K, int num_sms);
+int gemm_splits(int M, int N, int K, int num_sms, int tn);
+// Tokens per CTA for an M x N x K call: kGemmTNSmall when its tiles fit one
+// wave of num_sms CTAs and the wide tile cannot split K four ways, else
+// kGemmTN.
+int gemm_tile_tokens(int M, int N, int K, int num_sms);
 
 // qmap: packed weights u8 [N, K] (box 128 x kGemmBN, 128B swizzle: two
 // k-tiles per copy).

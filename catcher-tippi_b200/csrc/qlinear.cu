@@ -145,16 +145,17 @@ CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, in
   return encode_map(dt, 2, base, dims, strides, box, swizzle);
 }
 
-cq::GemmActMaps make_act_maps(const void* base, int rows, int K, int ld) {
+cq::GemmActMaps make_act_maps(const void* base, int rows, int K, int ld, int tn) {
   cq::GemmActMaps m{};
-  m.tile = make_map_2d(base, 2, rows, K, ld, cq::kGemmTN, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  m.tn = tn;
+  m.tile = make_map_2d(base, 2, rows, K, ld, tn, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   const int full = K / 64;
   if (full >= 2) {
     // {64 k, rows, k-tile}: element (k, r, t) at r * ld + 64 t + k; only the
     // full k-tiles, so no copy reaches past a row's K elements
     const cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), static_cast<cuuint64_t>(full)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, 128};
-    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(cq::kGemmTN), 2};
+    const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(tn), 2};
     m.pair = encode_map(CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, base, dims, strides, box,
                         CU_TENSOR_MAP_SWIZZLE_128B);
     m.pair_tiles = full;
@@ -273,7 +274,7 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
     row_scale = rs;
   }
   if (a_ptr != amap_ptr_ || a_ld != amap_ld_ || rows != amap_rows_) {
-    amap_ = make_act_maps(a_ptr, rows, K_, a_ld);
+    amap_ = make_act_maps(a_ptr, rows, K_, a_ld, cq::gemm_tile_tokens(rows, N_, K_, ctx.num_sms));
     amap_ptr_ = a_ptr;
     amap_ld_ = a_ld;
     amap_rows_ = rows;
@@ -289,7 +290,8 @@ void QuantizedLinear::forward_gemm(const void* x, int ldx, int rows, void* y, in
   g.K = K_;
   g.ldy = ldy;
   g.act = act;
-  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  g.tn = amap_.tn;
+  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms, g.tn);
   g.pair_tiles = amap_.pair_tiles;
   check_cuda(cq::launch_gemm(dtype_, group_, amap_, qmap_gemm_, g, stream, pdl_enabled()), "qgemm");
 }
@@ -311,7 +313,7 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
   DeviceContext& ctx = device_context(device_);
   DeviceGuard guard(device_);
   if (x16 != amap_pre_ptr_ || rows != amap_pre_rows_) {
-    amap_pre_ = make_act_maps(x16, rows, K_, K_);
+    amap_pre_ = make_act_maps(x16, rows, K_, K_, cq::gemm_tile_tokens(rows, N_, K_, ctx.num_sms));
     amap_pre_ptr_ = x16;
     amap_pre_rows_ = rows;
   }
@@ -326,7 +328,8 @@ void QuantizedLinear::forward_prescaled(const void* x16, const float* row_scale,
   g.K = K_;
   g.ldy = ldy;
   g.act = act;
-  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  g.tn = amap_pre_.tn;
+  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms, g.tn);
   g.pair_tiles = amap_pre_.pair_tiles;
   check_cuda(cq::launch_gemm(dtype_, group_, amap_pre_, qmap_gemm_, g, stream, pdl_enabled()),
              "qgemm");
@@ -383,7 +386,7 @@ void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows,
   check_cuda(cq::launch_gemm_prepass(x, ldx, rows, K_, scratch, K_, rs, stream, pdl_enabled()),
              "qgemm prepass");
   if (scratch != amap_scratch_ptr_ || rows != amap_scratch_rows_) {
-    amap_scratch_ = make_act_maps(scratch, rows, K_, K_);
+    amap_scratch_ = make_act_maps(scratch, rows, K_, K_, cq::gemm_tile_tokens(rows, N_, K_, ctx.num_sms));
     amap_scratch_ptr_ = scratch;
     amap_scratch_rows_ = rows;
   }
@@ -398,7 +401,8 @@ void QuantizedLinear::forward_array_in_scratch(const void* x, int ldx, int rows,
   g.K = K_;
   g.ldy = ldy;
   g.act = act;
-  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms);
+  g.tn = amap_scratch_.tn;
+  g.splits = cq::gemm_splits(rows, N_, K_, ctx.num_sms, g.tn);
   g.pair_tiles = amap_scratch_.pair_tiles;
   check_cuda(cq::launch_gemm(dtype_, group_, amap_scratch_, qmap_gemm_, g, stream, pdl_enabled()),
              "qgemm");

@@ -60,7 +60,7 @@ CUtensorMap make_map_2d(const void* base, int elem_bytes, int rows, int cols, in
                         int box_rows, int box_cols, CUtensorMapSwizzle swizzle);
 
 // The K2 GEMM's activation maps over f16 [rows, K] with row stride ld.
-cq::GemmActMaps make_act_maps(const void* base, int rows, int K, int ld);
+cq::GemmActMaps make_act_maps(const void* base, int rows, int K, int ld, int tn);
 
 // Programmatic dependent launch (PDL) on this thread's kernel launches: on,
 // or as the innermost live PdlScope says.  Encoder and RNNT
