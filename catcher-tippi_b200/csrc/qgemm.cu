@@ -6,8 +6,9 @@
 // the operation behind QuantizedLinear::forward_array
 // (crates/nemotron-mlx/src/model/layers.rs:298-310) at batched row counts.
 //
-// Per CTA: one output tile of 128 weight rows x 224 tokens over the full K
-// (or its slice of a cluster's K split), 19 warps.  Everything moves in
+// Per CTA: one output tile of 128 weight rows x TN tokens (224, or 128 where
+// 224-token tiles would leave most SMs idle; the sizes below are for 224)
+// over the full K (or its slice of a cluster's K split), 19 warps.  Everything moves in
 // pairs of 64-wide k-tiles (128 k): one copy per pair for the activations
 // and for the weights, one hand-off per pair from the dequantisers, and the
 // MMA issuer waits and commits once per pair around eight MMAs (measured on
