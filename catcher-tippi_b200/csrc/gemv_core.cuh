@@ -20,6 +20,17 @@
 
 namespace cq {
 
+// Column of (weight row, token) in the cross-warp reduction buffers
+// ([warp][row][16] floats): the token index is XORed with an even mask built
+// from row bits 1..3 (bit 1 -> 8, bit 2 -> 2, bit 3 -> 4).  The float2
+// partial stores of a half-warp (rows r4 = 0..3 x lanes c) then fall on
+// disjoint banks, and the sums read rows-fastest (32 lanes = 16 rows x 2
+// tokens at 16 rows per CTA) hit 32 distinct banks; with 32 or more rows the
+// reads are 2-way.  An even mask keeps each float2 pair adjacent.
+__device__ __forceinline__ int red_col(int row, int tok) {
+  return tok ^ (((row & 2) << 2) | ((row & 12) >> 1));
+}
+
 // Raw activation loads of one token for one 64-wide sub-block (this lane's 16
 // values; zeros past M and past K):
 //   G >= 64: k = kb + 16c + [0, 16)

@@ -61,7 +61,7 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int rt, int sb_per_cta, int
   off += static_cast<size_t>(sb_per_cta) * subg * rb * sizeof(float2);
   L.biasm = off;  // [rb] output bias
   off += static_cast<size_t>(rb) * sizeof(float);
-  L.red = off;  // [kNW][rb][16] per-warp partials
+  L.red = off;  // [kNW][rb][16] per-warp partials (columns swizzled by red_col)
   off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
   L.fin = off;  // [ksplit][rb][16]: CTA partials pushed into the cluster leader
   // (at least 16 u64: the per-token maxima of the greedy epilogue)
@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
       sv[i] = 0.f;
       bv[i] = 0.f;
       if (e < total) {
-        const int row = e / per_row, jh = e - row * per_row;
+        const int row = e % RB, jh = e / RB;  // rows fastest: conflict-free float2 stores
         const int n = n0 + row;
         const int kfirst = (sb0 + jh / SUBG) * 64 + (jh % SUBG) * 32;
         if (n < a.N && kfirst < a.K) {
@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
     for (int i = 0; i < kMaxSbPerThread; ++i) {
       const int e = tid + i * kThreads;
       if (e < total) {
-        const int row = e / per_row, jh = e - row * per_row;
+        const int row = e % RB, jh = e / RB;  // rows fastest: conflict-free float2 stores
         sbsm[jh * RB + row] = make_float2(sv[i], fmaf(-1024.0f, sv[i], bv[i]));
       }
     }
@@ -296,9 +296,9 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
       const int ra = 16 * i + r4, rb = ra + 8;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        *reinterpret_cast<float2*>(&red[(warp * RB + ra) * 16 + 8 * nt + 2 * c]) =
+        *reinterpret_cast<float2*>(&red[(warp * RB + ra) * 16 + red_col(ra, 8 * nt + 2 * c)]) =
             make_float2(acc[i][nt][0], acc[i][nt][1]);
-        *reinterpret_cast<float2*>(&red[(warp * RB + rb) * 16 + 8 * nt + 2 * c]) =
+        *reinterpret_cast<float2*>(&red[(warp * RB + rb) * 16 + red_col(rb, 8 * nt + 2 * c)]) =
             make_float2(acc[i][nt][2], acc[i][nt][3]);
       }
     }
@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
         const int row = e % RB, tok = e / RB;
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kNW; ++w) v += red[(w * RB + row) * 16 + tok];
+        for (int w = 0; w < kNW; ++w) v += red[(w * RB + row) * 16 + red_col(row, tok)];
         const int n = n0 + row, m = mt * 16 + tok;
         if (n < a.N && m < a.M) {
           const float o = epilogue_value<DT>(v, has_bias, biasm[row], a.act);
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
       for (int e = tid; e < RB * 16; e += kThreads) {
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kNW; ++w) v += red[w * RB * 16 + e];
+        for (int w = 0; w < kNW; ++w) v += red[(w * RB + e / 16) * 16 + red_col(e / 16, e % 16)];
         st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
       }
       cluster_sync_all();

@@ -53,7 +53,7 @@ __host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg, int rb, 
   off += kMaxSb * 8;
   L.sbsm = off;  // [sbn * subg][rb] (s, b - 1024 s)
   off += static_cast<size_t>(sbn) * subg * rb * sizeof(float2);
-  L.red = off;  // [8][rb][16] per-warp partials
+  L.red = off;  // [8][rb][16] per-warp partials (columns swizzled by red_col)
   off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
   L.fin = off;  // [fin_bufs tiles in flight][2 products][rb][16] of rank 0's band
   off += static_cast<size_t>(fin_bufs) * 2 * rb * 16 * sizeof(float);
@@ -235,9 +235,9 @@ __global__ void __launch_bounds__(kThreads, MINB)
       const int ra = 16 * i + r4, rb = ra + 8;
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        *reinterpret_cast<float2*>(&red[(warp * kRB + ra) * 16 + 8 * nt + 2 * c]) =
+        *reinterpret_cast<float2*>(&red[(warp * kRB + ra) * 16 + red_col(ra, 8 * nt + 2 * c)]) =
             make_float2(acc[i][nt][0], acc[i][nt][1]);
-        *reinterpret_cast<float2*>(&red[(warp * kRB + rb) * 16 + 8 * nt + 2 * c]) =
+        *reinterpret_cast<float2*>(&red[(warp * kRB + rb) * 16 + red_col(rb, 8 * nt + 2 * c)]) =
             make_float2(acc[i][nt][2], acc[i][nt][3]);
       }
     }
@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
       for (int e = tid; e < kRB * 16; e += kThreads) {
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
+        for (int w = 0; w < kNW; ++w) v += red[(w * kRB + e / 16) * 16 + red_col(e / 16, e % 16)];
         fbuf[kRB * 16 + e] = v;
       }
       __syncthreads();
@@ -261,7 +261,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
       for (int e = tid; e < kRB * 16; e += kThreads) {
         float v = 0.f;
 #pragma unroll
-        for (int w = 0; w < kNW; ++w) v += red[w * kRB * 16 + e];
+        for (int w = 0; w < kNW; ++w) v += red[(w * kRB + e / 16) * 16 + red_col(e / 16, e % 16)];
         st_dsmem_f32(slot + static_cast<uint32_t>(e * sizeof(float)), v);
       }
       cluster_sync_all();
