@@ -1,16 +1,19 @@
-// Arithmetic of the small-M dequant-GEMV (K1, qgemv.cu): activation loads and
-// their conversion to f16 MMA operands, the per-64-k-sub-block tensor-core
-// step over a weight tile in shared memory, and the output rounding.
+// Arithmetic of the small-M dequant-GEMV (K1, qgemv.cu): activation loads,
+// the per-64-k-sub-block tensor-core step over a weight tile in shared
+// memory, and the output rounding.
 //
 // Operation: y[m, n] = sum_k x[m, k] * (s[n, k/g] * q[n, k] + b[n, k/g]) in
 // the MLX affine INT8 layout (QuantizedLinear::forward_array,
 // crates/nemotron-mlx/src/model/layers.rs:298-310).  Weight rows are the MMA M
-// dimension, tokens the N dimension (two n8 tiles = 16 tokens).  A weight byte
-// q becomes the f16 value 1024 + q with one PRMT (bits 0x64qq), exact; the
+// dimension, tokens the N dimension (two n8 tiles = 16 tokens).  The
+// activations are the B operand in their own type, as loaded; the weight
+// bytes become exact values of that type offset by a constant o, and the
 // offset is folded into the group bias term
-//     y += s * sum(x * (1024 + q)) + (b - 1024 s) * sum(x)
-// so the dequantised weight is never rounded.  bf16 activations move to f16
-// with a per-(token, 64-wide sub-block) power-of-two scale undone in fp32.
+//     y += s * sum(x * (o + q)) + (b - o s) * sum(x)
+// so the dequantised weight is never rounded:
+//   f16:  q -> 1024 + q with one PRMT (bits 0x64qq), o = 1024;
+//   bf16: q = l + 128 h (l < 128) -> two A fragments, 128 + l (bits 0x43,l)
+//         and 128 h (0x4300 or 0), accumulated by two MMAs, o = 128.
 // Each lane reads 16 contiguous weight bytes per row; the k-slot order of the
 // MMA fragments is permuted identically for A and B, so the MLX layout is
 // consumed as is.
@@ -19,6 +22,12 @@
 #include "common.cuh"
 
 namespace cq {
+
+// The constant o that the A-fragment values of a weight byte q carry (o + q).
+template <int DT>
+__host__ __device__ constexpr float weight_offset() {
+  return DT == kBF16 ? 128.0f : 1024.0f;
+}
 
 // Column of (weight row, token) in the cross-warp reduction buffers
 // ([warp][row][16] floats): the token index is XORed with an even mask built
@@ -51,43 +60,6 @@ __device__ __forceinline__ void load_x_raw(const void* __restrict__ x, int ldx, 
   }
 }
 
-// Converts this lane's 16 raw activation values into f16 MMA B-fragments and
-// returns the inverse of the power-of-two scale that was applied (bf16: one
-// scale per token and 64-wide sub-block, shared by the quad's 4 lanes).
-template <int DT>
-__device__ __forceinline__ void x_frag(const uint4& r0, const uint4& r1, uint32_t (&xb)[8],
-                                       float& inv) {
-  const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
-  if constexpr (DT == kF16) {
-#pragma unroll
-    for (int p = 0; p < 8; ++p) xb[p] = w[p];
-    inv = 1.0f;
-  } else {
-    float v[16];
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      v[2 * p] = __uint_as_float(w[p] << 16);
-      v[2 * p + 1] = __uint_as_float(w[p] & 0xFFFF0000u);
-    }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
-    // scale = 2^(14 - floor(log2 amax)) puts the block maximum in [2^14, 2^15).
-    const int e = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFF);
-    int sh = e == 0 ? 0 : 141 - e;
-    sh = max(-126, min(126, sh));
-    const float scale = __uint_as_float(static_cast<uint32_t>(127 + sh) << 23);
-    inv = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
-#pragma unroll
-    for (int p = 0; p < 8; ++p) {
-      const __half2 h = __floats2half2_rn(v[2 * p] * scale, v[2 * p + 1] * scale);
-      xb[p] = *reinterpret_cast<const uint32_t*>(&h);
-    }
-  }
-}
-
 template <int DT>
 __device__ __forceinline__ float epilogue_value(float acc, bool has_bias, float bias, int act) {
   float o = round_t<DT>(acc);
@@ -101,31 +73,34 @@ __device__ __forceinline__ float epilogue_value(float acc, bool has_bias, float 
 }
 
 // Token-side operands of one 64-wide sub-block for this lane: B fragments of
-// both 8-token halves, and the activation sums / inverse scales the epilogue
-// of the accumulator columns 2c, 2c+1 needs.
+// both 8-token halves, and the activation sums the group term of the
+// accumulator columns 2c, 2c+1 needs.
 template <int G>
 struct XOperands {
   static constexpr int SUBG = (G == 32) ? 2 : 1;
   uint32_t xb[2][8];
-  float xsA[2][SUBG], xsB[2][SUBG], ivA[2], ivB[2];
+  float xsA[2][SUBG], xsB[2][SUBG];
 };
 
-// xr: this lane's raw loads (load_x_raw) for tokens r4 and r4 + 8.
-// The per-(token, group) sums of the converted activations, which the group
-// term of the epilogue needs, come from the tensor pipe: an MMA with an
-// all-ones A fragment sums each token's sixteen k-slots of a k-step, and
-// lands them in the accumulator layout the epilogue reads (columns 2c and
-// 2c + 1 = tokens 2c and 2c + 1), so no unpacking, adds or shuffles are
-// needed for them.
+// xr: this lane's raw loads (load_x_raw) for tokens r4 and r4 + 8; the 16-bit
+// pairs are the B fragments as they are.  The per-(token, group) activation
+// sums come from the tensor pipe: an MMA with an all-ones A fragment sums
+// each token's sixteen k-slots of a k-step, and lands them in the accumulator
+// layout the epilogue reads (columns 2c and 2c + 1 = tokens 2c and 2c + 1),
+// so no unpacking, adds or shuffles are needed for them.
 template <int DT, int G>
 __device__ __forceinline__ XOperands<G> x_operands(const uint4 (&xr)[2][2], int lane) {
   constexpr int SUBG = XOperands<G>::SUBG;
-  const int c = lane & 3;
   XOperands<G> o;
-  float inv[2];
-  x_frag<DT>(xr[0][0], xr[0][1], o.xb[0], inv[0]);
-  x_frag<DT>(xr[1][0], xr[1][1], o.xb[1], inv[1]);
-  constexpr uint32_t kOnes = 0x3C003C00u;  // f16 1.0 twice
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const uint4& r0 = xr[nt][0];
+    const uint4& r1 = xr[nt][1];
+    o.xb[nt][0] = r0.x; o.xb[nt][1] = r0.y; o.xb[nt][2] = r0.z; o.xb[nt][3] = r0.w;
+    o.xb[nt][4] = r1.x; o.xb[nt][5] = r1.y; o.xb[nt][6] = r1.z; o.xb[nt][7] = r1.w;
+  }
+  // 1.0 twice in the activations' type
+  constexpr uint32_t kOnes = DT == kBF16 ? 0x3F803F80u : 0x3C003C00u;
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
     float sm[SUBG][4];
@@ -136,22 +111,21 @@ __device__ __forceinline__ XOperands<G> x_operands(const uint4 (&xr)[2][2], int 
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
       const int h = (SUBG == 2) ? (s >> 1) : 0;  // k-steps 0, 1 / 2, 3: the two 32-wide groups
-      mma_16816_f16(sm[h], kOnes, kOnes, kOnes, kOnes, o.xb[nt][2 * s], o.xb[nt][2 * s + 1]);
+      mma_16816<DT>(sm[h], kOnes, kOnes, kOnes, kOnes, o.xb[nt][2 * s], o.xb[nt][2 * s + 1]);
     }
 #pragma unroll
     for (int h = 0; h < SUBG; ++h) {
       o.xsA[nt][h] = sm[h][0];
       o.xsB[nt][h] = sm[h][1];
     }
-    o.ivA[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c);
-    o.ivB[nt] = __shfl_sync(0xFFFFFFFFu, inv[nt], 8 * c + 4);
   }
+  (void)lane;
   return o;
 }
 
 // One 64-wide sub-block of a band of RB = 16 * RT weight rows: wj is the
-// [RB][64] u8 tile in shared memory, sbj the [SUBG][RB] (s, b - 1024 s) pairs;
-// accumulates into acc[row tile][token half][fragment].
+// [RB][64] u8 tile in shared memory, sbj the [SUBG][RB] (s, b - o s) pairs
+// (o = weight_offset<DT>()); accumulates into acc[row tile][token half][fragment].
 template <int DT, int G, int RT>
 __device__ __forceinline__ void subblock_mma(const uint8_t* wj, const float2* sbj,
                                              const XOperands<G>& xo, int lane,
@@ -187,14 +161,33 @@ __device__ __forceinline__ void subblock_mma(const uint8_t* wj, const float2* sb
     for (int s = 0; s < 4; ++s) {
       const int h = (SUBG == 2) ? (s >> 1) : 0;  // constant after unrolling
       // bytes 4s..4s+3 of this lane's 16: (b0,b1) -> k-slots 2c,2c+1;
-      // (b2,b3) -> k-slots 2c+8, 2c+9.  0x64qq is the f16 value 1024 + q.
-      const uint32_t a0 = __byte_perm(wa[s], 0x64646464u, 0x4140);
-      const uint32_t a1 = __byte_perm(wb[s], 0x64646464u, 0x4140);
-      const uint32_t a2 = __byte_perm(wa[s], 0x64646464u, 0x4342);
-      const uint32_t a3 = __byte_perm(wb[s], 0x64646464u, 0x4342);
+      // (b2,b3) -> k-slots 2c+8, 2c+9.
+      if constexpr (DT == kBF16) {
+        // 0x43qq with bit 7 of qq cleared is the bf16 value 128 + (q & 127);
+        // (0x0080 per set bit 7) * 0x86 = 0x4300 is the bf16 value 128.
+        const uint32_t p0 = __byte_perm(wa[s], 0x43434343u, 0x4140);
+        const uint32_t p1 = __byte_perm(wb[s], 0x43434343u, 0x4140);
+        const uint32_t p2 = __byte_perm(wa[s], 0x43434343u, 0x4342);
+        const uint32_t p3 = __byte_perm(wb[s], 0x43434343u, 0x4342);
+        const uint32_t l0 = p0 & 0xFF7FFF7Fu, h0 = (p0 & 0x00800080u) * 0x86u;
+        const uint32_t l1 = p1 & 0xFF7FFF7Fu, h1 = (p1 & 0x00800080u) * 0x86u;
+        const uint32_t l2 = p2 & 0xFF7FFF7Fu, h2 = (p2 & 0x00800080u) * 0x86u;
+        const uint32_t l3 = p3 & 0xFF7FFF7Fu, h3 = (p3 & 0x00800080u) * 0x86u;
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-        mma_16816_f16(d[nt][h], a0, a1, a2, a3, xo.xb[nt][2 * s], xo.xb[nt][2 * s + 1]);
+        for (int nt = 0; nt < 2; ++nt) {
+          mma_16816_bf16(d[nt][h], l0, l1, l2, l3, xo.xb[nt][2 * s], xo.xb[nt][2 * s + 1]);
+          mma_16816_bf16(d[nt][h], h0, h1, h2, h3, xo.xb[nt][2 * s], xo.xb[nt][2 * s + 1]);
+        }
+      } else {
+        // 0x64qq is the f16 value 1024 + q.
+        const uint32_t a0 = __byte_perm(wa[s], 0x64646464u, 0x4140);
+        const uint32_t a1 = __byte_perm(wb[s], 0x64646464u, 0x4140);
+        const uint32_t a2 = __byte_perm(wa[s], 0x64646464u, 0x4342);
+        const uint32_t a3 = __byte_perm(wb[s], 0x64646464u, 0x4342);
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+          mma_16816_f16(d[nt][h], a0, a1, a2, a3, xo.xb[nt][2 * s], xo.xb[nt][2 * s + 1]);
+      }
     }
 #pragma unroll
     for (int h = 0; h < SUBG; ++h) {
@@ -206,17 +199,10 @@ __device__ __forceinline__ void subblock_mma(const uint8_t* wj, const float2* sb
         const float t1 = fmaf(sa.x, d[nt][h][1], sa.y * xo.xsB[nt][h]);
         const float t2 = fmaf(sb.x, d[nt][h][2], sb.y * xo.xsA[nt][h]);
         const float t3 = fmaf(sb.x, d[nt][h][3], sb.y * xo.xsB[nt][h]);
-        if constexpr (DT == kF16) {
-          acc[i][nt][0] += t0;
-          acc[i][nt][1] += t1;
-          acc[i][nt][2] += t2;
-          acc[i][nt][3] += t3;
-        } else {
-          acc[i][nt][0] = fmaf(t0, xo.ivA[nt], acc[i][nt][0]);
-          acc[i][nt][1] = fmaf(t1, xo.ivB[nt], acc[i][nt][1]);
-          acc[i][nt][2] = fmaf(t2, xo.ivA[nt], acc[i][nt][2]);
-          acc[i][nt][3] = fmaf(t3, xo.ivB[nt], acc[i][nt][3]);
-        }
+        acc[i][nt][0] += t0;
+        acc[i][nt][1] += t1;
+        acc[i][nt][2] += t2;
+        acc[i][nt][3] += t3;
       }
     }
   }

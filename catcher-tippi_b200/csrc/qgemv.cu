@@ -16,13 +16,15 @@
 //    stream of this linear overlaps the previous kernel.
 //  * After the wait the critical path is short: every warp owns at most two
 //    sub-blocks and issues all of its activation loads at once (one L2 round
-//    trip), converts, runs the MMAs, and the K-split partials are reduced.
+//    trip), runs the MMAs on them as loaded, and the K-split partials are
+//    reduced.
 //  * The K-split CTAs of one band form a thread-block cluster: each pushes its
 //    fp32 partial into the leader CTA's shared memory (distributed shared
 //    memory stores), one cluster barrier, and the leader finishes the
 //    epilogue.  No global scratch, no atomics, deterministic order.
-//  * Tensor cores via mma.m16n8k16 on the exact f16 image 1024 + q of each
-//    weight byte, with the offset folded into the group bias term; the
+//  * Tensor cores via mma.m16n8k16 in the activations' type on an exact
+//    image o + q of each weight byte (f16: 1024 + q; bf16: 128 + q in two
+//    fragments), with the offset folded into the group bias term; the
 //    per-sub-block arithmetic lives in gemv_core.cuh.
 #include "common.cuh"
 #include "gemv_core.cuh"
@@ -57,7 +59,7 @@ __host__ __device__ inline GemvSmem gemv_smem_layout(int rt, int sb_per_cta, int
   off += static_cast<size_t>(sb_per_cta) * rb * 64;
   L.bars = off;  // one weight barrier per sub-block
   off += kMaxSubBlocks * 8;
-  L.sbsm = off;  // [sb_per_cta * subg][rb] (s, b - 1024 s)
+  L.sbsm = off;  // [sb_per_cta * subg][rb] (s, b - o s), o = weight_offset<DT>()
   off += static_cast<size_t>(sb_per_cta) * subg * rb * sizeof(float2);
   L.biasm = off;  // [rb] output bias
   off += static_cast<size_t>(rb) * sizeof(float);
@@ -193,7 +195,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
     }
   }
 
-  // ---- group scales/biases (fp32 (s, b - 1024 s)) and the output bias: all
+  // ---- group scales/biases (fp32 (s, b - o s)) and the output bias: all
   // loads issued back to back, then stored, so the CTA pays one latency.
   {
     const int per_row = sbn * SUBG;
@@ -222,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
       const int e = tid + i * kThreads;
       if (e < total) {
         const int row = e % RB, jh = e / RB;  // rows fastest: conflict-free float2 stores
-        sbsm[jh * RB + row] = make_float2(sv[i], fmaf(-1024.0f, sv[i], bv[i]));
+        sbsm[jh * RB + row] = make_float2(sv[i], fmaf(-weight_offset<DT>(), sv[i], bv[i]));
       }
     }
     if (tid < RB) biasm[tid] = bias_v;

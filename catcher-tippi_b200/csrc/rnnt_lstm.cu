@@ -51,7 +51,7 @@ __host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg, int rb, 
   off += static_cast<size_t>(sbn) * rb * 64;
   L.bars = off;
   off += kMaxSb * 8;
-  L.sbsm = off;  // [sbn * subg][rb] (s, b - 1024 s)
+  L.sbsm = off;  // [sbn * subg][rb] (s, b - o s), o = weight_offset<DT>()
   off += static_cast<size_t>(sbn) * subg * rb * sizeof(float2);
   L.red = off;  // [8][rb][16] per-warp partials (columns swizzled by red_col)
   off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
@@ -134,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
       tma_load_2d(wt + static_cast<size_t>(j) * kRB * 64, wmap, j * 64, n0, &bars[j], pol);
     }
   }
-  // ---- group scales / biases as (s, b - 1024 s)
+  // ---- group scales / biases as (s, b - o s), o = weight_offset<DT>()
   for (int e = tid; e < sbn * SUBG * kRB; e += kThreads) {
     const int jh = e / kRB, row = e - jh * kRB;
     const int n = n0 + row;
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
       sv = ld_t<DT>(scales, gi);
       bv = ld_t<DT>(biases, gi);
     }
-    sbsm[e] = make_float2(sv, fmaf(-1024.0f, sv, bv));
+    sbsm[e] = make_float2(sv, fmaf(-weight_offset<DT>(), sv, bv));
   }
   pdl_launch_dependents();
   __syncthreads();
