@@ -44,7 +44,9 @@ constexpr int kThreads = kNW * 32;
 constexpr int kMaxSubBlocks = 16;               // sub-blocks (of 64 k) per CTA
 constexpr int kSbPerWarp = kMaxSubBlocks / kNW;  // at most two per warp
 constexpr int kMaxSbPerThread = (kMaxSubBlocks * 2 * 64 + kThreads - 1) / kThreads;
-constexpr int kMaxCluster = 8;
+// K <= 8192 (checked when a linear is created) keeps the K-split cluster
+// within the portable 8 CTAs: ceil(8192 / 64 / 16) = 8.
+static_assert((8192 / 64 + kMaxSubBlocks - 1) / kMaxSubBlocks <= 8, "K-split cluster above 8 CTAs");
 
 struct GemvSmem {
   size_t wt, bars, sbsm, biasm, red, fin, total;
@@ -453,10 +455,6 @@ cudaError_t launch_kind(int dtype, int group, const GemvPlan& plan, const GemvPa
                            : launch_rt<kBF16, 128, KIND>(plan, P, count, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
-}
-
-bool plan_ok(int nsb, int s, int spc) {
-  return s >= 1 && s <= kMaxCluster && spc >= 1 && spc <= kMaxSubBlocks && (s - 1) * spc < nsb;
 }
 
 }  // namespace
