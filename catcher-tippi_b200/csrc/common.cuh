@@ -237,6 +237,14 @@ __device__ __forceinline__ uint4 ld_global_cg_v4(const void* p) {
   return v;
 }
 
+// 32 bytes at a 32-byte aligned address in one 256-bit load (L2 only).
+__device__ __forceinline__ void ld_global_cg_v8(const void* p, uint4& lo, uint4& hi) {
+  asm volatile("ld.global.cg.v8.u32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(lo.x), "=r"(lo.y), "=r"(lo.z), "=r"(lo.w), "=r"(hi.x), "=r"(hi.y),
+                 "=r"(hi.z), "=r"(hi.w)
+               : "l"(p));
+}
+
 // ------------------------------------------------------------------ MMA
 
 // D = A(16x16, row) * B(16x8, col) + C, f16 inputs, f32 accumulation.

@@ -44,20 +44,33 @@ __device__ __forceinline__ int red_col(int row, int tok) {
 // values; zeros past M and past K):
 //   G >= 64: k = kb + 16c + [0, 16)
 //   G == 32: k = kb + 8c + [0, 8) and kb + 32 + 8c + [0, 8)
+// wide (x and every row 32-byte aligned, x_rows_wide): the G >= 64 lane's 32
+// bytes come in one 256-bit load.  Two 16-byte loads would each touch all four
+// 32-byte sectors of the quad's 128 bytes by halves, so the sectors would
+// cross from L2 twice.
 template <int G>
 __device__ __forceinline__ void load_x_raw(const void* __restrict__ x, int ldx, int M, int K, int m,
-                                           int kb, int c, uint4& r0, uint4& r1) {
+                                           int kb, int c, uint4& r0, uint4& r1, bool wide) {
   r0 = make_uint4(0, 0, 0, 0);
   r1 = make_uint4(0, 0, 0, 0);
   if (m >= M) return;
   const uint16_t* xr = reinterpret_cast<const uint16_t*>(x) + static_cast<size_t>(m) * ldx;
   if constexpr (G >= 64) {
-    r0 = ld_global_cg_v4(xr + kb + 16 * c);
-    r1 = ld_global_cg_v4(xr + kb + 16 * c + 8);
+    if (wide) {
+      ld_global_cg_v8(xr + kb + 16 * c, r0, r1);
+    } else {
+      r0 = ld_global_cg_v4(xr + kb + 16 * c);
+      r1 = ld_global_cg_v4(xr + kb + 16 * c + 8);
+    }
   } else {
     r0 = ld_global_cg_v4(xr + kb + 8 * c);
     if (kb + 32 < K) r1 = ld_global_cg_v4(xr + kb + 32 + 8 * c);
   }
+}
+
+// Whether load_x_raw may use 256-bit loads on x[., ldx] (16-bit elements).
+__device__ __forceinline__ bool x_rows_wide(const void* x, int ldx) {
+  return ((reinterpret_cast<uintptr_t>(x) | (static_cast<uintptr_t>(ldx) * 2)) & 31) == 0;
 }
 
 template <int DT>

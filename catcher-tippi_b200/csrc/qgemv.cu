@@ -245,14 +245,15 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
   // Token tiles blockIdx.z, blockIdx.z + gridDim.z, ... belong to this CTA.
   const int mt0 = blockIdx.z, mstep = gridDim.z;
   // All activation loads of this warp's sub-blocks in flight at once.
+  const bool xw = x_rows_wide(a.x, a.ldx);
   uint4 xr[kSbPerWarp][2][2];
 #pragma unroll
   for (int u = 0; u < kSbPerWarp; ++u) {
     const int j = warp + u * kNW;
     if (j < sbn) {
       const int kb = (sb0 + j) * 64;
-      load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt0 * 16 + r4, kb, c, xr[u][0][0], xr[u][0][1]);
-      load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt0 * 16 + 8 + r4, kb, c, xr[u][1][0], xr[u][1][1]);
+      load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt0 * 16 + r4, kb, c, xr[u][0][0], xr[u][0][1], xw);
+      load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt0 * 16 + 8 + r4, kb, c, xr[u][1][0], xr[u][1][1], xw);
     }
   }
   bool first_tile = true;
@@ -287,9 +288,9 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
         const int j = warp + u * kNW;
         if (j < sbn) {
           const int kb = (sb0 + j) * 64;
-          load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt_next * 16 + r4, kb, c, xr[u][0][0], xr[u][0][1]);
+          load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt_next * 16 + r4, kb, c, xr[u][0][0], xr[u][0][1], xw);
           load_x_raw<G>(a.x, a.ldx, a.M, a.K, mt_next * 16 + 8 + r4, kb, c, xr[u][1][0],
-                        xr[u][1][1]);
+                        xr[u][1][1], xw);
         }
       }
     }

@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
   const void* scales = rank == 0 ? a.scales_ih : a.scales_hh;
   const void* biases = rank == 0 ? a.biases_ih : a.biases_hh;
   const void* x = rank == 0 ? a.x : a.h_prev;
+  const bool xw = x_rows_wide(x, H);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c = lane & 3, r4 = lane >> 2;
@@ -210,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, MINB)
     for (int u = 0; u < kSbPerWarp; ++u) {
       const int j = warp + u * kNW;
       if (j < sbn) {
-        load_x_raw<G>(x, H, a.S, K, mt * 16 + r4, j * 64, c, xr[u][0][0], xr[u][0][1]);
-        load_x_raw<G>(x, H, a.S, K, mt * 16 + 8 + r4, j * 64, c, xr[u][1][0], xr[u][1][1]);
+        load_x_raw<G>(x, H, a.S, K, mt * 16 + r4, j * 64, c, xr[u][0][0], xr[u][0][1], xw);
+        load_x_raw<G>(x, H, a.S, K, mt * 16 + 8 + r4, j * 64, c, xr[u][1][0], xr[u][1][1], xw);
       }
     }
     float acc[RT][2][4];
