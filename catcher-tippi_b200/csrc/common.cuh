@@ -127,6 +127,13 @@ static __device__ __noinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t pa
   }
 }
 
+// mbar_wait_bounded with the common case, the phase already complete, tested
+// inline: a call of the out-of-line wait costs a few hundred cycles of
+// register traffic even when it returns at once.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  return mbar_try_wait(bar, parity) || mbar_wait_bounded(bar, parity, status);
+}
+
 // ------------------------------------------------------------------ TMA
 
 // 2-D tiled bulk-tensor load global -> shared, completion on an mbarrier.

@@ -474,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       rs_s[r] = (a.row_scale != nullptr && m < a.M) ? a.row_scale[m] : 1.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"n"(kDequantWarps * 32) : "memory");
-    ok = mbar_wait_bounded(accum, 0, a.status) && ok;
+    ok = mbar_wait(accum, 0, a.status) && ok;
     tc_fence_after();
     // D [n = lane][m = column]: this warp's 32 lanes (weight rows) and every
     // fourth 32-token chunk from cg on

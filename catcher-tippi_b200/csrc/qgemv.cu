@@ -273,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
       if (j >= sbn) break;
       const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
 
-      if (first_tile) ok = mbar_wait_bounded(&bars[j], 0, a.status) && ok;
+      if (first_tile) ok = mbar_wait(&bars[j], 0, a.status) && ok;
 
       subblock_mma<DT, G, RT>(wt + static_cast<size_t>(j) * RB * 64,
                               sbsm + static_cast<size_t>(j) * SUBG * RB, xo, lane, acc);
