@@ -130,6 +130,18 @@ def test_token_tiles_beyond_16_rows(cq, torch_dev, oracle_mod, m):
                   bias_bits=bias)
 
 
+@pytest.mark.parametrize("m", [14, 17, 33, 100, 139])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_k_split_token_tiles(cq, torch_dev, oracle_mod, m, dtype):
+    """K = 4096 splits over a 4-CTA cluster whose partials meet in the leader's shared
+    memory: one token tile per CTA (M <= 33 here) or several per CTA (100, 139), where
+    the leader's slots are reused from tile to tile."""
+    q, s, b, x, bias = make_case(oracle_mod, 1024, 4096, m, 64, dtype, seed=40 + m, with_bias=True)
+    y = run_gpu(cq, torch_dev, q, s, b, bias, x, 64, dtype)
+    assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, dtype, bias), dtype, min_exact=0.97,
+                  bias_bits=bias)
+
+
 @pytest.mark.parametrize("act", ["silu", "relu"])
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_fused_activation(cq, torch_dev, oracle_mod, act, dtype):
