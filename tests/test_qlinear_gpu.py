@@ -151,15 +151,19 @@ def test_fused_activation(cq, torch_dev, oracle_mod, act, dtype):
                   bias_bits=bias, act=act)
 
 
-def test_strided_rows(cq, torch_dev, oracle_mod):
+@pytest.mark.parametrize("ldx_pad", [64, 8])
+def test_strided_rows(cq, torch_dev, oracle_mod, ldx_pad):
+    """Row strides of 1088 and 1032 elements: 32-byte aligned rows take the 256-bit
+    activation loads, 16-byte aligned ones the pairs of 128-bit loads."""
     q, s, b, x, _ = make_case(oracle_mod, 640, 1024, 9, 64, "bf16", seed=21)
-    y = run_gpu(cq, torch_dev, q, s, b, None, x, 64, "bf16", ldx_pad=64, ldy_pad=5)
+    y = run_gpu(cq, torch_dev, q, s, b, None, x, 64, "bf16", ldx_pad=ldx_pad, ldy_pad=5)
     assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.97)
 
 
 @pytest.mark.parametrize("xscale", [1e-30, 1e-3, 1e3, 1e30])
 def test_bf16_activation_range(cq, torch_dev, oracle_mod, xscale):
-    """bf16 activations far outside the f16 range stay exact (power-of-two block scaling)."""
+    """bf16 activations far outside the f16 range stay exact (the bf16 MMA takes them as
+    they are)."""
     q, s, b, x, _ = make_case(oracle_mod, 1024, 1024, 14, 64, "bf16", seed=3, xscale=xscale)
     y = run_gpu(cq, torch_dev, q, s, b, None, x, 64, "bf16")
     assert_parity(y, oracle_mod.qmatmul(x, q, s, b, 64, "bf16"), "bf16", min_exact=0.97)
