@@ -98,9 +98,9 @@ def set_blocks(n: int) -> None:
 
 
 # DRAM bytes (read + write) per algorithmic byte of K1, from one ncu capture of
-# the 4096x1024 linear at M = 14 (4.518 MB for 4.600 MB algorithmic); traffic
+# the 4096x1024 linear at M = 14 (4.515 MB for 4.600 MB algorithmic); traffic
 # grows with the bytes a launch streams, so it is scaled to the average launch.
-K1_TRAFFIC_PER_ALGO_BYTE = 4.5184e6 / 4599808
+K1_TRAFFIC_PER_ALGO_BYTE = 4.5146e6 / 4599808
 
 
 def _peaks() -> dict:
@@ -365,7 +365,7 @@ def hbm_roofline(bytes_per_launch: float, launch_us: float, kernel: str, note: s
             "frac": round(achieved / peak, 4), "peak_kind": f"{kind} copy bandwidth",
             "traffic": round(K1_TRAFFIC_PER_ALGO_BYTE * bytes_per_launch),
             "traffic_note": "DRAM read+write bytes per launch, scaled from the ncu capture of "
-                            "the 4096x1024 linear (0.982 of algorithmic)",
+                            "the 4096x1024 linear (0.981 of algorithmic)",
             "kernel": kernel, "avg_launch_us": round(launch_us, 3), "note": note}
 
 
