@@ -98,12 +98,27 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
+// This thread's 8 LayerNorm weights and biases (columns c0..c0+7, T values
+// as loaded).  They are parameters of the model, so kernels load them before
+// griddepcontrol.wait.
+struct LnParams8 {
+  uint4 w, b;
+};
+__device__ __forceinline__ LnParams8 ln_params8(const void* w, const void* b, int c0, bool active) {
+  LnParams8 p{make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (active && w != nullptr) {
+    p.w = ld16(w, c0);
+    p.b = ld16(b, c0);
+  }
+  return p;
+}
+
 // LayerNorm of one row spread 8 values per thread (thread i holds columns
-// 8i..8i+7, `active` when inside the row); v are T values, o the T-rounded output.
+// 8i..8i+7, `active` when inside the row); v are T values, o the T-rounded
+// output, prm from ln_params8.
 template <int DT>
-__device__ __forceinline__ void layernorm8(const float (&v)[8], float (&o)[8], bool active, int c0,
-                                           int D, const void* w, const void* b, float eps,
-                                           float* red) {
+__device__ __forceinline__ void layernorm8(const float (&v)[8], float (&o)[8], bool active, int D,
+                                           const LnParams8& prm, float eps, float* red) {
   float s = 0.0f;
   if (active) {
 #pragma unroll
@@ -122,8 +137,8 @@ __device__ __forceinline__ void layernorm8(const float (&v)[8], float (&o)[8], b
   const float rstd = 1.0f / sqrtf(var + eps);
   if (active) {
     float wv[8], bv[8];
-    unpack8<DT>(ld16(w, c0), wv);
-    unpack8<DT>(ld16(b, c0), bv);
+    unpack8<DT>(prm.w, wv);
+    unpack8<DT>(prm.b, bv);
 #pragma unroll
     for (int k = 0; k < 8; ++k) o[k] = round_t<DT>((v[k] - mean) * rstd * wv[k] + bv[k]);
   }
@@ -174,15 +189,20 @@ __device__ __forceinline__ void emit_scaled_f16(const float (&o)[8], bool active
 
 // ------------------------------------------------------------------ LayerNorm
 
-template <int DT>
-__global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
+// MAXT: threads per CTA at most (8 columns each); rows up to 2048 wide run
+// the 256-thread form, whose registers hold the parameters loaded before the
+// wait without spilling.
+template <int DT, int MAXT>
+__global__ void __launch_bounds__(MAXT) layernorm_kernel(const LnArgs a) {
   __shared__ float red[32];
-  pdl_wait();
-  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int D = a.D;
   const int c0 = threadIdx.x * 8;
   const bool active = c0 < D;
+  const LnParams8 p1 = ln_params8(a.w1, a.b1, c0, active);
+  const LnParams8 p2 = ln_params8(a.w2, a.b2, c0, active);
+  pdl_wait();
+  pdl_launch_dependents();
   float* res = a.res + static_cast<size_t>(row) * D;
   float r[8] = {}, t[8] = {}, o[8] = {};
   if (active) {
@@ -206,7 +226,7 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
 #pragma unroll
     for (int k = 0; k < 8; ++k) t[k] = round_t<DT>(r[k]);  // LayerNorm casts its input to T
   }
-  layernorm8<DT>(t, o, active, c0, D, a.w1, a.b1, a.eps, red);
+  layernorm8<DT>(t, o, active, D, p1, a.eps, red);
   const bool second = a.w2 != nullptr || a.out_kind == 1;
   // the residual stream keeps r, or the block output o after norm_out
   const float* keep = second ? o : r;
@@ -226,7 +246,7 @@ __global__ void __launch_bounds__(1024) layernorm_kernel(const LnArgs a) {
     return;
   }
   float o2[8] = {};
-  layernorm8<DT>(o, o2, active, c0, D, a.w2, a.b2, a.eps, red);
+  layernorm8<DT>(o, o2, active, D, p2, a.eps, red);
   if (active) st16(a.out, static_cast<size_t>(row) * a.ldo + c0, pack8<DT>(o2));
   if (DT == kBF16 && a.out16 != nullptr)
     emit_scaled_f16(o2, active, c0, row, D, a.out16, a.scale16, red);
@@ -327,12 +347,14 @@ __device__ __forceinline__ void cp_async_wait_all() {
 
 template <class Src>
 __device__ __forceinline__ void stage_t_rows(uint16_t* dst, int ld, int rows, int rows_pad, int hd,
-                                             Src src) {
+                                             Src src, int r_lo = 0, int r_hi = -1) {
+  // rows r_lo .. r_hi - 1 of the padded range (all of it by default)
+  if (r_hi < 0) r_hi = rows_pad;
   const int per_row = hd / 8;
-  const int n = rows_pad * per_row;
+  const int n = (r_hi - r_lo) * per_row;
   const uint16_t* any = src(0);  // a readable address for the zero-fill copies
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const int r = i / per_row, c8 = (i - r * per_row) * 8;
+    const int r = r_lo + i / per_row, c8 = (i % per_row) * 8;
     const bool valid = r < rows;
     cp_async_16(dst + r * ld + c8, valid ? src(r) + c8 : any, valid);
   }
@@ -365,9 +387,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnAr
   float* bd = reinterpret_cast<float*>(smem_raw + L.bd);
   uint16_t* ph = reinterpret_cast<uint16_t*>(smem_raw + L.p);
   uint16_t* pl = ph + kAttnMaxQ * L.ldp;
-  pdl_wait();
-  pdl_launch_dependents();
-  if (qn <= 0) return;
+  // The frame counter moves only in the chunk's last kernel, which lets no
+  // dependent start early: within a chunk it is final before any kernel
+  // starts, so it is read before griddepcontrol.wait.
   const int n_prev = a.counters[kCtrFramesSeen];
   const int cached = min(n_prev, a.cache_frames);
   const int V = cached + Q;
@@ -397,9 +419,19 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnAr
   auto rel_row = [&](int i) -> const uint16_t* { return relk + static_cast<size_t>(rbase + i) * D + col; };
   const int nrel = V + qn - 1;
 
-  stage_t_rows(sk, L.lds, V, (V + 7) / 8 * 8, hd, key_row);
-  stage_t_rows(sv, L.lds, V, (V + 15) / 16 * 16, hd, value_row);
-  stage_t_rows(sr, L.lds, nrel, (nrel + 7) / 8 * 8, hd, rel_row);
+  // Before the wait: the position rows (a table of the state) and the cached
+  // keys and values (frames of earlier chunks; this chunk's go to ring slots
+  // the window does not read).  After it: this chunk's projections.
+  if (qn > 0) {
+    stage_t_rows(sr, L.lds, nrel, (nrel + 7) / 8 * 8, hd, rel_row);
+    stage_t_rows(sk, L.lds, V, (V + 7) / 8 * 8, hd, key_row, 0, cached);
+    stage_t_rows(sv, L.lds, V, (V + 15) / 16 * 16, hd, value_row, 0, cached);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  if (qn <= 0) return;
+  stage_t_rows(sk, L.lds, V, (V + 7) / 8 * 8, hd, key_row, cached);
+  stage_t_rows(sv, L.lds, V, (V + 15) / 16 * 16, hd, value_row, cached);
   // (q + bias_u), (q + bias_v) in fp32, split into T hi + T lo
   for (int i = threadIdx.x; i < kAttnMaxQ * (hd / 8); i += blockDim.x) {
     const int q = i / (hd / 8), c8 = (i % (hd / 8)) * 8;
@@ -542,14 +574,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnAr
 template <int DT, int KT>
 __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const ConvArgs a) {
   __shared__ float red[32];
-  pdl_wait();
-  pdl_launch_dependents();
   const int row = blockIdx.x;
   const int s = row / a.Q, t = row % a.Q;
   const int D = a.D, Q = a.Q;
   const int K = KT > 0 ? KT : a.K;
   const int c0 = threadIdx.x * 8;
   const bool active = c0 < D;
+  // the model's parameters before griddepcontrol.wait: the depthwise taps
+  // (KT > 0), the depthwise bias and the LayerNorm weights
+  constexpr int kUnroll = KT > 0 ? KT : 1;
+  uint4 uw_pre[kUnroll];
+  float bias[8] = {};
+  if (active) {
+    if constexpr (KT > 0) {
+#pragma unroll
+      for (int i = 0; i < KT; ++i) uw_pre[i] = ld16(a.dw_wt, static_cast<size_t>(i) * D + c0);
+    }
+    unpack8<DT>(ld16(a.dw_b, c0), bias);
+  }
+  const LnParams8 lnp = ln_params8(a.ln_w, a.ln_b, c0, active);
+  pdl_wait();
+  pdl_launch_dependents();
   const int par = a.counters[kCtrChunk] & 1;
   const size_t per_stream = static_cast<size_t>(K - 1) * D;
   const uint16_t* old_c =
@@ -558,14 +603,14 @@ __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const 
   float dv[8] = {}, o[8] = {};
   if (active) {
     float acc[8] = {}, g_t[8] = {};
-    constexpr int kUnroll = KT > 0 ? KT : 1;
     for (int tap0 = 0; tap0 < K; tap0 += kUnroll) {
       uint4 u0[kUnroll], u1[kUnroll], uw[kUnroll];
 #pragma unroll
       for (int i = 0; i < kUnroll; ++i) {
         const int tap = tap0 + i;
         const int f = t - (K - 1) + tap;
-        uw[i] = ld16(a.dw_wt, static_cast<size_t>(tap) * D + c0);
+        if constexpr (KT > 0) uw[i] = uw_pre[i];
+        else uw[i] = ld16(a.dw_wt, static_cast<size_t>(tap) * D + c0);
         if (f >= 0) {
           const size_t off = (static_cast<size_t>(s) * Q + f) * a.ldp + c0;
           u0[i] = ld16(a.pw1, off);
@@ -598,8 +643,6 @@ __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const 
         }
       }
     }
-    float bias[8];
-    unpack8<DT>(ld16(a.dw_b, c0), bias);
 #pragma unroll
     for (int k = 0; k < 8; ++k) dv[k] = round_t<DT>(round_t<DT>(acc[k]) + bias[k]);
     // new cache = last K-1 frames of (old cache ++ this chunk)
@@ -608,7 +651,7 @@ __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const 
       for (int j = 0; j < K - 1 - Q; ++j)
         st16(new_c, static_cast<size_t>(j) * D + c0, ld16(old_c, static_cast<size_t>(Q + j) * D + c0));
   }
-  layernorm8<DT>(dv, o, active, c0, D, a.ln_w, a.ln_b, a.eps, red);
+  layernorm8<DT>(dv, o, active, D, lnp, a.eps, red);
   float y[8] = {};
   if (active) {
 #pragma unroll
@@ -849,8 +892,13 @@ cudaError_t allow_smem(K kern, size_t bytes) {
 cudaError_t launch_layernorm(int dtype, const LnArgs& a, cudaStream_t stream, bool pdl) {
   if (a.D % 8 != 0 || a.D > 8192 || a.rows <= 0 || a.ldy % 8 != 0 || a.ldo % 8 != 0)
     return cudaErrorInvalidValue;
-  auto k = dtype == kBF16 ? layernorm_kernel<kBF16> : layernorm_kernel<kF16>;
-  return launch_ex(k, dim3(a.rows), dim3(row_threads(a.D)), 0, stream, pdl, a);
+  const int threads = row_threads(a.D);
+  if (threads <= 256) {
+    auto k = dtype == kBF16 ? layernorm_kernel<kBF16, 256> : layernorm_kernel<kF16, 256>;
+    return launch_ex(k, dim3(a.rows), dim3(threads), 0, stream, pdl, a);
+  }
+  auto k = dtype == kBF16 ? layernorm_kernel<kBF16, 1024> : layernorm_kernel<kF16, 1024>;
+  return launch_ex(k, dim3(a.rows), dim3(threads), 0, stream, pdl, a);
 }
 
 size_t attention_smem_bytes(int rows_q, int vmax, int head_dim) {
