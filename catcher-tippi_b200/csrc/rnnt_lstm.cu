@@ -40,7 +40,7 @@ constexpr int kMaxSb = 16;  // K = hidden <= 1024
 constexpr int kSbPerWarp = kMaxSb / kNW;
 
 struct LstmSmem {
-  size_t wt, bars, sbsm, red, fin, total;
+  size_t wt, bars, sbsm, red, fin, gb, total;
 };
 
 // rb rows per band; fin_bufs 2 where a CTA walks several token tiles.
@@ -57,6 +57,8 @@ __host__ __device__ inline LstmSmem lstm_smem_layout(int sbn, int subg, int rb, 
   off += static_cast<size_t>(kNW) * rb * 16 * sizeof(float);
   L.fin = off;  // [fin_bufs tiles in flight][2 products][rb][16] of rank 0's band
   off += static_cast<size_t>(fin_bufs) * 2 * rb * 16 * sizeof(float);
+  L.gb = off;  // [rb] the band's gate biases
+  off += static_cast<size_t>(rb) * sizeof(float);
   L.total = off;
   return L;
 }
@@ -80,6 +82,11 @@ __device__ __forceinline__ int ld_volatile_s32(const int* p) {
 __device__ __forceinline__ unsigned long long ld_volatile_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_volatile_u16(const void* p) {
+  unsigned short v;
+  asm volatile("ld.global.u16 %0, [%1];" : "=h"(v) : "l"(p) : "memory");
   return v;
 }
 __device__ __forceinline__ uint2 ld_volatile_v2u32(const void* p) {
@@ -115,6 +122,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
   float2* sbsm = reinterpret_cast<float2*>(smem + L.sbsm);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* fin = reinterpret_cast<float*>(smem + L.fin);
+  float* gbias = reinterpret_cast<float*>(smem + L.gb);
   const CUtensorMap* wmap = RT == 4 ? &maps.m[rank] : &maps.m5[rank];
   const void* scales = rank == 0 ? a.scales_ih : a.scales_hh;
   const void* biases = rank == 0 ? a.biases_ih : a.biases_hh;
@@ -148,6 +156,9 @@ __global__ void __launch_bounds__(kThreads, MINB)
     }
     sbsm[e] = make_float2(sv, fmaf(-weight_offset<DT>(), sv, bv));
   }
+  // ---- the band's gate biases (parameters of the model, like the scales)
+  for (int e = tid; e < kRB; e += kThreads)
+    gbias[e] = a.gate_bias != nullptr && n0 + e < N ? ld_t<DT>(a.gate_bias, n0 + e) : 0.0f;
   pdl_launch_dependents();
   __syncthreads();
   pdl_wait();
@@ -159,6 +170,21 @@ __global__ void __launch_bounds__(kThreads, MINB)
     // then row) overlaps the MMAs
     uint2 gi_bits[kCellIters];
     bool steps[kCellIters];  // deferred greedy choice: the stream steps
+    // the cell's state reads, issued before the product so their latency
+    // overlaps it: c (low half) and h_prev (high half) of each (unit, stream)
+    // pair this thread updates -- only this thread writes them
+    uint32_t ch_bits[kCellIters];
+#pragma unroll
+    for (int it = 0; it < kCellIters; ++it) {
+      ch_bits[it] = 0u;
+      const int p = tid + it * kThreads;
+      const int s = mt * 16 + (p & 15), j = n0 / 4 + (p >> 4);
+      if ((rank == 0 || FORM == 1) && a.gi_out == nullptr && p < kUnits * 16 && s < a.S && j < H) {
+        const size_t hj = static_cast<size_t>(s) * H + j;
+        ch_bits[it] = ld_volatile_u16(static_cast<const uint16_t*>(a.c) + hj) |
+                      (ld_volatile_u16(static_cast<const uint16_t*>(a.h_prev) + hj) << 16);
+      }
+    }
 #pragma unroll
     for (int it = 0; it < kCellIters; ++it) {
       gi_bits[it] = make_uint2(0u, 0u);
@@ -304,19 +330,19 @@ __global__ void __launch_bounds__(kThreads, MINB)
           for (int q = 0; q < 4; ++q) {
             const int row = 4 * u + q;
             const float gh = round_t<DT>(fbuf[kRB * 16 + row * 16 + t]);
-            gate[q] = round_t<DT>(round_t<DT>(gi[q] + gh) + ld_t<DT>(a.gate_bias, n0 + row));
+            gate[q] = round_t<DT>(round_t<DT>(gi[q] + gh) + gbias[row]);
           }
           const float ig = sigmoid_t<DT>(gate[0]);
           const float fg = sigmoid_t<DT>(gate[1]);
           const float gg = round_t<DT>(tanhf(gate[2]));
           const float og = sigmoid_t<DT>(gate[3]);
-          const float c_prev = ld_t<DT>(a.c, hj);
+          const float c_prev = widen_t<DT>(ch_bits[it] & 0xFFFFu);
           const float c_new = round_t<DT>(round_t<DT>(fg * c_prev) + round_t<DT>(ig * gg));
           const float h_new = round_t<DT>(og * round_t<DT>(tanhf(c_new)));
           st_t<DT>(a.c, hj, c_new);
           st_t<DT>(a.h_out, hj, h_new);
         } else {
-          st_t<DT>(a.h_out, hj, ld_t<DT>(a.h_prev, hj));  // state kept
+          static_cast<uint16_t*>(a.h_out)[hj] = static_cast<uint16_t>(ch_bits[it] >> 16);  // state kept
         }
       }
     }
