@@ -512,7 +512,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnAr
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     float tot = 0.0f;
     for (int j = lane; j < V; j += 32) {
-      const float e = expf(row[j] - m);
+      const float e = __expf(row[j] - m);  // argument <= 0: the fast exponential
       row[j] = e;
       tot += e;
     }
@@ -629,9 +629,11 @@ __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const 
         unpack8<DT>(uw[i], w);
         if (f >= 0) {
           // GLU: first / (1 + exp(-gate)) in f32, cast to T by the convolution
+          // (the fast exponential and division: a few fp32 ulps, far inside
+          // T's rounding step; an infinite denominator gives the limit 0)
           unpack8<DT>(u1[i], x1);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) g[k] = round_t<DT>(x0[k] / (1.0f + expf(-x1[k])));
+          for (int k = 0; k < 8; ++k) g[k] = round_t<DT>(__fdividef(x0[k], 1.0f + __expf(-x1[k])));
         } else {
 #pragma unroll
           for (int k = 0; k < 8; ++k) g[k] = x0[k];
@@ -655,7 +657,7 @@ __global__ void __launch_bounds__(KT > 0 ? 256 : 1024) conv_module_kernel(const 
   float y[8] = {};
   if (active) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) y[k] = round_t<DT>(o[k] / (1.0f + expf(-o[k])));  // SiLU, cast to T for pw2
+    for (int k = 0; k < 8; ++k) y[k] = round_t<DT>(__fdividef(o[k], 1.0f + __expf(-o[k])));  // SiLU, cast to T for pw2
     st16(a.out, static_cast<size_t>(row) * D + c0, pack8<DT>(y));
   }
   if (DT == kBF16 && a.out16 != nullptr)
