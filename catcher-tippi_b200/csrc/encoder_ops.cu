@@ -461,6 +461,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnAr
   cp_async_wait_all();  // this thread's staged K, V and position rows have landed
   __syncthreads();
 
+  // Append this chunk's keys and values to the window (AttentionKvCache::update)
+  // from their staged rows, before the products so the stores overlap them.
+  // The ring holds cache_frames + Q frames, so these slots are not among the
+  // ones any query group reads; the first query group of each (stream, head)
+  // writes them.
+  if (qg == 0) {
+    uint16_t* kw = static_cast<uint16_t*>(a.kring);
+    uint16_t* vw = static_cast<uint16_t*>(a.vring);
+    const int per_row = hd / 8;
+    for (int i = threadIdx.x; i < Q * per_row; i += blockDim.x) {
+      const int t = i / per_row, c8 = (i % per_row) * 8;
+      const size_t dst = (static_cast<size_t>(s) * ring + (n_prev + t) % ring) * D + col + c8;
+      *reinterpret_cast<uint4*>(kw + dst) = *reinterpret_cast<const uint4*>(sk + (cached + t) * L.lds + c8);
+      *reinterpret_cast<uint4*>(vw + dst) = *reinterpret_cast<const uint4*>(sv + (cached + t) * L.lds + c8);
+    }
+  }
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   // ---- AC = (q + bias_u) K^T over ceil(V/8) key tiles, BD = (q + bias_v) R^T
@@ -547,22 +564,6 @@ __global__ void __launch_bounds__(kAttnThreads, 2) attention_kernel(const AttnAr
     if (g + 8 < qn)
       *reinterpret_cast<uint32_t*>(out + (row0 + q0 + g + 8) * D + d) =
           f_to_t_bits<DT>(acc[2]) | (static_cast<uint32_t>(f_to_t_bits<DT>(acc[3])) << 16);
-  }
-
-  // Append this chunk's keys and values to the window (AttentionKvCache::update).
-  // The ring holds cache_frames + Q frames, so these slots are not among the
-  // ones read above; the first query group of each (stream, head) writes them.
-  if (qg == 0) {
-    uint16_t* kw = static_cast<uint16_t*>(a.kring);
-    uint16_t* vw = static_cast<uint16_t*>(a.vring);
-    const int per_row = hd / 8;
-    for (int i = threadIdx.x; i < Q * per_row; i += blockDim.x) {
-      const int t = i / per_row, c = (i % per_row) * 8;
-      const size_t dst = (static_cast<size_t>(s) * ring + (n_prev + t) % ring) * D + col + c;
-      const size_t src = (row0 + t) * ldqkv + col + c;
-      st16(kw, dst, ld16(qkv, src + D));
-      st16(vw, dst, ld16(qkv, src + 2 * static_cast<size_t>(D)));
-    }
   }
 }
 
