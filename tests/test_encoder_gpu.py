@@ -140,6 +140,32 @@ def test_streams_are_independent_and_reset_restarts(cq, oracle_mod):
         assert torch.equal(a, b)
 
 
+def test_sixteen_streams_match_one_stream_bit_for_bit(cq, oracle_mod):
+    """Below 256 rows per linear every encoder kernel gives a row the same bits
+    whatever the row count (the GEMV's reduction order follows K alone; the
+    other kernels work per stream or per row), so each of 16 lock-step streams
+    equals the same stream decoded alone, bit for bit, over chunks of 14 and
+    13 frames."""
+    import torch
+    from nemotron_cuda.encoder import Encoder, EncoderConfig
+    enc = Encoder.random(EncoderConfig.default(**SMALL), seed=8, dtype="bf16")
+    rng = np.random.default_rng(3)
+    S = 16
+    mels = [torch.from_numpy(rng.standard_normal((S, n, SMALL["mel_bins"])).astype(np.float32)).cuda()
+            for n in (112, 104, 112)]
+    st = enc.state(S, 112)
+    outs = [st.encode_chunk(m).clone() for m in mels]
+    for k in (0, 7, 15):
+        one = enc.state(1, 112)
+        alone = [one.encode_chunk(m[k:k + 1].contiguous()).clone() for m in mels]
+        torch.cuda.synchronize()
+        for c, (a, b) in enumerate(zip(outs, alone)):
+            q = b.shape[0]
+            assert a.shape[0] == S * q
+            assert torch.equal(a[k * q:(k + 1) * q], b), (k, c)
+    assert cq.device_status(0) == 0
+
+
 def test_prompt_changes_only_through_the_projector(cq, oracle_mod):
     import torch
     from nemotron_cuda.encoder import Encoder, EncoderConfig
