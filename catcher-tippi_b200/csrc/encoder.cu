@@ -70,6 +70,9 @@ Encoder::Encoder(const cq_encoder_config& cfg, cq_dtype dtype, int device)
   if (c.mel_bins <= 0 || c.sub_channels <= 0 || c.sub_channels % 8 != 0 || c.num_prompts < 0 ||
       c.prompt_hidden <= 0)
     throw_invalid("invalid subsampling or prompt dimensions");
+  // the Conv2D kernels keep a thread on one group of 8 channels
+  if (!cq::conv2d_channels_ok(c.sub_channels))
+    throw_invalid("subsampling channels must be 8 times a power of two up to 2048");
   device_context(device);
   DeviceGuard guard(device);
 

@@ -688,6 +688,20 @@ __device__ __forceinline__ void stage_conv_weights(float* wt, float* bias, const
   for (int c = threadIdx.x; c < C; c += blockDim.x) bias[c] = ld_t<DT>(b, c);
 }
 
+// This thread's channel group c0..c0+7 of the staged [9][C] weights and bias.
+__device__ __forceinline__ void conv_weights8(const float* wt, const float* bias, int C, int c0,
+                                              float (&wr)[9][8], float (&br)[8]) {
+#pragma unroll
+  for (int tap = 0; tap < 9; ++tap) {
+    const float4 w0 = *reinterpret_cast<const float4*>(wt + tap * C + c0);
+    const float4 w1 = *reinterpret_cast<const float4*>(wt + tap * C + c0 + 4);
+    wr[tap][0] = w0.x; wr[tap][1] = w0.y; wr[tap][2] = w0.z; wr[tap][3] = w0.w;
+    wr[tap][4] = w1.x; wr[tap][5] = w1.y; wr[tap][6] = w1.z; wr[tap][7] = w1.w;
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) br[k] = bias[c0 + k];
+}
+
 // One CTA per (output frame, stream).  The three input frames it reads are
 // staged (rounded to T, frequency zero-padded 2 left and 1 right) in shared
 // memory; each thread then produces eight channels of one frequency bin.
@@ -717,32 +731,29 @@ __global__ void __launch_bounds__(kThreads) stem_conv_kernel(const Conv2dArgs a)
     xs[i] = v;
   }
   __syncthreads();
+  // blockDim.x is a multiple of C / 8 (launch_stem_conv): a thread's channel
+  // group is the same for all its items, so its 9 x 8 weights live in registers
   const int CG = C / 8;
+  const int c0 = (threadIdx.x % CG) * 8;
+  float wr[9][8], br[8];
+  conv_weights8(wt, bias, C, c0, wr, br);
   const bool masked = t >= a.valid_out;  // mask_invalid_time, then ReLU
   for (int item = threadIdx.x; item < a.Fout * CG; item += blockDim.x) {
-    const int f = item / CG, c0 = (item % CG) * 8;
+    const int f = item / CG;
     float acc[8] = {};
 #pragma unroll
     for (int kt = 0; kt < 3; ++kt) {
 #pragma unroll
       for (int kf = 0; kf < 3; ++kf) {
         const float x = xs[kt * Fp + 2 * f + kf];
-        const float4 w0 = *reinterpret_cast<const float4*>(wt + (kt * 3 + kf) * C + c0);
-        const float4 w1 = *reinterpret_cast<const float4*>(wt + (kt * 3 + kf) * C + c0 + 4);
-        acc[0] = fmaf(w0.x, x, acc[0]);
-        acc[1] = fmaf(w0.y, x, acc[1]);
-        acc[2] = fmaf(w0.z, x, acc[2]);
-        acc[3] = fmaf(w0.w, x, acc[3]);
-        acc[4] = fmaf(w1.x, x, acc[4]);
-        acc[5] = fmaf(w1.y, x, acc[5]);
-        acc[6] = fmaf(w1.z, x, acc[6]);
-        acc[7] = fmaf(w1.w, x, acc[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = fmaf(wr[kt * 3 + kf][k], x, acc[k]);
       }
     }
     float o[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const float v = round_t<DT>(round_t<DT>(acc[k]) + bias[c0 + k]);
+      const float v = round_t<DT>(round_t<DT>(acc[k]) + br[k]);
       o[k] = masked ? 0.0f : fmaxf(v, 0.0f);
     }
     st16(a.out, ((static_cast<size_t>(s) * a.Tout + t) * a.Fout + f) * C + c0, pack8<DT>(o));
@@ -779,8 +790,13 @@ __global__ void __launch_bounds__(kThreads) depthwise_conv2d_kernel(const Conv2d
     if (src[kt] >= a.valid_in) src[kt] = -2;  // masked input frames read as zero
   }
   __syncthreads();
+  // blockDim.x is a multiple of C / 8 (launch_depthwise_conv2d): a thread's
+  // channel group is the same for all its items, so its weights live in registers
+  const int c0 = (threadIdx.x % CG) * 8;
+  float wr[9][8], br[8];
+  conv_weights8(wt, bias, C, c0, wr, br);
   for (int item = threadIdx.x; item < a.Fout * CG; item += blockDim.x) {
-    const int f = item / CG, c0 = (item % CG) * 8;
+    const int f = item / CG;
     uint4 u[9];
 #pragma unroll
     for (int kt = 0; kt < 3; ++kt) {
@@ -800,20 +816,12 @@ __global__ void __launch_bounds__(kThreads) depthwise_conv2d_kernel(const Conv2d
     for (int tap = 0; tap < 9; ++tap) {
       float x[8];
       unpack8<DT>(u[tap], x);
-      const float4 w0 = *reinterpret_cast<const float4*>(wt + tap * C + c0);
-      const float4 w1 = *reinterpret_cast<const float4*>(wt + tap * C + c0 + 4);
-      acc[0] = fmaf(w0.x, x[0], acc[0]);
-      acc[1] = fmaf(w0.y, x[1], acc[1]);
-      acc[2] = fmaf(w0.z, x[2], acc[2]);
-      acc[3] = fmaf(w0.w, x[3], acc[3]);
-      acc[4] = fmaf(w1.x, x[4], acc[4]);
-      acc[5] = fmaf(w1.y, x[5], acc[5]);
-      acc[6] = fmaf(w1.z, x[6], acc[6]);
-      acc[7] = fmaf(w1.w, x[7], acc[7]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc[k] = fmaf(wr[tap][k], x[k], acc[k]);
     }
     float o[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) o[k] = round_t<DT>(round_t<DT>(acc[k]) + bias[c0 + k]);
+    for (int k = 0; k < 8; ++k) o[k] = round_t<DT>(round_t<DT>(acc[k]) + br[k]);
     st16(a.out, ((static_cast<size_t>(s) * a.Tout + t) * a.Fout + f) * C + c0, pack8<DT>(o));
   }
   // the next chunk's cache: the last input frame (zero if masked)
@@ -940,8 +948,12 @@ cudaError_t launch_conv_module(int dtype, const ConvArgs& a, cudaStream_t stream
   return launch_ex(k, grid, block, 0, stream, pdl, a);
 }
 
+// Both Conv2D kernels keep a thread on one group of 8 channels: C / 8 must
+// divide the block (C in 8, 16, 32, ..., 2048).
+bool conv2d_channels_ok(int C) { return C > 0 && C % 8 == 0 && kThreads % (C / 8) == 0; }
+
 cudaError_t launch_stem_conv(int dtype, const Conv2dArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.C % 8) return cudaErrorInvalidValue;
+  if (!conv2d_channels_ok(a.C)) return cudaErrorInvalidValue;
   auto k = dtype == kBF16 ? stem_conv_kernel<kBF16> : stem_conv_kernel<kF16>;
   const size_t smem = (static_cast<size_t>(10) * a.C + 3 * (a.Fin + 3) + 4) * sizeof(float);
   cudaError_t e = allow_smem(k, smem);
@@ -950,7 +962,7 @@ cudaError_t launch_stem_conv(int dtype, const Conv2dArgs& a, cudaStream_t stream
 }
 
 cudaError_t launch_depthwise_conv2d(int dtype, const Conv2dArgs& a, cudaStream_t stream, bool pdl) {
-  if (a.C % 8) return cudaErrorInvalidValue;
+  if (!conv2d_channels_ok(a.C)) return cudaErrorInvalidValue;
   auto k = dtype == kBF16 ? depthwise_conv2d_kernel<kBF16> : depthwise_conv2d_kernel<kF16>;
   const size_t smem = static_cast<size_t>(10) * a.C * sizeof(float);
   cudaError_t e = allow_smem(k, smem);

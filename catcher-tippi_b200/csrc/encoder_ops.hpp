@@ -106,6 +106,8 @@ struct Conv2dArgs {
   const int* counters;
   int S, C;
 };
+// C / 8 divides the Conv2D kernels' 256 threads (C = 8, 16, ..., 2048).
+bool conv2d_channels_ok(int C);
 cudaError_t launch_stem_conv(int dtype, const Conv2dArgs& a, cudaStream_t stream, bool pdl);
 cudaError_t launch_depthwise_conv2d(int dtype, const Conv2dArgs& a, cudaStream_t stream, bool pdl);
 
