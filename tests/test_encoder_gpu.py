@@ -198,6 +198,9 @@ def test_encoder_binding_errors(cq):
         enc.set_linear("encoder.layers.0.feed_forward1.linear1.weight", q, s, b, None, 64)
     with pytest.raises(CQError, match="is not bound"):
         enc.state(1, 112)
+    # the subsampling Conv2D keeps a thread on one group of 8 channels
+    with pytest.raises(CQError, match="subsampling channels must be 8 times a power of two"):
+        Encoder(EncoderConfig.default(**{**SMALL, "sub_channels": 72}), "bf16")
     names = enc.tensor_names()
     assert names[0] == "encoder.subsampling.layers.0.pointwise_conv.weight"
     assert "encoder.layers.1.self_attn.bias_v" in names
