@@ -102,7 +102,7 @@ struct XOperands {
 // layout the epilogue reads (columns 2c and 2c + 1 = tokens 2c and 2c + 1),
 // so no unpacking, adds or shuffles are needed for them.
 template <int DT, int G>
-__device__ __forceinline__ XOperands<G> x_operands(const uint4 (&xr)[2][2], int lane) {
+__device__ __forceinline__ XOperands<G> x_operands(const uint4 (&xr)[2][2]) {
   constexpr int SUBG = XOperands<G>::SUBG;
   XOperands<G> o;
 #pragma unroll
@@ -132,7 +132,6 @@ __device__ __forceinline__ XOperands<G> x_operands(const uint4 (&xr)[2][2], int 
       o.xsB[nt][h] = sm[h][1];
     }
   }
-  (void)lane;
   return o;
 }
 

@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 2) qgemv_kernel(const __grid_constan
     for (int u = 0; u < kSbPerWarp; ++u) {
       const int j = warp + u * kNW;
       if (j >= sbn) break;
-      const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
+      const XOperands<G> xo = x_operands<DT, G>(xr[u]);
 
       if (first_tile) ok = mbar_wait(&bars[j], 0, a.status) && ok;
 

@@ -252,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, MINB)
     for (int u = 0; u < kSbPerWarp; ++u) {
       const int j = warp + u * kNW;
       if (j >= sbn) break;
-      const XOperands<G> xo = x_operands<DT, G>(xr[u], lane);
+      const XOperands<G> xo = x_operands<DT, G>(xr[u]);
       ok = mbar_wait(&bars[j], 0, a.status) && ok;
       subblock_mma<DT, G, RT>(wt + static_cast<size_t>(j) * kRB * 64,
                                sbsm + static_cast<size_t>(j) * SUBG * kRB, xo, lane, acc);
