@@ -773,10 +773,6 @@ int gemm_splits(int M, int N, int K, int num_sms, int tn) {
   return 1;
 }
 
-size_t gemm_smem_bytes() {
-  return std::max(GemmSmem<2, kGemmTN>::kBytes, GemmSmem<2, kGemmTNSmall>::kBytes) + 1024;
-}
-
 // (scale, bias) pairs as f16 in the GEMM's k-tile order:
 // out[ntile][ktile][row][h], h over the 32-wide halves of a 64-wide k-tile
 // when g = 32 (otherwise one pair per row and k-tile); zero past N and K.

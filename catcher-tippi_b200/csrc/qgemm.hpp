@@ -52,7 +52,6 @@ cudaError_t launch_gemm(int dtype, int group, const GemmActMaps& amaps, const CU
 // bf16 [M, ldx] -> f16 [M, ldo] with row_scale[m] = 2^e (power-of-two per row).
 cudaError_t launch_gemm_prepass(const void* x, int ldx, int M, int K, void* xo, int ldo,
                                 float* row_scale, cudaStream_t stream, bool pdl);
-size_t gemm_smem_bytes();
 // Repacks T scales/biases [N, K/g] into the f16 (scale, bias) pair order the
 // GEMM streams per k-tile: [ceil(N/kGemmBN)][ceil(K/64)][kGemmBN][g == 32 ? 2 : 1].
 size_t sb_tiles_bytes(int N, int K, int group);

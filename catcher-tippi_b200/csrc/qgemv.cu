@@ -496,10 +496,6 @@ GemvPlan plan_gemv_rows(const GemvPlan& base, int N, int M) {
   return p;
 }
 
-size_t gemv_smem_bytes(const GemvPlan& plan, int group) {
-  return gemv_smem_layout(plan.rt, plan.sb_per_cta, group == 32 ? 2 : 1, plan.ksplit).total;
-}
-
 cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const GemvMaps& maps,
                               const GemvGroup& g, cudaStream_t stream, bool pdl,
                               const RnntEpilogue* epi) {

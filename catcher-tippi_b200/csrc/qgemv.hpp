@@ -85,7 +85,6 @@ GemvPlan plan_gemv(int N, int K, int num_sms);
 // then taller weight bands (32 or 64 rows) leave room for the tiles to run
 // side by side on grid.z, so each CTA reads its tokens' activations once.
 GemvPlan plan_gemv_rows(const GemvPlan& base, int N, int M);
-size_t gemv_smem_bytes(const GemvPlan& plan, int group);
 cudaError_t launch_gemv(int dtype, int group, const GemvPlan& plan, const CUtensorMap& wmap,
                         const GemvArgs& args, cudaStream_t stream, bool pdl);
 cudaError_t launch_gemv_group(int dtype, int group, const GemvPlan& plan, const GemvMaps& maps,
