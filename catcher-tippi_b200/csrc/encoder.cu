@@ -17,8 +17,6 @@ namespace nemotron_cuda {
 
 namespace {
 
-size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
-
 // Output length of the stride-2 kernel-3 convolution over `combined` frames
 // (MLX conv2d without time padding).
 int conv_out(int combined) { return combined < 3 ? 0 : (combined - 3) / 2 + 1; }

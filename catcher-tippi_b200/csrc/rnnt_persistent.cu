@@ -84,8 +84,6 @@ __device__ bool grid_sync(Bar* bar, unsigned& epoch, int* status) {
   return aborted == 0;
 }
 
-__device__ __forceinline__ uint4 ldcg16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
-
 template <int DT>
 __device__ __forceinline__ float ldcg_t(const void* p, size_t i) {
   const uint16_t v = __ldcg(reinterpret_cast<const unsigned short*>(p) + i);
